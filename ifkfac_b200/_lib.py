@@ -1,0 +1,90 @@
+"""ctypes binding of libifk.so (the C ABI declared in include/ifk.h).
+
+The library is loaded from this package directory; it is built in-tree by
+``python -m ifkfac_b200.build``.  There is no fallback: when the library is
+missing or the device is not an sm_100 part, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libifk.so")
+HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "ifk.h")
+
+OK, ERR_RANK, ERR_NONFINITE, ERR_SHAPE, ERR_TIMEOUT, ERR_CUDA, ERR_WORKSPACE, ERR_DTYPE, \
+    ERR_ARG, ERR_DEVICE = range(10)
+F32, BF16 = 0, 1
+PREC_AUTO, PREC_FP32, PREC_BF16 = 0, 1, 2
+FOLD_TRAPEZOIDAL_CHUNK = 1
+
+_i64, _sz, _vp, _int, _dbl = ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int, ctypes.c_double
+
+# name -> (restype, argtypes); mirrors include/ifk.h
+SIGNATURES = {
+    "ifk_version": (ctypes.c_char_p, []),
+    "ifk_status_string": (ctypes.c_char_p, [_int]),
+    "ifk_device_check": (_int, []),
+    "ifk_tsqr_fold_workspace": (_sz, [_i64, _i64]),
+    "ifk_tsqr_fold": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _sz,
+                             _vp]),
+    "ifk_finalize_workspace": (_sz, [_i64]),
+    "ifk_finalize": (_int, [_vp, _i64, _i64, _i64, _dbl, _dbl, _vp, _i64, _int, _int, _vp, _vp, _sz,
+                            _vp]),
+    "ifk_natgrad_workspace": (_sz, [_i64, _i64]),
+    "ifk_natgrad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
+                           _vp, _sz, _vp]),
+    "ifk_natgrad_bias": (_int, [_vp, _vp, _i64, _int, _vp, _i64, _int, _vp, _sz, _vp]),
+    "ifk_update_workspace": (_sz, [_i64]),
+    "ifk_update": (_int, [_vp, _vp, _vp, _i64, _dbl, _dbl, _dbl, _dbl, _int, _vp, _sz, _vp]),
+    "ifk_update_bias": (_int, [_vp, _vp, _i64, _dbl, _dbl, _vp]),
+}
+
+
+class IFKError(RuntimeError):
+    """A libifk call returned a non-zero status."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        msg = status_string(status) if _LIB is not None else str(status)
+        super().__init__(f"{where}: {msg} (status {status})")
+
+
+_LIB = None
+_LOCK = threading.Lock()
+
+
+def header_symbols() -> list:
+    """Names of the entry points declared in include/ifk.h."""
+    with open(HEADER) as f:
+        return re.findall(r"IFK_API\s+[\w\s\*]+?\b(ifk_\w+)\s*\(", f.read())
+
+
+def lib() -> ctypes.CDLL:
+    """Load libifk.so once and attach the C signatures."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(f"{LIB_PATH} is not built (python -m ifkfac_b200.build)")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = L
+    return _LIB
+
+
+def status_string(status: int) -> str:
+    return lib().ifk_status_string(int(status)).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != OK:
+        raise IFKError(status, where)

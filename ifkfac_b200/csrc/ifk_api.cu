@@ -1,0 +1,207 @@
+// extern "C" entry points of libifk.so (declared in include/ifk.h).
+// Host-side validation happens before anything is queued on the stream.
+#include "ifk_common.cuh"
+#include "ifk_internal.h"
+
+using namespace ifk;
+
+namespace {
+
+constexpr size_t ALIGN = 256;
+size_t align_up(size_t b) { return (b + ALIGN - 1) / ALIGN * ALIGN; }
+bool aligned(const void* p) { return ((uintptr_t)p % ALIGN) == 0; }
+bool dtype_ok(int d) { return d == IFK_F32 || d == IFK_BF16; }
+bool prec_ok(int p) { return p == IFK_PREC_AUTO || p == IFK_PREC_FP32 || p == IFK_PREC_BF16; }
+cudaStream_t S(ifk_stream_t s) { return (cudaStream_t)s; }
+
+size_t fold_ws(int64_t rows, int64_t n) { return align_up(xw_bytes(rows, n)) + align_up(fold_tbuf_bytes(rows)); }
+
+}  // namespace
+
+extern "C" {
+
+const char* ifk_version(void) { return "ifkfac_b200 0.1.0 (sm_100a)"; }
+
+const char* ifk_status_string(int status) {
+  switch (status) {
+    case IFK_OK: return "ok";
+    case IFK_ERR_RANK: return "factor is rank deficient: fewer accumulated rows than columns";
+    case IFK_ERR_NONFINITE: return "non-finite value in a factor";
+    case IFK_ERR_SHAPE: return "inconsistent shape or leading dimension";
+    case IFK_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case IFK_ERR_CUDA: return "CUDA runtime error";
+    case IFK_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
+    case IFK_ERR_DTYPE: return "unsupported element type";
+    case IFK_ERR_ARG: return "invalid argument";
+    case IFK_ERR_DEVICE: return "current device is not compute capability 10.0 (sm_100a)";
+    default: return "unknown status";
+  }
+}
+
+int ifk_device_check(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return IFK_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return IFK_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return IFK_ERR_CUDA;
+  return (major == 10 && minor == 0) ? IFK_OK : IFK_ERR_DEVICE;
+}
+
+size_t ifk_tsqr_fold_workspace(int64_t rows, int64_t n) {
+  if (rows < 0 || n <= 0) return 0;
+  return fold_ws(rows, n);
+}
+
+int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int64_t ld_chunk,
+                  int64_t rows, int64_t n, int chunk_dtype, int prec, int flags, int* d_status,
+                  void* workspace, size_t workspace_bytes, ifk_stream_t stream) {
+  if (!R || (!chunk && rows > 0)) return IFK_ERR_ARG;
+  if (n <= 0 || rows < 0 || rows_R < 0 || rows_R > n || ldR < n || (rows > 0 && ld_chunk < n))
+    return IFK_ERR_SHAPE;
+  if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec) || (flags & ~IFK_FOLD_TRAPEZOIDAL_CHUNK)) return IFK_ERR_ARG;
+  if (rows == 0) return IFK_OK;
+  if (!workspace || !aligned(workspace) || workspace_bytes < fold_ws(rows, n))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  FoldArgs a;
+  a.R = R;
+  a.ldR = ldR;
+  a.X = (float*)workspace;
+  a.ldX = xw_ld(n);
+  a.Tb = (float*)((char*)workspace + align_up(xw_bytes(rows, n)));
+  a.n = n;
+  a.rows = rows;
+  a.rows_R = rows_R;
+  a.tiles = (int)cdiv(rows, SUB);
+  a.K = (int)cdiv(n, NB);
+  a.tri = (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0;
+  a.err = d_status;
+  cudaStream_t s = S(stream);
+  int rc = copy_chunk(a.X, a.ldX, chunk, ld_chunk, rows, n, chunk_dtype, s);
+  if (rc != IFK_OK) return rc;
+  return fold_run(a, prec, s);
+}
+
+size_t ifk_finalize_workspace(int64_t n) {
+  if (n <= 0) return 0;
+  return align_up((size_t)n * xw_ld(n) * sizeof(float)) + fold_ws(n, n);
+}
+
+int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, double rows_total,
+                 double damping, void* R_out, int64_t ld_out, int out_dtype, int prec,
+                 int* d_status, void* workspace, size_t workspace_bytes, ifk_stream_t stream) {
+  if (!R_in || !R_out) return IFK_ERR_ARG;
+  if (n <= 0 || ldR < n || ld_out < n) return IFK_ERR_SHAPE;
+  if (!dtype_ok(out_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec) || !(rows_total > 0) || !(damping >= 0)) return IFK_ERR_ARG;
+  if (rows_R < n) return IFK_ERR_RANK;
+  if (!workspace || !aligned(workspace) || workspace_bytes < ifk_finalize_workspace(n))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = out_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  const int64_t ldF = xw_ld(n);
+  float* Rf = (float*)workspace;
+  void* fws = (char*)workspace + align_up((size_t)n * ldF * sizeof(float));
+  int rc = scale_upper(Rf, ldF, R_in, ldR, n, (float)std::sqrt(rows_total), s);
+  if (rc != IFK_OK) return rc;
+  if (damping > 0) {
+    FoldArgs a;
+    a.R = Rf;
+    a.ldR = ldF;
+    a.X = (float*)fws;
+    a.ldX = xw_ld(n);
+    a.Tb = (float*)((char*)fws + align_up(xw_bytes(n, n)));
+    a.n = n;
+    a.rows = n;
+    a.rows_R = n;
+    a.tiles = (int)cdiv(n, SUB);
+    a.K = (int)cdiv(n, NB);
+    a.tri = 1;
+    a.err = d_status;
+    rc = fill_scaled_identity(a.X, a.ldX, n, (float)std::sqrt(damping), s);
+    if (rc != IFK_OK) return rc;
+    rc = fold_run(a, prec, s);
+    if (rc != IFK_OK) return rc;
+  }
+  return finish_factor(R_out, ld_out, out_dtype, Rf, ldF, n, d_status, s);
+}
+
+size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {
+  (void)n_out;
+  (void)n_in;
+  return ALIGN;
+}
+
+int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
+                int64_t ld_rg, int r_dtype, float* nat, int64_t ld_nat, int64_t n_out, int64_t n_in,
+                int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                ifk_stream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!grad_W || !R_X || !R_G || !nat) return IFK_ERR_ARG;
+  if (n_out <= 0 || n_in <= 0 || ld_g < n_in || ld_nat < n_in || ld_rx < n_in || ld_rg < n_out)
+    return IFK_ERR_SHAPE;
+  if (!dtype_ok(r_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec)) return IFK_ERR_ARG;
+  if (prec == IFK_PREC_AUTO) prec = r_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  if (nat != grad_W || ld_nat != ld_g) {
+    IFK_CUDA_TRY(cudaMemcpy2DAsync(nat, ld_nat * sizeof(float), grad_W, ld_g * sizeof(float),
+                                   n_in * sizeof(float), n_out, cudaMemcpyDeviceToDevice, s));
+  }
+  int rc;
+  // left: R_G^T T1 = g ; R_G T2 = T1   (columns of nat are independent right-hand sides)
+  rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, s);
+  if (rc != IFK_OK) return rc;
+  rc = trsm_run(R_G, ld_rg, r_dtype, 0, nat, ld_nat, 1, n_out, n_in, prec, s);
+  if (rc != IFK_OK) return rc;
+  // right: R_X^T T3^T = T2^T ; R_X T4^T = T3^T on the transposed view of nat
+  rc = trsm_run(R_X, ld_rx, r_dtype, 1, nat, 1, ld_nat, n_in, n_out, prec, s);
+  if (rc != IFK_OK) return rc;
+  return trsm_run(R_X, ld_rx, r_dtype, 0, nat, 1, ld_nat, n_in, n_out, prec, s);
+}
+
+int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_dtype, float* nat_b,
+                     int64_t n_out, int prec, void* workspace, size_t workspace_bytes,
+                     ifk_stream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!grad_b || !R_G || !nat_b) return IFK_ERR_ARG;
+  if (n_out <= 0 || ld_rg < n_out) return IFK_ERR_SHAPE;
+  if (!dtype_ok(r_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec)) return IFK_ERR_ARG;
+  cudaStream_t s = S(stream);
+  if (nat_b != grad_b)
+    IFK_CUDA_TRY(cudaMemcpyAsync(nat_b, grad_b, n_out * sizeof(float), cudaMemcpyDeviceToDevice, s));
+  // a single right-hand side: the fp32 path (tensor-core tiles would be 1/64 full)
+  int rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, s);
+  if (rc != IFK_OK) return rc;
+  return trsm_run(R_G, ld_rg, r_dtype, 0, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, s);
+}
+
+size_t ifk_update_workspace(int64_t count) {
+  (void)count;
+  return ALIGN;
+}
+
+int ifk_update(float* W, float* buf, const float* nat, int64_t count, double lr, double momentum,
+               double weight_decay, double grad_clip, int buf_is_new, void* workspace,
+               size_t workspace_bytes, ifk_stream_t stream) {
+  if (!W || !nat || (momentum > 0 && !buf)) return IFK_ERR_ARG;
+  if (count < 0) return IFK_ERR_SHAPE;
+  if (grad_clip > 0 && (!workspace || !aligned(workspace) || workspace_bytes < sizeof(double)))
+    return IFK_ERR_WORKSPACE;
+  return update_run(W, buf, nat, count, lr, momentum, weight_decay, grad_clip, buf_is_new,
+                    (double*)workspace, S(stream));
+}
+
+int ifk_update_bias(float* b, const float* nat_b, int64_t count, double lr, double weight_decay,
+                    ifk_stream_t stream) {
+  if (!b || !nat_b) return IFK_ERR_ARG;
+  if (count < 0) return IFK_ERR_SHAPE;
+  return update_bias_run(b, nat_b, count, lr, weight_decay, S(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// Shared definitions of the IFKFAC sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/ifk.h"
+
+namespace ifk {
+
+// Blocking of the streaming TSQR (TPQRT: triangle on top of a row tile).
+// A chunk is folded in sub-tiles of SUB rows; each sub-tile is a blocked
+// Householder fold with panels of NB columns and compact-WY trailing updates
+// on column blocks of WC columns.
+constexpr int NB = 64;
+constexpr int SUB = 256;
+constexpr int WC = 64;
+
+// Blocking of the triangular solves: NS rows per diagonal block, NRHS
+// right-hand-side columns per tile.
+constexpr int NS = 64;
+constexpr int NRHS = 64;
+
+__host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+template <typename T>
+__host__ __device__ __forceinline__ T mn(T a, T b) { return a < b ? a : b; }
+template <typename T>
+__host__ __device__ __forceinline__ T mx(T a, T b) { return a < b ? b : a; }
+
+__device__ __forceinline__ float ld_elem(const float* p, int64_t i) { return p[i]; }
+__device__ __forceinline__ float ld_elem(const __nv_bfloat16* p, int64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+// A strided read-only matrix view: element (i, j) at base[i*rs + j*cs].
+// Transposed factors and transposed right-hand sides are views, not copies.
+template <typename T>
+struct View {
+  const T* base;
+  int64_t rs, cs;
+  __device__ __forceinline__ float operator()(int64_t i, int64_t j) const {
+    return ld_elem(base, i * rs + j * cs);
+  }
+};
+
+struct MutView {
+  float* base;
+  int64_t rs, cs;
+  __device__ __forceinline__ float& operator()(int64_t i, int64_t j) const {
+    return base[i * rs + j * cs];
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace ifk
+
+#define IFK_CUDA_TRY(expr)                                  \
+  do {                                                      \
+    cudaError_t e_ = (expr);                                \
+    if (e_ != cudaSuccess) return IFK_ERR_CUDA;             \
+  } while (0)

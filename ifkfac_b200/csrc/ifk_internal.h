@@ -1,0 +1,56 @@
+// Host-side launchers shared between the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace ifk {
+
+// Working state of one fold: R (n x n fp32, in place) absorbs the rows of X
+// (rows x n fp32 working copy, overwritten with Householder vectors).
+struct FoldArgs {
+  float* R;
+  int64_t ldR;
+  float* X;
+  int64_t ldX;
+  float* Tb;       // one NB x NB compact-WY T per sub-tile (column-major)
+  int64_t n;
+  int64_t rows;
+  int64_t rows_R;  // meaningful rows of R before the fold
+  int tiles;       // ceil(rows / SUB)
+  int K;           // ceil(n / NB)
+  int tri;         // chunk row i is zero left of column i
+  int* err;        // device status word for bounded-wait timeouts (may be null)
+};
+
+size_t fold_tbuf_bytes(int64_t rows);
+size_t xw_bytes(int64_t rows, int64_t n);
+int64_t xw_ld(int64_t n);
+
+// chunk (bf16 or fp32, rows x n) -> X fp32
+int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows,
+               int64_t n, int dtype, cudaStream_t s);
+// X = sqrt(damping) I (n x n)
+int fill_scaled_identity(float* X, int64_t ldX, int64_t n, float v, cudaStream_t s);
+// Rout = upper(Rin) * scale (n x n fp32)
+int scale_upper(float* Rout, int64_t ldo, const float* Rin, int64_t ldi, int64_t n, float scale,
+                cudaStream_t s);
+// Run the fold waves.  prec: IFK_PREC_FP32 or IFK_PREC_BF16.
+int fold_run(const FoldArgs& a, int prec, cudaStream_t s);
+// Cast an n x n fp32 factor to the output type and flag non-finite entries.
+int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t ldR, int64_t n,
+                  int* d_status, cudaStream_t s);
+
+// In-place triangular solve op(A) X = B on a strided view of B (n x N).
+// A is an n x n upper-triangular factor (fp32 or bf16); trans != 0 solves
+// with A^T (lower, forward order), trans == 0 with A (upper, backward).
+int trsm_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs,
+             int64_t cs, int64_t n, int64_t N, int prec, cudaStream_t s);
+
+int update_run(float* W, float* buf, const float* nat, int64_t count, double lr, double mom,
+               double wd, double clip, int buf_is_new, double* norm_ws, cudaStream_t s);
+int update_bias_run(float* b, const float* nat, int64_t count, double lr, double wd,
+                    cudaStream_t s);
+
+}  // namespace ifk

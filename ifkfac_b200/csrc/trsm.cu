@@ -1,0 +1,149 @@
+// Blocked multi-right-hand-side triangular solves.
+//
+// op(A) X = B is solved in place on a strided view of B (n x N), with A an
+// upper-triangular factor (fp32 or bf16 storage) and op(A) = A (upper,
+// back substitution) or A^T (lower, forward substitution).  Block rows of NS
+// rows are visited in solve order; at each step the diagonal block is solved
+// for every right-hand-side tile (one thread per column, substitution with
+// fp32 FMAs), then the solved block is eliminated from every later block row
+// by a GEMM tile update B_j -= op(A)_{j,s} X_s.
+//
+// The four solves of the natural gradient (ifkfac/triangular.py:630-656)
+// are two calls on grad_W (R_G^T then R_G) and two on its transpose view
+// (R_X^T then R_X).
+#include "ifk_common.cuh"
+#include "ifk_internal.h"
+
+namespace ifk {
+
+namespace {
+
+constexpr int LDS_ = NRHS + 1;
+
+// op(A)[i][j] for block-local reads.
+template <typename TA>
+__device__ __forceinline__ float opA(const TA* A, int64_t ldA, int trans, int64_t i, int64_t j) {
+  return trans ? ld_elem(A, j * ldA + i) : ld_elem(A, i * ldA + j);
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ldA, int trans,
+                                                         float* B, int64_t rs, int64_t cs,
+                                                         int64_t n, int64_t N, int64_t b0) {
+  __shared__ float Ad[NS][NS + 1];
+  __shared__ float Bs[NS][LDS_];
+  const int tid = threadIdx.x;
+  const int64_t c0 = (int64_t)blockIdx.x * NRHS;
+  const int nb = (int)mn<int64_t>(NS, n - b0);
+  const int nc = (int)mn<int64_t>(NRHS, N - c0);
+  for (int idx = tid; idx < NS * NS; idx += NRHS) {
+    const int i = idx / NS, j = idx % NS;
+    Ad[i][j] = (i < nb && j < nb) ? opA(A, ldA, trans, b0 + i, b0 + j) : (i == j ? 1.f : 0.f);
+  }
+  for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
+    const int i = idx / NRHS, j = idx % NRHS;
+    Bs[i][j] = (i < nb && j < nc) ? B[(b0 + i) * rs + (c0 + j) * cs] : 0.f;
+  }
+  __syncthreads();
+  const int c = tid;
+  if (trans) {  // lower: forward
+    for (int r = 0; r < nb; ++r) {
+      float s = Bs[r][c];
+      for (int l = 0; l < r; ++l) s -= Ad[r][l] * Bs[l][c];
+      Bs[r][c] = s / Ad[r][r];
+    }
+  } else {  // upper: backward
+    for (int r = nb - 1; r >= 0; --r) {
+      float s = Bs[r][c];
+      for (int l = r + 1; l < nb; ++l) s -= Ad[r][l] * Bs[l][c];
+      Bs[r][c] = s / Ad[r][r];
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
+    const int i = idx / NRHS, j = idx % NRHS;
+    if (i < nb && j < nc) B[(b0 + i) * rs + (c0 + j) * cs] = Bs[i][j];
+  }
+}
+
+// B_j -= op(A)[j block, s block] X_s for every block row j after s in solve order.
+template <typename TA>
+__global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t ldA, int trans,
+                                                          float* B, int64_t rs, int64_t cs,
+                                                          int64_t n, int64_t N, int64_t s0) {
+  __shared__ float As[NS][NS + 1];
+  __shared__ float Xs[NS][LDS_];
+  const int tid = threadIdx.x;
+  // trans (forward): targets are the blocks after s; otherwise the blocks before s.
+  const int64_t jb = trans ? (s0 / NS + 1 + blockIdx.x) : blockIdx.x;
+  const int64_t j0 = jb * NS;
+  if (trans ? (j0 >= n) : (j0 >= s0)) return;
+  const int64_t c0 = (int64_t)blockIdx.y * NRHS;
+  const int nj = (int)mn<int64_t>(NS, n - j0);
+  const int ns = (int)mn<int64_t>(NS, n - s0);
+  const int nc = (int)mn<int64_t>(NRHS, N - c0);
+  for (int idx = tid; idx < NS * NS; idx += 256) {
+    const int i = idx / NS, l = idx % NS;
+    As[i][l] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
+  }
+  for (int idx = tid; idx < NS * NRHS; idx += 256) {
+    const int l = idx / NRHS, c = idx % NRHS;
+    Xs[l][c] = (l < ns && c < nc) ? B[(s0 + l) * rs + (c0 + c) * cs] : 0.f;
+  }
+  __syncthreads();
+  const int ty = tid / 16, tx = tid % 16;
+  float acc[4][4] = {};
+  for (int l = 0; l < NS; ++l) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) av[r] = As[ty * 4 + r][l];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bv[q] = Xs[l][tx * 4 + q];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = ty * 4 + r, c = tx * 4 + q;
+      if (i < nj && c < nc) B[(j0 + i) * rs + (c0 + c) * cs] -= acc[r][q];
+    }
+}
+
+template <typename TA>
+int trsm_simt(const TA* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t cs, int64_t n,
+              int64_t N, cudaStream_t s) {
+  const int64_t nblk = cdiv(n, NS);
+  const unsigned ctiles = (unsigned)cdiv(N, NRHS);
+  for (int64_t step = 0; step < nblk; ++step) {
+    const int64_t sb = trans ? step : (nblk - 1 - step);
+    const int64_t s0 = sb * NS;
+    trsm_diag_kernel<TA><<<ctiles, NRHS, 0, s>>>(A, ldA, trans, B, rs, cs, n, N, s0);
+    const int64_t rem = trans ? (nblk - 1 - sb) : sb;
+    if (rem > 0) {
+      trsm_update_kernel<TA><<<dim3((unsigned)rem, ctiles), 256, 0, s>>>(A, ldA, trans, B, rs, cs,
+                                                                         n, N, s0);
+    }
+  }
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+}  // namespace
+
+int trsm_tc_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs,
+                int64_t cs, int64_t n, int64_t N, cudaStream_t s);
+
+int trsm_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs, int64_t cs,
+             int64_t n, int64_t N, int prec, cudaStream_t s) {
+  if (n == 0 || N == 0) return IFK_OK;
+  if (prec == IFK_PREC_BF16) return trsm_tc_run(A, ldA, a_dtype, trans, B, rs, cs, n, N, s);
+  if (a_dtype == IFK_BF16)
+    return trsm_simt((const __nv_bfloat16*)A, ldA, trans, B, rs, cs, n, N, s);
+  return trsm_simt((const float*)A, ldA, trans, B, rs, cs, n, N, s);
+}
+
+}  // namespace ifk

@@ -1,0 +1,419 @@
+// Streaming TSQR fold: R <- qr([R; X]).R with a non-negative diagonal.
+//
+// Algorithm (restated from LAPACK's triangular-pentagonal QR, xTPQRT, and
+// matching the result of the reference's leaf + merge QR,
+// ifkfac/triangular.py:246-307): the chunk is cut into sub-tiles of SUB rows
+// that are folded one after another.  Folding a sub-tile is a blocked
+// Householder QR of the stack [R; X_t] in which panel k (NB columns) only
+// touches rows k*NB.. of R and the rows of X_t: reflector j maps
+// [R[j,j]; X_t[:, j]] to [beta; 0] with beta >= 0 (the reflector form of
+// LAPACK's xLARFGP, computed without cancellation), so no sign pass is
+// needed afterwards.  The panel's reflectors are aggregated in compact-WY
+// form V = [I; Y], Q = I - V T V^T, and applied to the trailing columns as
+//   W = T^T (R[k rows, c] + Y^T X_t[:, c]);  R[k rows, c] -= W;  X_t[:, c] -= Y W.
+// T comes from T^-1 = strict_upper(Y^T Y) + diag(1/tau) (Puglisi's identity).
+//
+// Scheduling: task (t, k) = panel k of sub-tile t.  It depends on (t-1, k)
+// (R rows of block k) and on (t, k-1) (X_t columns of block k), so all tasks
+// with t + k = d form wave d and waves run in order: one panel launch and one
+// trailing-update launch per wave.
+#include "ifk_common.cuh"
+#include "ifk_internal.h"
+
+namespace ifk {
+
+namespace {
+
+constexpr int PT = 256;  // threads of the panel and SIMT update kernels
+static_assert(SUB == PT, "panel kernel maps one thread to one row");
+constexpr int LDP = NB + 1;
+
+__device__ __forceinline__ bool task_active(const FoldArgs& a, int t, int k, int64_t* lim_out) {
+  if (t < 0 || t >= a.tiles || k < 0 || k >= a.K) return false;
+  const int64_t row0 = (int64_t)t * SUB;
+  const int64_t h = mn<int64_t>(SUB, a.rows - row0);
+  if (a.tri && (int64_t)k * NB + NB <= row0) return false;  // sub-tile is zero left of its diagonal
+  const int64_t lim = mn<int64_t>(a.n, a.rows_R + row0 + h);       // rank bound: columns that can be reduced
+  if ((int64_t)k * NB >= lim) return false;
+  *lim_out = lim;
+  return true;
+}
+
+constexpr size_t panel_smem_bytes() {
+  return sizeof(float) * ((size_t)SUB * LDP + 3 * (size_t)NB * LDP + 3 * NB);
+}
+
+// One panel factorisation per block: block t handles task (t, wave - t).
+__global__ void __launch_bounds__(PT) fold_panel_kernel(FoldArgs a, int wave) {
+  const int t = blockIdx.x;
+  const int k = wave - t;
+  int64_t lim;
+  if (!task_active(a, t, k, &lim)) return;
+
+  extern __shared__ float sm[];
+  float* P = sm;                  // SUB x LDP: X_t[:, panel] -> Y
+  float* Rk = P + SUB * LDP;      // NB x LDP: diagonal block of R
+  float* G = Rk + NB * LDP;       // NB x LDP: strict upper part of Y^T Y
+  float* Tm = G + NB * LDP;       // NB x LDP: column j holds T[:, j]
+  float* dv = Tm + NB * LDP;      // NB: dot products of the current column
+  float* wv = dv + NB;            // NB: w of the current reflector
+  float* tau = wv + NB;           // NB
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int64_t row0 = (int64_t)t * SUB;
+  const int h = (int)mn<int64_t>(SUB, a.rows - row0);
+  const int64_t c0 = (int64_t)k * NB;
+  const int nbk = (int)mn<int64_t>(NB, a.n - c0);
+  const int nact = (int)mx<int64_t>(0, mn<int64_t>(nbk, lim - c0));
+
+  for (int idx = tid; idx < SUB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    P[i * LDP + j] = (i < h && j < nbk) ? a.X[(row0 + i) * a.ldX + c0 + j] : 0.f;
+  }
+  for (int idx = tid; idx < NB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? a.R[(c0 + i) * a.ldR + c0 + j] : 0.f;
+    G[i * LDP + j] = 0.f;
+  }
+  __syncthreads();
+
+  for (int j = 0; j < nact; ++j) {
+    // dv[c] = X[:, j] . P[:, c] for every panel column (c == j: squared norm,
+    // c > j: inputs of w, c < j: future entries of Y^T Y).
+    for (int c = warp; c < nbk; c += PT / 32) {
+      float s = 0.f;
+      for (int i = lane; i < h; i += 32) s += P[i * LDP + j] * P[i * LDP + c];
+      s = warp_sum(s);
+      if (lane == 0) dv[c] = s;
+    }
+    __syncthreads();
+    const float aj = Rk[j * LDP + j];
+    const float xn2 = dv[j];
+    float tj, beta, inv_v0;
+    if (xn2 == 0.f) {
+      // nothing to annihilate; flip the row if its diagonal is negative
+      tj = aj >= 0.f ? 0.f : 2.f;
+      beta = fabsf(aj);
+      inv_v0 = 0.f;
+    } else {
+      const float nrm = sqrtf(aj * aj + xn2);
+      const float v0 = aj > 0.f ? -xn2 / (aj + nrm) : aj - nrm;
+      beta = nrm;
+      tj = -v0 / nrm;
+      inv_v0 = 1.f / v0;
+    }
+    if (tid < nbk) {
+      const int c = tid;
+      if (c > j) {
+        const float w = Rk[j * LDP + c] + dv[c] * inv_v0;
+        wv[c] = w;
+        Rk[j * LDP + c] -= tj * w;
+      } else if (c < j) {
+        G[c * LDP + j] = dv[c] * inv_v0;
+      } else {
+        Rk[j * LDP + j] = beta;
+        tau[j] = tj;
+      }
+    }
+    __syncthreads();
+    {
+      const int i = tid;  // one row per thread
+      const float y = P[i * LDP + j] * inv_v0;
+      P[i * LDP + j] = y;
+      const float ty = tj * y;
+      for (int c = j + 1; c < nbk; ++c) P[i * LDP + c] -= ty * wv[c];
+    }
+    __syncthreads();
+  }
+  // inactive columns (beyond the rank bound): identity reflectors
+  for (int idx = tid; idx < SUB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    if (j >= nact) P[i * LDP + j] = 0.f;
+  }
+  if (tid < NB && tid >= nact) tau[tid] = 0.f;
+  __syncthreads();
+
+  // T = (strict_upper(G) + diag(1/tau))^-1, one column per thread; a zero tau
+  // gives a zero row and column of T.
+  if (tid < NB) {
+    const int j = tid;
+    for (int i = 0; i < NB; ++i) Tm[j * LDP + i] = 0.f;
+    if (j < nbk) {
+      Tm[j * LDP + j] = tau[j];
+      for (int i = j - 1; i >= 0; --i) {
+        float s = 0.f;
+        for (int l = i + 1; l <= j; ++l) s += G[i * LDP + l] * Tm[j * LDP + l];
+        Tm[j * LDP + i] = -tau[i] * s;
+      }
+    }
+  }
+  __syncthreads();
+
+  float* Tb = a.Tb + (size_t)t * NB * NB;
+  for (int idx = tid; idx < NB * NB; idx += PT) Tb[idx] = Tm[(idx / NB) * LDP + (idx % NB)];
+  for (int idx = tid; idx < SUB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    if (i < h && j < nbk) a.X[(row0 + i) * a.ldX + c0 + j] = P[i * LDP + j];
+  }
+  for (int idx = tid; idx < NB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    if (i < nbk && j < nbk && j >= i) a.R[(c0 + i) * a.ldR + c0 + j] = Rk[i * LDP + j];
+  }
+}
+
+constexpr int LDW = WC + 1;
+constexpr size_t upd_smem_bytes() {
+  return sizeof(float) * ((size_t)SUB * LDP + (size_t)SUB * LDW + (size_t)NB * LDW + (size_t)NB * LDP);
+}
+
+// fp32 trailing update of one (sub-tile, panel, column block) per block.
+__global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldArgs a, int wave) {
+  const int t = blockIdx.x;
+  const int k = wave - t;
+  int64_t lim;
+  if (!task_active(a, t, k, &lim)) return;
+  const int64_t c0 = (int64_t)k * NB;
+  const int64_t cs = (int64_t)blockIdx.y * WC;
+  if (cs < c0 + NB || cs >= a.n) return;
+
+  extern __shared__ float sm[];
+  float* Y = sm;                 // SUB x LDP
+  float* Xb = Y + SUB * LDP;     // SUB x LDW
+  float* W = Xb + SUB * LDW;     // NB x LDW
+  float* Ts = W + NB * LDW;      // NB x LDP: Ts[i][l] = T[l][i]
+
+  const int tid = threadIdx.x;
+  const int64_t row0 = (int64_t)t * SUB;
+  const int h = (int)mn<int64_t>(SUB, a.rows - row0);
+  const int nbk = (int)mn<int64_t>(NB, a.n - c0);
+  const int wc = (int)mn<int64_t>(WC, a.n - cs);
+  const float* Tb = a.Tb + (size_t)t * NB * NB;
+
+  for (int idx = tid; idx < SUB * NB; idx += PT) {
+    const int i = idx / NB, j = idx % NB;
+    Y[i * LDP + j] = (i < h && j < nbk) ? a.X[(row0 + i) * a.ldX + c0 + j] : 0.f;
+  }
+  for (int idx = tid; idx < SUB * WC; idx += PT) {
+    const int i = idx / WC, j = idx % WC;
+    Xb[i * LDW + j] = (i < h && j < wc) ? a.X[(row0 + i) * a.ldX + cs + j] : 0.f;
+  }
+  for (int idx = tid; idx < NB * NB; idx += PT) {
+    const int i = idx / NB, l = idx % NB;  // Tb column-major: Tb[i*NB + l] = T[l][i]
+    Ts[i * LDP + l] = Tb[i * NB + l];
+  }
+  __syncthreads();
+
+  const int ty = tid / 16, tx = tid % 16;
+  float acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+  for (int kk = 0; kk < h; ++kk) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) av[r] = Y[kk * LDP + ty * 4 + r];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bv[q] = Xb[kk * LDW + tx * 4 + q];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = ty * 4 + r, c = tx * 4 + q;
+      const float rv = (i < nbk && c < wc) ? a.R[(c0 + i) * a.ldR + cs + c] : 0.f;
+      W[i * LDW + c] = acc[r][q] + rv;
+    }
+  __syncthreads();
+  // W2 = T^T W
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+  for (int l = 0; l < NB; ++l) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) av[r] = Ts[(ty * 4 + r) * LDP + l];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bv[q] = W[l * LDW + tx * 4 + q];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = ty * 4 + r, c = tx * 4 + q;
+      W[i * LDW + c] = acc[r][q];
+      if (i < nbk && c < wc) a.R[(c0 + i) * a.ldR + cs + c] -= acc[r][q];
+    }
+  __syncthreads();
+  // X_t[:, cols] -= Y W2 ; thread (ty, tx): rows ty*16.., cols tx*4..
+  float acc2[16][4];
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc2[r][q] = 0.f;
+  for (int l = 0; l < NB; ++l) {
+    float bv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bv[q] = W[l * LDW + tx * 4 + q];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float av = Y[(ty * 16 + r) * LDP + l];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc2[r][q] += av * bv[q];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = ty * 16 + r, c = tx * 4 + q;
+      if (i < h && c < wc) a.X[(row0 + i) * a.ldX + cs + c] = Xb[i * LDW + c] - acc2[r][q];
+    }
+}
+
+template <typename Tin>
+__global__ void copy_chunk_kernel(float* X, int64_t ldX, const Tin* src, int64_t lds, int64_t rows,
+                                  int64_t n) {
+  const int64_t total = rows * n;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / n, j = idx % n;
+    X[i * ldX + j] = ld_elem(src, i * lds + j);
+  }
+}
+
+__global__ void fill_identity_kernel(float* X, int64_t ldX, int64_t n, float v) {
+  const int64_t total = n * n;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / n, j = idx % n;
+    X[i * ldX + j] = (i == j) ? v : 0.f;
+  }
+}
+
+__global__ void scale_upper_kernel(float* Ro, int64_t ldo, const float* Ri, int64_t ldi, int64_t n,
+                                   float scale) {
+  const int64_t total = n * n;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / n, j = idx % n;
+    Ro[i * ldo + j] = (j >= i) ? Ri[i * ldi + j] / scale : 0.f;
+  }
+}
+
+template <typename Tout>
+__global__ void finish_factor_kernel(Tout* out, int64_t ldo, const float* R, int64_t ldR, int64_t n,
+                                     int* status) {
+  const int64_t total = n * n;
+  bool bad = false;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / n, j = idx % n;
+    const float v = R[i * ldR + j];
+    bad |= !isfinite(v);
+    if constexpr (sizeof(Tout) == 2) {
+      out[i * ldo + j] = __float2bfloat16_rn(v);
+    } else {
+      if ((const void*)out != (const void*)R || ldo != ldR) out[i * ldo + j] = v;
+    }
+  }
+  if (bad && status) atomicExch(status, IFK_ERR_NONFINITE);
+}
+
+int grid_for(int64_t total) {
+  int64_t g = cdiv(total, 256);
+  if (g > 148 * 16) g = 148 * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+bool set_smem_attr_once() {
+  static thread_local int done_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (done_dev == dev) return true;
+  if (cudaFuncSetAttribute(fold_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)panel_smem_bytes()) != cudaSuccess)
+    return false;
+  if (cudaFuncSetAttribute(fold_update_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)upd_smem_bytes()) != cudaSuccess)
+    return false;
+  done_dev = dev;
+  return true;
+}
+
+}  // namespace
+
+// Defined in tsqr_tc.cu: tensor-core trailing update of one wave.
+int fold_update_tc_launch(const FoldArgs& a, int wave, cudaStream_t s);
+
+int64_t xw_ld(int64_t n) { return cdiv(n, 4) * 4; }
+size_t xw_bytes(int64_t rows, int64_t n) { return (size_t)rows * xw_ld(n) * sizeof(float); }
+size_t fold_tbuf_bytes(int64_t rows) { return (size_t)cdiv(rows, SUB) * NB * NB * sizeof(float); }
+
+int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows, int64_t n,
+               int dtype, cudaStream_t s) {
+  if (rows == 0) return IFK_OK;
+  if (dtype == IFK_BF16)
+    copy_chunk_kernel<<<grid_for(rows * n), 256, 0, s>>>(
+        X, ldX, (const __nv_bfloat16*)chunk, ld_chunk, rows, n);
+  else
+    copy_chunk_kernel<<<grid_for(rows * n), 256, 0, s>>>(X, ldX, (const float*)chunk, ld_chunk,
+                                                         rows, n);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+int fill_scaled_identity(float* X, int64_t ldX, int64_t n, float v, cudaStream_t s) {
+  fill_identity_kernel<<<grid_for(n * n), 256, 0, s>>>(X, ldX, n, v);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+int scale_upper(float* Rout, int64_t ldo, const float* Rin, int64_t ldi, int64_t n, float scale,
+                cudaStream_t s) {
+  scale_upper_kernel<<<grid_for(n * n), 256, 0, s>>>(Rout, ldo, Rin, ldi, n, scale);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t ldR, int64_t n,
+                  int* d_status, cudaStream_t s) {
+  if (out_dtype == IFK_BF16)
+    finish_factor_kernel<<<grid_for(n * n), 256, 0, s>>>((__nv_bfloat16*)out, ldo, R, ldR, n,
+                                                         d_status);
+  else
+    finish_factor_kernel<<<grid_for(n * n), 256, 0, s>>>((float*)out, ldo, R, ldR, n, d_status);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+int fold_run(const FoldArgs& a, int prec, cudaStream_t s) {
+  if (a.rows == 0) return IFK_OK;
+  if (!set_smem_attr_once()) return IFK_ERR_CUDA;
+  const int waves = a.tiles + a.K - 1;
+  const dim3 ugrid(a.tiles, (unsigned)cdiv(a.n, WC));
+  for (int w = 0; w < waves; ++w) {
+    fold_panel_kernel<<<a.tiles, PT, panel_smem_bytes(), s>>>(a, w);
+    if (prec == IFK_PREC_BF16) {
+      const int rc = fold_update_tc_launch(a, w, s);
+      if (rc != IFK_OK) return rc;
+    } else {
+      fold_update_simt_kernel<<<ugrid, PT, upd_smem_bytes(), s>>>(a, w);
+    }
+  }
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+}  // namespace ifk

@@ -1,0 +1,195 @@
+/*
+ * ifk.h — C ABI of the B200 (sm_100a) IFKFAC curvature library (libifk.so).
+ *
+ * The library replaces the linear algebra under the reference's Python front
+ * end (Gsend/ifkfac): the streaming TSQR that folds captured activations X and
+ * back-propagated gradients delta into upper-triangular factors R_X / R_G, the
+ * damping fold, the four triangular solves that give the natural gradient,
+ * and the momentum / lr update of fp32 master weights.
+ *
+ * Conventions
+ *  - All matrices are device pointers, row-major, with an explicit leading
+ *    dimension in elements.  The caller owns every buffer; the library never
+ *    allocates device memory on these paths and never frees caller memory.
+ *  - R factors are n x n fp32 (or bf16 where stated), upper triangular, with a
+ *    non-negative diagonal (the reference's positive-diagonal convention,
+ *    ifkfac/triangular.py:230-239).  A running factor that has seen fewer
+ *    than n rows is trapezoidal: only its first rows_R rows are meaningful and
+ *    the remaining rows are zero.
+ *  - Every call is asynchronous on `stream` (a cudaStream_t) and returns an
+ *    ifk status code.  Host-side argument errors are reported before any GPU
+ *    work is queued.  Errors found on the device (non-finite factors, a timed
+ *    out wait) are written to a caller-provided device int, which stays 0 on
+ *    success.
+ *  - Calls are reentrant: no hidden global state other than the per-device
+ *    kernel attributes set on first use.  Calls that share a workspace must be
+ *    ordered on one stream.
+ *  - Precision: IFK_PREC_BF16 runs the GEMM-shaped work on tcgen05 tensor
+ *    cores with bf16 operands and fp32 accumulation (fp32 panels, norms,
+ *    divides and storage); IFK_PREC_FP32 runs everything in fp32 on the CUDA
+ *    cores.  IFK_PREC_AUTO picks BF16 for a bf16 chunk and FP32 otherwise.
+ *
+ * Reference citations are path:line inside the reference project.
+ */
+#ifndef IFK_H_
+#define IFK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define IFK_OK             0
+#define IFK_ERR_RANK       1  /* factor still trapezoidal: fewer rows than columns seen */
+#define IFK_ERR_NONFINITE  2  /* a factor has a NaN or Inf entry */
+#define IFK_ERR_SHAPE      3  /* inconsistent sizes or leading dimensions */
+#define IFK_ERR_TIMEOUT    4  /* a bounded device-side wait gave up */
+#define IFK_ERR_CUDA       5  /* a CUDA runtime call failed */
+#define IFK_ERR_WORKSPACE  6  /* workspace missing, too small or misaligned */
+#define IFK_ERR_DTYPE      7  /* unsupported element type */
+#define IFK_ERR_ARG        8  /* other invalid argument (null pointer, bad flag) */
+#define IFK_ERR_DEVICE     9  /* current device is not an sm_100 part */
+
+/* ---- element types ---------------------------------------------------- */
+#define IFK_F32   0
+#define IFK_BF16  1
+
+/* ---- precision modes -------------------------------------------------- */
+#define IFK_PREC_AUTO  0
+#define IFK_PREC_FP32  1
+#define IFK_PREC_BF16  2
+
+/* ---- fold flags ------------------------------------------------------- */
+#define IFK_FOLD_TRAPEZOIDAL_CHUNK 1  /* chunk row i is zero left of column i (an R factor) */
+
+typedef void* ifk_stream_t;  /* a cudaStream_t */
+
+#if defined(__GNUC__)
+#define IFK_API __attribute__((visibility("default")))
+#else
+#define IFK_API
+#endif
+
+/* Library version string and a message for a status code. */
+IFK_API const char* ifk_version(void);
+IFK_API const char* ifk_status_string(int status);
+
+/* IFK_OK when the current CUDA device is compute capability 10.0 (B200). */
+IFK_API int ifk_device_check(void);
+
+/* ---- streaming TSQR ---------------------------------------------------- */
+
+/* Workspace bytes for ifk_tsqr_fold on a chunk of `rows` rows and n columns. */
+IFK_API size_t ifk_tsqr_fold_workspace(int64_t rows, int64_t n);
+
+/*
+ * Fold `rows` rows of `chunk` (rows x n, element type chunk_dtype, leading
+ * dimension ld_chunk) into the running factor R (n x n fp32, in place).
+ * R holds rows_R meaningful rows (0 for an empty factor: R must then be all
+ * zero); afterwards it holds min(n, rows_R + rows) rows, upper triangular
+ * with a non-negative diagonal, such that R'^T R' = R^T R + chunk^T chunk.
+ * flags: IFK_FOLD_TRAPEZOIDAL_CHUNK when the chunk is itself an R factor
+ * (zero left of its diagonal), which skips the known-zero work.
+ *
+ * Replaces streaming_tsqr_update (ifkfac/triangular.py:246-307), i.e. the
+ * leaf QR + merge QR + _positive_diagonal_R (:230-239) that the forward and
+ * backward hooks call (ifkfac/activation_hooks.py:579,642).  Also the merge
+ * step of the tile/tree TSQR (ifkfac/triangular.py:207-220) when the chunk
+ * is another R factor.  *d_status (device int, may be NULL) receives
+ * IFK_ERR_TIMEOUT if a bounded device-side wait gave up.
+ */
+IFK_API int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R,
+                  const void* chunk, int64_t ld_chunk, int64_t rows, int64_t n,
+                  int chunk_dtype, int prec, int flags, int* d_status,
+                  void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/* ---- damping fold ------------------------------------------------------ */
+
+/* Workspace bytes for ifk_finalize on an n x n factor. */
+IFK_API size_t ifk_finalize_workspace(int64_t n);
+
+/*
+ * R_out = the positive-diagonal R factor of [R_in / sqrt(rows_total);
+ * sqrt(damping) I_n], so that R_out^T R_out = R_in^T R_in / rows_total +
+ * damping I.  R_in (n x n fp32) must be square (rows_R == n), otherwise
+ * IFK_ERR_RANK is returned and nothing is queued, matching the reference's
+ * skip of a non-square factor.  R_out has element type out_dtype (fp32, or
+ * bf16 for use_true_bf16) and may not alias R_in.  *d_status (device int,
+ * may be NULL) receives IFK_ERR_NONFINITE if any entry of the result is not
+ * finite (or IFK_ERR_TIMEOUT if a bounded device-side wait gave up); it is
+ * not cleared on success.
+ *
+ * Replaces the factor half of RawActivationHooks.get_factors
+ * (ifkfac/activation_hooks.py:328-332), finalize_R
+ * (ifkfac/triangular.py:386-421), and the finite check and bf16 cast of
+ * IFKFAC._update_factors (ifkfac/ifkfac.py:231-237, 292-294).
+ */
+IFK_API int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n,
+                 double rows_total, double damping,
+                 void* R_out, int64_t ld_out, int out_dtype, int prec,
+                 int* d_status, void* workspace, size_t workspace_bytes,
+                 ifk_stream_t stream);
+
+/* ---- natural gradient ---------------------------------------------------- */
+
+/* Workspace bytes for ifk_natgrad on an n_out x n_in gradient. */
+IFK_API size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in);
+
+/*
+ * nat = R_G^-1 R_G^-T grad_W R_X^-1 R_X^-T (n_out x n_in fp32), by four
+ * blocked triangular solves.  R_X (n_in x n_in) and R_G (n_out x n_out) have
+ * element type r_dtype (fp32, or bf16 for bf16-stored factors); grad_W and
+ * nat are fp32 and may alias.
+ *
+ * Replaces apply_vered (ifkfac/triangular.py:551-656), including the
+ * bf16-stored dispatch (:607-628), and the per-layer loop of
+ * apply_vered_batched / _apply_vered_batched_impl (:430-451, :506-544).
+ * *d_status (device int, may be NULL) receives IFK_ERR_TIMEOUT if a bounded
+ * device-side wait gave up.
+ */
+IFK_API int ifk_natgrad(const float* grad_W, int64_t ld_g,
+                const void* R_X, int64_t ld_rx, const void* R_G, int64_t ld_rg,
+                int r_dtype, float* nat, int64_t ld_nat,
+                int64_t n_out, int64_t n_in, int prec, int* d_status,
+                void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/*
+ * nat_b = R_G^-1 R_G^-T grad_b (vectors of n_out fp32; may alias).
+ * Replaces apply_vered_bias (ifkfac/triangular.py:659-705).
+ */
+IFK_API int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_dtype,
+                     float* nat_b, int64_t n_out, int prec,
+                     void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/* ---- update epilogue ------------------------------------------------------ */
+
+/*
+ * Per-layer update of the bucketed fast path (ifkfac/ifkfac.py:394-413):
+ *   g = nat, scaled by grad_clip/||nat|| when grad_clip > 0 and ||nat|| > grad_clip;
+ *   if momentum > 0: buf = momentum*buf + g (buf is read as zero when
+ *   buf_is_new != 0, the reference's zero-initialised buffer), g = buf;
+ *   if weight_decay > 0: W *= 1 - lr*weight_decay;  W -= lr*g.
+ * W, buf and nat are `count` contiguous fp32 values; buf may be NULL when
+ * momentum == 0.  grad_clip <= 0 disables clipping.  workspace holds the
+ * norm reduction (ifk_update_workspace bytes) and may be NULL when clipping
+ * is off.
+ */
+IFK_API size_t ifk_update_workspace(int64_t count);
+IFK_API int ifk_update(float* W, float* buf, const float* nat, int64_t count,
+               double lr, double momentum, double weight_decay, double grad_clip,
+               int buf_is_new, void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/*
+ * Bias update (ifkfac/ifkfac.py:415-423): b *= 1 - lr*wd (wd > 0), b -= lr*nat_b.
+ */
+IFK_API int ifk_update_bias(float* b, const float* nat_b, int64_t count, double lr,
+                    double weight_decay, ifk_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* IFK_H_ */

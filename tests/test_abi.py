@@ -1,0 +1,50 @@
+"""The C-ABI library loads on CPU-only hosts and exports every symbol include/ifk.h declares.
+
+No compute call is made here (no GPU in this process); host-side queries that
+touch no device (workspace sizes, status strings, argument validation that
+fails before any CUDA call) are exercised.
+"""
+import ctypes
+
+import pytest
+
+from ifkfac_b200 import _lib
+
+
+def test_library_exports_header_symbols():
+    L = _lib.lib()
+    names = _lib.header_symbols()
+    assert len(names) >= 13
+    for name in names:
+        assert hasattr(L, name), name
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    assert b"sm_100a" in _lib.lib().ifk_version()
+    for s in range(10):
+        assert _lib.status_string(s)
+    assert "rank" in _lib.status_string(_lib.ERR_RANK)
+
+
+def test_workspace_sizes_are_host_only():
+    L = _lib.lib()
+    a = L.ifk_tsqr_fold_workspace(2048, 4096)
+    assert a >= 2048 * 4096 * 4          # fp32 working copy of the chunk
+    assert L.ifk_tsqr_fold_workspace(0, 0) == 0
+    assert L.ifk_finalize_workspace(4096) >= 2 * 4096 * 4096 * 4
+    assert L.ifk_update_workspace(10) >= 8
+
+
+def test_argument_errors_before_any_gpu_work():
+    L = _lib.lib()
+    # rank-deficient factor: the reference skips it; the ABI says so without touching the device
+    fake = ctypes.c_void_p(256)
+    rc = L.ifk_finalize(fake, 64, 32, 64, 100.0, 1e-2, fake, 64, _lib.F32, 0, None, fake, 1 << 20, None)
+    assert rc == _lib.ERR_RANK
+    assert L.ifk_tsqr_fold(None, 64, 0, fake, 64, 10, 64, _lib.F32, 0, 0, None, fake, 1 << 20, None) == _lib.ERR_ARG
+    assert L.ifk_tsqr_fold(fake, 32, 0, fake, 64, 10, 64, _lib.F32, 0, 0, None, fake, 1 << 20, None) == _lib.ERR_SHAPE
+    assert L.ifk_tsqr_fold(fake, 64, 0, fake, 64, 10, 64, 7, 0, 0, None, fake, 1 << 20, None) == _lib.ERR_DTYPE
+    assert L.ifk_tsqr_fold(fake, 64, 0, fake, 64, 10, 64, _lib.F32, 0, 0, None, fake, 16, None) == _lib.ERR_WORKSPACE
+    assert L.ifk_natgrad(fake, 8, fake, 8, fake, 4, 9, fake, 8, 4, 8, 0, None, fake, 256, None) == _lib.ERR_DTYPE
+    assert L.ifk_update(None, None, fake, 4, 0.1, 0.0, 0.0, 0.0, 0, None, 0, None) == _lib.ERR_ARG

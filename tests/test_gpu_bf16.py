@@ -1,0 +1,87 @@
+"""GPU parity of the bf16 tensor-core path (IFK_PREC_BF16).
+
+Reference points:
+* the reference's executed path for use_true_bf16 (fp32 QR -> damping fold ->
+  bf16 R -> fp32 solves, ifkfac/ifkfac.py:292-294, ifkfac/triangular.py:607-628)
+  fed the fp32 upcast of the same bf16 inputs: natural gradient within 2e-2
+  relative Frobenius error (the bf16 tolerance);
+* the reference's bf16_linalg composition (golden vectors): R factors within
+  2e-2 up to row signs.
+R factors of the bf16 fold are checked against the fp32 oracle at 1e-2
+(bf16 operand rounding, fp32 accumulation and storage).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ifk_oracle as O
+from tests.golden_io import load, rel, rel_rowsign
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+BF16, FP32 = 2, 1
+
+
+def _t(a, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def _scaled_bf16(rng, p, n):
+    s = np.exp(rng.uniform(0, math.log(100.0), n))
+    return O.bf16_round((rng.standard_normal((p, n)) * s).astype(np.float32))
+
+
+@pytest.mark.parametrize("n,rows", [(64, [300]), (200, [150, 333]), (512, [256, 1024, 100]),
+                                    (700, [2048])])
+def test_bf16_fold_matches_oracle(n, rows):
+    from ifkfac_b200 import triangular as T
+    rng = np.random.default_rng(n)
+    R = None
+    Ro = None
+    for p in rows:
+        X = _scaled_bf16(rng, p, n)
+        R = T.streaming_tsqr_update(R, _t(X, torch.bfloat16), prec=BF16)
+        Ro = O.streaming_tsqr_update(Ro, X)
+        assert tuple(R.shape) == Ro.shape
+        e = rel(R.cpu().numpy(), Ro)
+        assert e < 1e-2, e
+        assert np.all(np.diagonal(R.cpu().numpy()) >= 0)
+
+
+def test_bf16_factor_and_natgrad_vs_executed_path():
+    from ifkfac_b200 import triangular as T
+    rng = np.random.default_rng(7)
+    n_in, n_out, p, lam = 384, 256, 1536, 1e-2
+    X = _scaled_bf16(rng, p, n_in)
+    D = _scaled_bf16(rng, p, n_out)
+    gW = (rng.standard_normal((n_out, n_in)) * 1e-2).astype(np.float32)
+    fx = T.RunningFactor(n_in, DEV, BF16)
+    fd = T.RunningFactor(n_out, DEV, BF16)
+    for lo in range(0, p, 512):
+        fx.fold(_t(X[lo:lo + 512], torch.bfloat16))
+        fd.fold(_t(D[lo:lo + 512], torch.bfloat16))
+    RX = fx.damped(lam, out_dtype=torch.bfloat16)
+    RG = fd.damped(lam, out_dtype=torch.bfloat16)
+    RXo = O.get_factor(O.streaming_tsqr_update(None, X), p, lam)
+    RGo = O.get_factor(O.streaming_tsqr_update(None, D), p, lam)
+    assert rel(RX.float().cpu().numpy(), RXo) < 1e-2
+    assert rel(RG.float().cpu().numpy(), RGo) < 1e-2
+    nat_exec = O.apply_vered(gW, O.bf16_round(RXo), O.bf16_round(RGo), r_is_bf16=True)
+    nat = T.apply_vered(_t(gW), RX, RG, prec=FP32).cpu().numpy()
+    assert rel(nat, nat_exec) < 2e-2
+
+
+def test_bf16_fold_vs_bf16_linalg_golden():
+    """R of the reference's bf16_linalg composition (golden) vs the bf16 fold, up to row signs."""
+    from ifkfac_b200 import triangular as T
+    g = load("bf16_linalg")
+    lam = float(g["comp_lam"])
+    for key, rkey in (("comp_X", "comp_RX"), ("comp_D", "comp_RG")):
+        A = g[key]
+        p, n = A.shape
+        f = T.RunningFactor(n, DEV, BF16)
+        f.fold(_t(A, torch.bfloat16))
+        R = f.damped(lam).cpu().numpy()
+        assert rel_rowsign(R, g[rkey]) < 2e-2
