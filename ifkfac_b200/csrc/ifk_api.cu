@@ -1,5 +1,8 @@
 // extern "C" entry points of libifk.so (declared in include/ifk.h).
 // Host-side validation happens before anything is queued on the stream.
+#include <algorithm>
+#include <cmath>
+
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
 
@@ -129,23 +132,23 @@ int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, doub
 }
 
 size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {
-  (void)n_out;
-  (void)n_in;
-  return ALIGN;
+  if (n_out <= 0 || n_in <= 0) return 0;
+  return align_up(std::max(trsm_tc_workspace(n_out), trsm_tc_workspace(n_in)));
 }
 
 int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
                 int64_t ld_rg, int r_dtype, float* nat, int64_t ld_nat, int64_t n_out, int64_t n_in,
                 int prec, int* d_status, void* workspace, size_t workspace_bytes,
                 ifk_stream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (!grad_W || !R_X || !R_G || !nat) return IFK_ERR_ARG;
   if (n_out <= 0 || n_in <= 0 || ld_g < n_in || ld_nat < n_in || ld_rx < n_in || ld_rg < n_out)
     return IFK_ERR_SHAPE;
   if (!dtype_ok(r_dtype)) return IFK_ERR_DTYPE;
   if (!prec_ok(prec)) return IFK_ERR_ARG;
   if (prec == IFK_PREC_AUTO) prec = r_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  if (prec == IFK_PREC_BF16 &&
+      (!workspace || !aligned(workspace) || workspace_bytes < ifk_natgrad_workspace(n_out, n_in)))
+    return IFK_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
   if (nat != grad_W || ld_nat != ld_g) {
     IFK_CUDA_TRY(cudaMemcpy2DAsync(nat, ld_nat * sizeof(float), grad_W, ld_g * sizeof(float),
@@ -153,14 +156,14 @@ int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_r
   }
   int rc;
   // left: R_G^T T1 = g ; R_G T2 = T1   (columns of nat are independent right-hand sides)
-  rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, s);
+  rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s);
   if (rc != IFK_OK) return rc;
-  rc = trsm_run(R_G, ld_rg, r_dtype, 0, nat, ld_nat, 1, n_out, n_in, prec, s);
+  rc = trsm_run(R_G, ld_rg, r_dtype, 0, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s);
   if (rc != IFK_OK) return rc;
   // right: R_X^T T3^T = T2^T ; R_X T4^T = T3^T on the transposed view of nat
-  rc = trsm_run(R_X, ld_rx, r_dtype, 1, nat, 1, ld_nat, n_in, n_out, prec, s);
+  rc = trsm_run(R_X, ld_rx, r_dtype, 1, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s);
   if (rc != IFK_OK) return rc;
-  return trsm_run(R_X, ld_rx, r_dtype, 0, nat, 1, ld_nat, n_in, n_out, prec, s);
+  return trsm_run(R_X, ld_rx, r_dtype, 0, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s);
 }
 
 int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_dtype, float* nat_b,
@@ -176,9 +179,9 @@ int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_
   if (nat_b != grad_b)
     IFK_CUDA_TRY(cudaMemcpyAsync(nat_b, grad_b, n_out * sizeof(float), cudaMemcpyDeviceToDevice, s));
   // a single right-hand side: the fp32 path (tensor-core tiles would be 1/64 full)
-  int rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, s);
+  int rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, nullptr, nullptr, s);
   if (rc != IFK_OK) return rc;
-  return trsm_run(R_G, ld_rg, r_dtype, 0, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, s);
+  return trsm_run(R_G, ld_rg, r_dtype, 0, nat_b, 1, 1, n_out, 1, IFK_PREC_FP32, nullptr, nullptr, s);
 }
 
 size_t ifk_update_workspace(int64_t count) {

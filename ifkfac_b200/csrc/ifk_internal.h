@@ -45,8 +45,11 @@ int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t
 // In-place triangular solve op(A) X = B on a strided view of B (n x N).
 // A is an n x n upper-triangular factor (fp32 or bf16); trans != 0 solves
 // with A^T (lower, forward order), trans == 0 with A (upper, backward).
+// ws: trsm_tc_workspace(n) bytes for the tensor-core path (inverses of the
+// diagonal blocks); err: device status word for bounded-wait timeouts.
 int trsm_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs,
-             int64_t cs, int64_t n, int64_t N, int prec, cudaStream_t s);
+             int64_t cs, int64_t n, int64_t N, int prec, void* ws, int* err, cudaStream_t s);
+size_t trsm_tc_workspace(int64_t n);
 
 int update_run(float* W, float* buf, const float* nat, int64_t count, double lr, double mom,
                double wd, double clip, int buf_is_new, double* norm_ws, cudaStream_t s);

@@ -135,12 +135,12 @@ int trsm_simt(const TA* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t
 }  // namespace
 
 int trsm_tc_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs,
-                int64_t cs, int64_t n, int64_t N, cudaStream_t s);
+                int64_t cs, int64_t n, int64_t N, void* ws, int* err, cudaStream_t s);
 
 int trsm_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs, int64_t cs,
-             int64_t n, int64_t N, int prec, cudaStream_t s) {
+             int64_t n, int64_t N, int prec, void* ws, int* err, cudaStream_t s) {
   if (n == 0 || N == 0) return IFK_OK;
-  if (prec == IFK_PREC_BF16) return trsm_tc_run(A, ldA, a_dtype, trans, B, rs, cs, n, N, s);
+  if (prec == IFK_PREC_BF16) return trsm_tc_run(A, ldA, a_dtype, trans, B, rs, cs, n, N, ws, err, s);
   if (a_dtype == IFK_BF16)
     return trsm_simt((const __nv_bfloat16*)A, ldA, trans, B, rs, cs, n, N, s);
   return trsm_simt((const float*)A, ldA, trans, B, rs, cs, n, N, s);

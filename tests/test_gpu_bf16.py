@@ -69,8 +69,9 @@ def test_bf16_factor_and_natgrad_vs_executed_path():
     assert rel(RX.float().cpu().numpy(), RXo) < 1e-2
     assert rel(RG.float().cpu().numpy(), RGo) < 1e-2
     nat_exec = O.apply_vered(gW, O.bf16_round(RXo), O.bf16_round(RGo), r_is_bf16=True)
-    nat = T.apply_vered(_t(gW), RX, RG, prec=FP32).cpu().numpy()
-    assert rel(nat, nat_exec) < 2e-2
+    for prec in (FP32, BF16):
+        nat = T.apply_vered(_t(gW), RX, RG, prec=prec).cpu().numpy()
+        assert rel(nat, nat_exec) < 2e-2
 
 
 def test_bf16_fold_vs_bf16_linalg_golden():
@@ -85,3 +86,52 @@ def test_bf16_fold_vs_bf16_linalg_golden():
         f.fold(_t(A, torch.bfloat16))
         R = f.damped(lam).cpu().numpy()
         assert rel_rowsign(R, g[rkey]) < 2e-2
+
+
+@pytest.mark.parametrize("n_out,n_in", [(24, 40), (130, 300), (256, 512), (640, 384)])
+def test_bf16_natgrad_tensor_core_vs_executed_path(n_out, n_in):
+    """Tensor-core trsm on bf16-stored factors vs the reference's fp32 solves on the same factors."""
+    from ifkfac_b200 import triangular as T
+    rng = np.random.default_rng(n_out * 7 + n_in)
+    RX = O.bf16_round(O.get_factor(O.streaming_tsqr_update(None, _scaled_bf16(rng, 2 * n_in, n_in)),
+                                   2 * n_in, 1e-2))
+    RG = O.bf16_round(O.get_factor(O.streaming_tsqr_update(None, _scaled_bf16(rng, 2 * n_out, n_out)),
+                                   2 * n_out, 1e-2))
+    gW = (rng.standard_normal((n_out, n_in)) * 1e-2).astype(np.float32)
+    nat = T.apply_vered(_t(gW), _t(RX, torch.bfloat16), _t(RG, torch.bfloat16), prec=BF16)
+    e = rel(nat.cpu().numpy(), O.apply_vered(gW, RX, RG, r_is_bf16=True))
+    assert e < 5e-3, e
+
+
+def test_bf16_natgrad_golden():
+    from ifkfac_b200 import triangular as T
+    g = load("apply_vered")
+    nat = T.apply_vered(_t(g["f32_gW"]), _t(g["bf16_RX"], torch.bfloat16), _t(g["bf16_RG"], torch.bfloat16),
+                        prec=BF16)
+    assert rel(nat.cpu().numpy(), g["bf16_nat"]) < 5e-3
+
+
+def test_bf16_end_to_end_vs_bf16_linalg_composition():
+    """Natural gradient of the full bf16 path vs the reference's bf16_linalg composition.
+
+    The composition's own error against an fp64 truth is 2-3e-2 (its row-by-row
+    bf16 solves), so the bound is: no farther from it than its own error plus
+    ours, and ours is smaller than its own."""
+    from ifkfac_b200 import triangular as T
+    g = load("bf16_linalg")
+    lam = float(g["comp_lam"])
+    X, D, gW = g["comp_X"], g["comp_D"], g["comp_gW"]
+    p, n = X.shape
+    fs = []
+    for A in (X, D):
+        f = T.RunningFactor(n, DEV, BF16)
+        f.fold(_t(A, torch.bfloat16))
+        fs.append(f.damped(lam, out_dtype=torch.bfloat16))
+    nat = T.apply_vered(_t(gW), fs[0], fs[1], prec=BF16).cpu().numpy()
+    tx = O.get_factor(O.streaming_tsqr_update(None, X.astype(np.float64)), p, lam)
+    td = O.get_factor(O.streaming_tsqr_update(None, D.astype(np.float64)), p, lam)
+    truth = O.apply_vered(gW.astype(np.float64), tx, td)
+    e_ours, e_ref = rel(nat, truth), rel(g["comp_nat"], truth)
+    assert e_ours < e_ref
+    assert rel(nat, g["comp_nat"]) <= e_ref + e_ours + 1e-6
+    assert e_ours < 2e-2
