@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the IFKFAC curvature hot path on B200.
+
+One step = one single-layer operator: streaming TSQR of X and delta
+(16384 x 4096 bf16 each, 8 row tiles of 2048 folded one after another into
+R_X / R_G), the damping fold (R/sqrt(p), lambda = 1e-2) to bf16 factors, the
+four triangular solves on grad_W (4096 x 4096 fp32) and the momentum 0.9 /
+lr 1e-3 update of fp32 master weights.  Inputs are synthetic with the
+config's distributions (no dataset is involved): X, delta ~ N(0,1) times
+per-column scales log-uniform in [1, 100] (kappa ~ 1e2), grad_W ~ N(0, 1e-2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (launched with torchrun, one rank per GPU): layers are dealt
+round-robin to ranks (rank r owns layer r with its own data), so the units
+are independent and no collective is on the data path ("scaling": "weak");
+timing is the max over ranks of the device-timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_DIM, P_ROWS, TILE, DAMPING, LR, MOM = 4096, 16384, 2048, 1e-2, 1e-3, 0.9
+METRIC = "preconditioned steps/sec; TSQR+trsm TFLOP/s on 4096² bf16 layer, 1/2/4/8 B200"
+WORKLOAD = ("C2 single-layer operator: streaming TSQR of X and delta (16384x4096 bf16, 8 tiles of 2048), "
+            "damping fold lambda=1e-2 to bf16 R, 4 trsm on grad_W 4096x4096 fp32, momentum/lr update")
+
+
+def algorithmic_flops(n=N_DIM, p=P_ROWS, n_in=N_DIM, n_out=N_DIM):
+    """Per-operator work (unit counts of the survey's measurement section):
+    TSQR 2*(2pn^2 - 2/3 n^3), two triangle-on-diagonal damping folds 2*(2/3 n^3),
+    four trsm 2*n_out^2*n_in + 2*n_in^2*n_out."""
+    tsqr = 2 * (2 * p * n * n - 2.0 / 3.0 * n ** 3)
+    fold = 2 * (2.0 / 3.0 * n ** 3)
+    trsm = 2 * n_out * n_out * n_in + 2 * n_in * n_in * n_out
+    return {"tsqr": tsqr, "fold": fold, "trsm": trsm, "total": tsqr + fold + trsm}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "hbm": d["hbm_gbs"], "source": "measured"}
+    except Exception:
+        return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
+
+
+def launch_count(n=N_DIM, p=P_ROWS, tile=TILE):
+    """libifk kernel launches of one step (mirrors the host schedule in csrc/)."""
+    sub, nb, nb2 = 256, 64, 128
+    K = -(-n // nb)
+    per_fold = 1 + 2 * (-(-tile // sub) + K - 1)
+    folds = 2 * (p // tile) * per_fold
+    fin = 2 * (1 + 1 + 2 * (-(-n // sub) + K - 1) + 1)
+    trsm = 4 * (1 + -(-n // nb2))
+    return folds + fin + trsm + 1
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.lines = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1].split()[0]))
+                mx = float(f[2].split()[0])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def make_inputs(device, seed):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def scaled():
+        s = torch.exp(torch.rand(N_DIM, generator=g, device=device) * math.log(100.0))
+        return (torch.randn(P_ROWS, N_DIM, generator=g, device=device) * s).to(torch.bfloat16)
+
+    X, D = scaled(), scaled()
+    gW = torch.randn(N_DIM, N_DIM, generator=g, device=device) * 1e-2
+    W = torch.randn(N_DIM, N_DIM, generator=g, device=device) * 1e-2
+    return X, D, gW, W
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import LayerCurvature
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    _lib.check(_lib.lib().ifk_device_check(), "ifk_device_check")
+    X, D, gW, W = make_inputs(dev, 1234 + rank)
+    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_BF16, torch.bfloat16, TILE)
+    tiles = [(t * TILE, (t + 1) * TILE) for t in range(P_ROWS // TILE)]
+
+    def step(x, d, g, w):
+        lc.clear()
+        for lo, hi in tiles:
+            lc.fx.fold(x[lo:hi])
+            lc.fg.fold(d[lo:hi])
+        lc.refresh(DAMPING)
+        nat = lc.natgrad(g)
+        lc.update(w, nat, LR, MOM, 0.0, None)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up (also sets kernel attributes and creates the momentum buffer)
+    for _ in range(args.warmup):
+        step(X, D, gW, W)
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step(X, D, gW, W)  # one more eager warm-up on the capture stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=s):
+                step(X, D, gW, W)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+
+    def run_steps(k):
+        for _ in range(k):
+            if graph is not None:
+                graph.replay()
+            else:
+                step(X, D, gW, W)
+
+    # ---- timed region: device time, max over ranks ----
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record()
+        run_steps(args.steps)
+        e1.record()
+        e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = algorithmic_flops()
+    pk = peaks()
+
+    # ---- component timing (eager, events on the launching stream) ----
+    comp = {}
+    if rank == 0:
+        ev = lambda: torch.cuda.Event(enable_timing=True)
+        lc.clear()
+        torch.cuda.synchronize()
+        fold_ms = 0.0
+        for lo, hi in tiles:
+            for f, src in ((lc.fx, X), (lc.fg, D)):
+                a, b = ev(), ev()
+                a.record()
+                f.fold(src[lo:hi])
+                b.record()
+                b.synchronize()
+                fold_ms += a.elapsed_time(b)
+        a, b = ev(), ev()
+        a.record()
+        lc.refresh(DAMPING)
+        b.record()
+        b.synchronize()
+        fin_ms = a.elapsed_time(b)
+        a, b = ev(), ev()
+        a.record()
+        nat = lc.natgrad(gW)
+        b.record()
+        b.synchronize()
+        nat_ms = a.elapsed_time(b)
+        a, b = ev(), ev()
+        a.record()
+        lc.update(W, nat, LR, MOM, 0.0, None)
+        b.record()
+        b.synchronize()
+        upd_ms = a.elapsed_time(b)
+        comp = {"tsqr_ms": fold_ms, "fold_ms": fin_ms, "trsm_ms": nat_ms, "update_ms": upd_ms}
+
+    # ---- end to end through the public API: pinned host inputs in, weights out ----
+    e2e = None
+    if rank == 0 or world > 1:
+        hX = X.cpu().pin_memory()
+        hD = D.cpu().pin_memory()
+        hG = gW.cpu().pin_memory()
+        hW = torch.empty_like(W, device="cpu").pin_memory()
+        bi = hX.numel() * 2 + hD.numel() * 2 + hG.numel() * 4
+        bo = hW.numel() * 4
+        k2 = max(1, min(args.steps, 5))
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k2):
+            X.copy_(hX, non_blocking=True)
+            D.copy_(hD, non_blocking=True)
+            gW.copy_(hG, non_blocking=True)
+            run_steps(1)
+            hW.copy_(W, non_blocking=True)
+        b.record()
+        b.synchronize()
+        e2e_ms = a.elapsed_time(b) / k2
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": bi,
+               "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms}
+
+    if rank != 0:
+        return
+    out = {
+        "metric": METRIC, "value": world * 1000.0 / ms, "unit": "steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "n": N_DIM, "p": P_ROWS, "tile_rows": TILE,
+                   "damping": DAMPING, "lr": LR, "momentum": MOM, "use_true_bf16": True,
+                   "parallelism": f"layers round-robin over {world} GPU(s)",
+                   "l2": "inputs larger than L2 (X + delta bf16 = 268 MB read per step)",
+                   "cuda_graph": graph is not None},
+        "tflops": world * flops["total"] / (ms * 1e-3) / 1e12,
+        "tflops_frac_of_measured_bf16": flops["total"] / (ms * 1e-3) / 1e12 / pk["bf16"],
+        "components_ms": comp,
+        "gpu_launches": launch_count() * args.steps,
+        "clocks": clk.summary(),
+        "e2e": e2e,
+    }
+    if comp:
+        # dominant component by time; achieved = its algorithmic flops / its device time
+        name, key = max((("tsqr", "tsqr_ms"), ("fold", "fold_ms"), ("trsm", "trsm_ms")),
+                        key=lambda x: comp[x[1]])
+        ach = flops[name] / (comp[key] * 1e-3) / 1e12
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(name)
+        except Exception:
+            pass
+        out["roofline"] = {"kernel": f"{name} (all libifk launches of the {name} stage, one step)",
+                           "bound": "tensor", "achieved": ach, "peak": pk["bf16"],
+                           "unit": "TFLOP/s", "frac": ach / pk["bf16"], "traffic": traffic,
+                           "peak_source": f"{pk['source']} bf16 burst"}
+    if not args.no_cpu_baseline and world == 1:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_sample_scale)
+    print(json.dumps(out), flush=True)
+
+
+def cpu_baseline(scale=1.0):
+    """The oracle port (scipy LAPACK fp32, the reference's algorithm) on host cores,
+    timed on a bounded sample and extrapolated to one operator."""
+    import numpy as np
+    from oracle import ifk_oracle as O
+    rng = np.random.default_rng(0)
+    n = N_DIM
+    tile = int(TILE * scale)
+    s = np.exp(rng.uniform(0, math.log(100.0), n)).astype(np.float32)
+    tiles = [(rng.standard_normal((tile, n), dtype=np.float32) * s) for _ in range(3)]
+    t0 = time.perf_counter()
+    R = O.streaming_tsqr_update(None, tiles[0])
+    t1 = time.perf_counter()
+    R = O.streaming_tsqr_update(R, tiles[1])
+    t2 = time.perf_counter()
+    R = O.streaming_tsqr_update(R, tiles[2])
+    t3 = time.perf_counter()
+    F = O.finalize_R(O.scale_rows(R, 3 * tile), DAMPING) if R.shape[0] == n else None
+    t4 = time.perf_counter()
+    gW = (rng.standard_normal((n, n), dtype=np.float32) * 1e-2)
+    if F is not None:
+        O.apply_vered(gW, F, F)
+    t5 = time.perf_counter()
+    ntile = P_ROWS // TILE
+    est = 2 * ((t1 - t0) + (t2 - t1) + (ntile - 2) * (t3 - t2)) + 2 * (t4 - t3) + (t5 - t4)
+    return {"value": 1.0 / est, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": (f"oracle (scipy LAPACK sgeqrf/strtrs, fp32) on the box's host cores: fold of 3 row "
+                       f"tiles of {tile}x{n}, one damping fold, one 4-trsm natural gradient; the "
+                       f"operator time is extrapolated as 2*(leaf + first merge + {ntile - 2} full merges)"
+                       f" + 2*fold + trsm = {est:.1f} s"),
+            "sample_seconds": t5 - t0}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU path (the oracle port, since the reference is
+    pure Python and is not shipped to the box) on all host cores; rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np
+    try:
+        import threadpoolctl  # noqa: F401
+    except Exception:
+        pass
+    vals = []
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(args.cpu_sample_scale)
+        if i >= args.warmup:
+            vals.append(1.0 / cb["value"])
+    ms = 1000.0 * float(np.mean(vals))
+    v = 1000.0 / ms
+    out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": WORKLOAD, "n": N_DIM, "p": P_ROWS, "tile_rows": TILE,
+                      "damping": DAMPING},
+           "cpu_baseline": dict(cb, value=v),
+           "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-scale", type=float, default=1.0)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
+        return
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
