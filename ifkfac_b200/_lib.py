@@ -31,7 +31,13 @@ SIGNATURES = {
     "ifk_tsqr_fold_workspace": (_sz, [_i64, _i64]),
     "ifk_tsqr_fold": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _sz,
                              _vp]),
+    "ifk_tsqr_fold_batched_workspace": (_sz, [_int, _vp, _vp]),
+    "ifk_tsqr_fold_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp,
+                                     _vp, _sz, _vp]),
     "ifk_finalize_workspace": (_sz, [_i64]),
+    "ifk_finalize_batched_workspace": (_sz, [_int, _vp]),
+    "ifk_finalize_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp,
+                                    _vp, _sz, _vp]),
     "ifk_finalize": (_int, [_vp, _i64, _i64, _i64, _dbl, _dbl, _vp, _i64, _int, _int, _vp, _vp, _sz,
                             _vp]),
     "ifk_natgrad_workspace": (_sz, [_i64, _i64]),

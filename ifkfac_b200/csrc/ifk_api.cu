@@ -87,6 +87,63 @@ int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int6
   return fold_run(a, prec, s);
 }
 
+size_t ifk_tsqr_fold_batched_workspace(int nfolds, const int64_t* rows, const int64_t* n) {
+  if (nfolds <= 0 || !rows || !n) return 0;
+  size_t b = 0;
+  for (int f = 0; f < nfolds; ++f)
+    if (rows[f] > 0 && n[f] > 0) b += fold_ws(rows[f], n[f]);
+  return b;
+}
+
+int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const int64_t* rows_R,
+                          const void* const* chunk, const int64_t* ld_chunk, const int64_t* rows,
+                          const int64_t* n, int chunk_dtype, int prec, int flags, int* d_status,
+                          void* workspace, size_t workspace_bytes, ifk_stream_t stream) {
+  if (nfolds < 0 || (nfolds > 0 && (!R || !ldR || !rows_R || !chunk || !ld_chunk || !rows || !n)))
+    return IFK_ERR_ARG;
+  if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec) || (flags & ~IFK_FOLD_TRAPEZOIDAL_CHUNK)) return IFK_ERR_ARG;
+  for (int f = 0; f < nfolds; ++f) {
+    if (!R[f] || (!chunk[f] && rows[f] > 0)) return IFK_ERR_ARG;
+    if (n[f] <= 0 || rows[f] < 0 || rows_R[f] < 0 || rows_R[f] > n[f] || ldR[f] < n[f] ||
+        (rows[f] > 0 && ld_chunk[f] < n[f]))
+      return IFK_ERR_SHAPE;
+  }
+  if (!workspace || !aligned(workspace) ||
+      workspace_bytes < ifk_tsqr_fold_batched_workspace(nfolds, rows, n))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  char* ws = (char*)workspace;
+  FoldBatch b;
+  b.nf = 0;
+  for (int f = 0; f < nfolds; ++f) {
+    if (rows[f] == 0) continue;
+    FoldArgs& a = b.f[b.nf++];
+    a.R = R[f];
+    a.ldR = ldR[f];
+    a.X = (float*)ws;
+    a.ldX = xw_ld(n[f]);
+    a.Tb = (float*)(ws + align_up(xw_bytes(rows[f], n[f])));
+    ws += fold_ws(rows[f], n[f]);
+    a.n = n[f];
+    a.rows = rows[f];
+    a.rows_R = rows_R[f];
+    a.tiles = (int)cdiv(rows[f], SUB);
+    a.K = (int)cdiv(n[f], NB);
+    a.tri = (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0;
+    a.err = d_status;
+    int rc = copy_chunk(a.X, a.ldX, chunk[f], ld_chunk[f], rows[f], n[f], chunk_dtype, s);
+    if (rc != IFK_OK) return rc;
+    if (b.nf == MAX_FOLDS) {
+      rc = fold_run_batch(b, prec, s);
+      if (rc != IFK_OK) return rc;
+      b.nf = 0;
+    }
+  }
+  return fold_run_batch(b, prec, s);
+}
+
 size_t ifk_finalize_workspace(int64_t n) {
   if (n <= 0) return 0;
   return align_up((size_t)n * xw_ld(n) * sizeof(float)) + fold_ws(n, n);
@@ -129,6 +186,79 @@ int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, doub
     if (rc != IFK_OK) return rc;
   }
   return finish_factor(R_out, ld_out, out_dtype, Rf, ldF, n, d_status, s);
+}
+
+size_t ifk_finalize_batched_workspace(int nfactors, const int64_t* n) {
+  if (nfactors <= 0 || !n) return 0;
+  size_t b = 0;
+  for (int f = 0; f < nfactors; ++f)
+    if (n[f] > 0) b += ifk_finalize_workspace(n[f]);
+  return b;
+}
+
+int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
+                         const int64_t* rows_R, const int64_t* n, const double* rows_total,
+                         double damping, void* const* R_out, const int64_t* ld_out, int out_dtype,
+                         int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                         ifk_stream_t stream) {
+  if (nfactors < 0 ||
+      (nfactors > 0 && (!R_in || !ldR || !rows_R || !n || !rows_total || !R_out || !ld_out)))
+    return IFK_ERR_ARG;
+  if (!dtype_ok(out_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec) || !(damping >= 0)) return IFK_ERR_ARG;
+  for (int f = 0; f < nfactors; ++f) {
+    if (!R_in[f] || !R_out[f] || !(rows_total[f] > 0)) return IFK_ERR_ARG;
+    if (n[f] <= 0 || ldR[f] < n[f] || ld_out[f] < n[f]) return IFK_ERR_SHAPE;
+    if (rows_R[f] < n[f]) return IFK_ERR_RANK;
+  }
+  if (!workspace || !aligned(workspace) ||
+      workspace_bytes < ifk_finalize_batched_workspace(nfactors, n))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = out_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  char* ws = (char*)workspace;
+  float* Rf[MAX_FOLDS];
+  int base = 0;
+  while (base < nfactors) {
+    FoldBatch b;
+    b.nf = 0;
+    const int cnt = std::min(MAX_FOLDS, nfactors - base);
+    for (int q = 0; q < cnt; ++q) {
+      const int f = base + q;
+      const int64_t ldF = xw_ld(n[f]);
+      Rf[q] = (float*)ws;
+      char* fws = ws + align_up((size_t)n[f] * ldF * sizeof(float));
+      ws += ifk_finalize_workspace(n[f]);
+      int rc = scale_upper(Rf[q], ldF, R_in[f], ldR[f], n[f], (float)std::sqrt(rows_total[f]), s);
+      if (rc != IFK_OK) return rc;
+      if (damping > 0) {
+        FoldArgs& a = b.f[b.nf++];
+        a.R = Rf[q];
+        a.ldR = ldF;
+        a.X = (float*)fws;
+        a.ldX = xw_ld(n[f]);
+        a.Tb = (float*)(fws + align_up(xw_bytes(n[f], n[f])));
+        a.n = n[f];
+        a.rows = n[f];
+        a.rows_R = n[f];
+        a.tiles = (int)cdiv(n[f], SUB);
+        a.K = (int)cdiv(n[f], NB);
+        a.tri = 1;
+        a.err = d_status;
+        rc = fill_scaled_identity(a.X, a.ldX, n[f], (float)std::sqrt(damping), s);
+        if (rc != IFK_OK) return rc;
+      }
+    }
+    int rc = fold_run_batch(b, prec, s);
+    if (rc != IFK_OK) return rc;
+    for (int q = 0; q < cnt; ++q) {
+      const int f = base + q;
+      rc = finish_factor(R_out[f], ld_out[f], out_dtype, Rf[q], xw_ld(n[f]), n[f], d_status, s);
+      if (rc != IFK_OK) return rc;
+    }
+    base += cnt;
+  }
+  return IFK_OK;
 }
 
 size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {

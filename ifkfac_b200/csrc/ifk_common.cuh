@@ -52,6 +52,25 @@ struct MutView {
   }
 };
 
+// 4 consecutive floats from a 16-byte aligned address; elements at index >= valid read as 0.
+__device__ __forceinline__ float4 ld4(const float* p, int valid) {
+  if (valid >= 4) return *reinterpret_cast<const float4*>(p);
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (valid > 0) r.x = p[0];
+  if (valid > 1) r.y = p[1];
+  if (valid > 2) r.z = p[2];
+  return r;
+}
+__device__ __forceinline__ void st4(float* p, float4 v, int valid) {
+  if (valid >= 4) {
+    *reinterpret_cast<float4*>(p) = v;
+    return;
+  }
+  if (valid > 0) p[0] = v.x;
+  if (valid > 1) p[1] = v.y;
+  if (valid > 2) p[2] = v.z;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -24,6 +24,13 @@ struct FoldArgs {
   int* err;        // device status word for bounded-wait timeouts (may be null)
 };
 
+// Up to MAX_FOLDS independent folds share one wave schedule (blockIdx.z selects the fold).
+constexpr int MAX_FOLDS = 8;
+struct FoldBatch {
+  FoldArgs f[MAX_FOLDS];
+  int nf;
+};
+
 size_t fold_tbuf_bytes(int64_t rows);
 size_t xw_bytes(int64_t rows, int64_t n);
 int64_t xw_ld(int64_t n);
@@ -38,6 +45,7 @@ int scale_upper(float* Rout, int64_t ldo, const float* Rin, int64_t ldi, int64_t
                 cudaStream_t s);
 // Run the fold waves.  prec: IFK_PREC_FP32 or IFK_PREC_BF16.
 int fold_run(const FoldArgs& a, int prec, cudaStream_t s);
+int fold_run_batch(const FoldBatch& b, int prec, cudaStream_t s);
 // Cast an n x n fp32 factor to the output type and flag non-finite entries.
 int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t ldR, int64_t n,
                   int* d_status, cudaStream_t s);

@@ -39,26 +39,115 @@ __device__ __forceinline__ bool task_active(const FoldArgs& a, int t, int k, int
   return true;
 }
 
-constexpr size_t panel_smem_bytes() {
-  return sizeof(float) * ((size_t)SUB * LDP + 3 * (size_t)NB * LDP + 3 * NB);
+// ---- panel factorisation ----------------------------------------------------
+// 128 threads; thread t owns rows t and t + 128 of the sub-tile.  The NB = 64
+// panel columns are processed in 4 leaves of 16: a leaf's two rows per thread
+// live in registers and each column step needs one reduction of 16 dot
+// products (x_j . x_c for every leaf column c: c == j gives the squared norm,
+// c > j the inputs of w, c < j the entries of Y^T Y for T) and one
+// __syncthreads.  The reduction is a warp butterfly that halves the payload
+// each round (8+4+2+1+1 shuffles), then 4 warp partials from shared memory.
+// After a leaf, its compact-WY block reflector is applied to the remaining
+// panel columns; after the panel, T is assembled from the leaf T's by
+// T_AB = -T_A (Y_A^T Y_B) T_B.
+constexpr int PT2 = 128;
+constexpr int LEAF = 16;
+constexpr int NLEAF = NB / LEAF;
+static_assert(SUB == 2 * PT2, "panel kernel maps two rows to each thread");
+
+struct PanelSmem {
+  float P[SUB * LDP];        // X_t[:, panel] -> Y
+  float Rk[NB * LDP];        // diagonal block of R
+  float G[NB * LDP];         // strict upper part of Y^T Y
+  float Tm[NB * LDP];        // T, row-major
+  float Tmp[NB * LDP];       // scratch of the T assembly / inner-update W
+  float Rl[LEAF * (LEAF + 1)];
+  float part[2][PT2 / 32][LEAF];
+  float tau[NB];
+};
+
+constexpr size_t panel_smem_bytes() { return sizeof(PanelSmem); }
+
+__device__ __forceinline__ void reflector(float aj, float xn2, float& tj, float& beta, float& inv_v0) {
+  if (xn2 == 0.f) {
+    // nothing to annihilate; flip the row if its diagonal is negative
+    tj = aj >= 0.f ? 0.f : 2.f;
+    beta = fabsf(aj);
+    inv_v0 = 0.f;
+  } else {
+    const float nrm = sqrtf(aj * aj + xn2);
+    const float v0 = aj > 0.f ? -xn2 / (aj + nrm) : aj - nrm;
+    beta = nrm;
+    tj = -v0 / nrm;
+    inv_v0 = 1.f / v0;
+  }
+}
+
+// Butterfly reduce-scatter of 16 values over a warp: returns the warp total of
+// value index ((lane>>4)&1)*8 + ((lane>>3)&1)*4 + ((lane>>2)&1)*2 + ((lane>>1)&1).
+__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
+  const unsigned F = 0xffffffffu;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool hi = lane & 16;
+    const float send = hi ? v[k] : v[k + 8];
+    const float keep = hi ? v[k + 8] : v[k];
+    v[k] = keep + __shfl_xor_sync(F, send, 16);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bool hi = lane & 8;
+    const float send = hi ? v[k] : v[k + 4];
+    const float keep = hi ? v[k + 4] : v[k];
+    v[k] = keep + __shfl_xor_sync(F, send, 8);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool hi = lane & 4;
+    const float send = hi ? v[k] : v[k + 2];
+    const float keep = hi ? v[k + 2] : v[k];
+    v[k] = keep + __shfl_xor_sync(F, send, 4);
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? v[0] : v[1];
+    const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(F, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(F, v[0], 1);
+}
+
+// C (m x n block at Cr, Cc of dst) = -A (m x k) * M (k x n) for row-major smem
+// blocks with stride LDP; done by all PT2 threads.  Used for T assembly.
+__device__ __forceinline__ void neg_matmul(float* dst, int dr, int dc, const float* A, int ar, int ac,
+                                           const float* M, int mr, int mc, int m, int k, int n, int tid) {
+  for (int o = tid; o < m * n; o += PT2) {
+    const int i = o / n, j = o % n;
+    float s = 0.f;
+    for (int l = 0; l < k; ++l) s += A[(ar + i) * LDP + ac + l] * M[(mr + l) * LDP + mc + j];
+    dst[(dr + i) * LDP + dc + j] = -s;
+  }
+}
+__device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* A, int ar, int ac,
+                                       const float* M, int mr, int mc, int m, int k, int n, int tid) {
+  for (int o = tid; o < m * n; o += PT2) {
+    const int i = o / n, j = o % n;
+    float s = 0.f;
+    for (int l = 0; l < k; ++l) s += A[(ar + i) * LDP + ac + l] * M[(mr + l) * LDP + mc + j];
+    dst[(dr + i) * LDP + dc + j] = s;
+  }
 }
 
 // One panel factorisation per block: block t handles task (t, wave - t).
-__global__ void __launch_bounds__(PT) fold_panel_kernel(FoldArgs a, int wave) {
+__global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave) {
+  const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
   int64_t lim;
   if (!task_active(a, t, k, &lim)) return;
 
-  extern __shared__ float sm[];
-  float* P = sm;                  // SUB x LDP: X_t[:, panel] -> Y
-  float* Rk = P + SUB * LDP;      // NB x LDP: diagonal block of R
-  float* G = Rk + NB * LDP;       // NB x LDP: strict upper part of Y^T Y
-  float* Tm = G + NB * LDP;       // NB x LDP: column j holds T[:, j]
-  float* dv = Tm + NB * LDP;      // NB: dot products of the current column
-  float* wv = dv + NB;            // NB: w of the current reflector
-  float* tau = wv + NB;           // NB
-
+  extern __shared__ float smraw[];
+  PanelSmem& S = *reinterpret_cast<PanelSmem*>(smraw);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int64_t row0 = (int64_t)t * SUB;
@@ -67,98 +156,212 @@ __global__ void __launch_bounds__(PT) fold_panel_kernel(FoldArgs a, int wave) {
   const int nbk = (int)mn<int64_t>(NB, a.n - c0);
   const int nact = (int)mx<int64_t>(0, mn<int64_t>(nbk, lim - c0));
 
-  for (int idx = tid; idx < SUB * NB; idx += PT) {
-    const int i = idx / NB, j = idx % NB;
-    P[i * LDP + j] = (i < h && j < nbk) ? a.X[(row0 + i) * a.ldX + c0 + j] : 0.f;
+  // X_t panel -> P: 16-byte loads, 8 in flight per thread
+  for (int q0 = tid; q0 < SUB * NB / 4; q0 += 8 * PT2) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = q0 + u * PT2, i = q / (NB / 4), j4 = (q % (NB / 4)) * 4;
+      v[u] = (i < h) ? ld4(a.X + (row0 + i) * a.ldX + c0 + j4, nbk - j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = q0 + u * PT2, i = q / (NB / 4), j4 = (q % (NB / 4)) * 4;
+      float* d = S.P + i * LDP + j4;
+      d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+    }
   }
-  for (int idx = tid; idx < NB * NB; idx += PT) {
-    const int i = idx / NB, j = idx % NB;
-    Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? a.R[(c0 + i) * a.ldR + c0 + j] : 0.f;
-    G[i * LDP + j] = 0.f;
+  for (int q0 = tid; q0 < NB * NB; q0 += 8 * PT2) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = q0 + u * PT2, i = idx / NB, j = idx % NB;
+      v[u] = (i < nbk && j < nbk && j >= i) ? a.R[(c0 + i) * a.ldR + c0 + j] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = q0 + u * PT2, i = idx / NB, j = idx % NB;
+      S.Rk[i * LDP + j] = v[u];
+      S.G[i * LDP + j] = 0.f;
+      S.Tm[i * LDP + j] = 0.f;
+    }
   }
+  if (tid < NB) S.tau[tid] = 0.f;
   __syncthreads();
 
-  for (int j = 0; j < nact; ++j) {
-    // dv[c] = X[:, j] . P[:, c] for every panel column (c == j: squared norm,
-    // c > j: inputs of w, c < j: future entries of Y^T Y).
-    for (int c = warp; c < nbk; c += PT / 32) {
-      float s = 0.f;
-      for (int i = lane; i < h; i += 32) s += P[i * LDP + j] * P[i * LDP + c];
-      s = warp_sum(s);
-      if (lane == 0) dv[c] = s;
+  const int r0 = tid, r1 = tid + PT2;
+  const int vidx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  int buf = 0;
+#pragma unroll 1
+  for (int s = 0; s < NLEAF; ++s) {
+    const int L0 = s * LEAF;
+    if (L0 >= nbk) break;
+    float a0[LEAF], a1[LEAF];
+#pragma unroll
+    for (int c = 0; c < LEAF; ++c) {
+      a0[c] = S.P[r0 * LDP + L0 + c];
+      a1[c] = S.P[r1 * LDP + L0 + c];
     }
-    __syncthreads();
-    const float aj = Rk[j * LDP + j];
-    const float xn2 = dv[j];
-    float tj, beta, inv_v0;
-    if (xn2 == 0.f) {
-      // nothing to annihilate; flip the row if its diagonal is negative
-      tj = aj >= 0.f ? 0.f : 2.f;
-      beta = fabsf(aj);
-      inv_v0 = 0.f;
-    } else {
-      const float nrm = sqrtf(aj * aj + xn2);
-      const float v0 = aj > 0.f ? -xn2 / (aj + nrm) : aj - nrm;
-      beta = nrm;
-      tj = -v0 / nrm;
-      inv_v0 = 1.f / v0;
-    }
-    if (tid < nbk) {
-      const int c = tid;
-      if (c > j) {
-        const float w = Rk[j * LDP + c] + dv[c] * inv_v0;
-        wv[c] = w;
-        Rk[j * LDP + c] -= tj * w;
-      } else if (c < j) {
-        G[c * LDP + j] = dv[c] * inv_v0;
+#pragma unroll
+    for (int jj = 0; jj < LEAF; ++jj) {
+      const int j = L0 + jj;
+      if (j < nact) {
+        float v[LEAF];
+#pragma unroll
+        for (int c = 0; c < LEAF; ++c) v[c] = a0[jj] * a0[c] + a1[jj] * a1[c];
+        const float part = warp_reduce16(v, lane);
+        if ((lane & 1) == 0) S.part[buf][warp][vidx] = part;
+        __syncthreads();
+        float tl = 0.f;
+        if (lane < LEAF) {
+#pragma unroll
+          for (int w = 0; w < PT2 / 32; ++w) tl += S.part[buf][w][lane];
+        }
+        float tot[LEAF];
+#pragma unroll
+        for (int c = 0; c < LEAF; ++c) tot[c] = __shfl_sync(0xffffffffu, tl, c);
+        buf ^= 1;
+        float tj, beta, inv_v0;
+        reflector(S.Rk[j * LDP + j], tot[jj], tj, beta, inv_v0);
+        float wv[LEAF];
+#pragma unroll
+        for (int c = jj + 1; c < LEAF; ++c) {
+          const float r = S.Rk[j * LDP + L0 + c];
+          wv[c] = r + tot[c] * inv_v0;
+          if (tid == 0) S.Rl[jj * (LEAF + 1) + c] = r - tj * wv[c];
+        }
+        if (tid == 0) {
+          S.Rl[jj * (LEAF + 1) + jj] = beta;
+          S.tau[j] = tj;
+#pragma unroll
+          for (int c = 0; c < jj; ++c) S.G[(L0 + c) * LDP + j] = tot[c] * inv_v0;
+        }
+        const float y0 = a0[jj] * inv_v0, y1 = a1[jj] * inv_v0;
+        a0[jj] = y0;
+        a1[jj] = y1;
+        const float ty0 = tj * y0, ty1 = tj * y1;
+#pragma unroll
+        for (int c = jj + 1; c < LEAF; ++c) {
+          a0[c] -= ty0 * wv[c];
+          a1[c] -= ty1 * wv[c];
+        }
       } else {
-        Rk[j * LDP + j] = beta;
-        tau[j] = tj;
+        // beyond the rank bound: identity reflector, zero Householder vector
+        a0[jj] = 0.f;
+        a1[jj] = 0.f;
+        if (tid == 0) {
+#pragma unroll
+          for (int c = jj; c < LEAF; ++c) S.Rl[jj * (LEAF + 1) + c] = S.Rk[j * LDP + L0 + c];
+        }
       }
     }
-    __syncthreads();
-    {
-      const int i = tid;  // one row per thread
-      const float y = P[i * LDP + j] * inv_v0;
-      P[i * LDP + j] = y;
-      const float ty = tj * y;
-      for (int c = j + 1; c < nbk; ++c) P[i * LDP + c] -= ty * wv[c];
+#pragma unroll
+    for (int c = 0; c < LEAF; ++c) {
+      S.P[r0 * LDP + L0 + c] = a0[c];
+      S.P[r1 * LDP + L0 + c] = a1[c];
     }
     __syncthreads();
-  }
-  // inactive columns (beyond the rank bound): identity reflectors
-  for (int idx = tid; idx < SUB * NB; idx += PT) {
-    const int i = idx / NB, j = idx % NB;
-    if (j >= nact) P[i * LDP + j] = 0.f;
-  }
-  if (tid < NB && tid >= nact) tau[tid] = 0.f;
-  __syncthreads();
-
-  // T = (strict_upper(G) + diag(1/tau))^-1, one column per thread; a zero tau
-  // gives a zero row and column of T.
-  if (tid < NB) {
-    const int j = tid;
-    for (int i = 0; i < NB; ++i) Tm[j * LDP + i] = 0.f;
-    if (j < nbk) {
-      Tm[j * LDP + j] = tau[j];
-      for (int i = j - 1; i >= 0; --i) {
-        float s = 0.f;
-        for (int l = i + 1; l <= j; ++l) s += G[i * LDP + l] * Tm[j * LDP + l];
-        Tm[j * LDP + i] = -tau[i] * s;
+    // leaf R block back into Rk; leaf T by the column recursion, one row per lane of warp 0
+    if (tid < LEAF) {
+#pragma unroll
+      for (int c = 0; c < LEAF; ++c)
+        if (c >= tid && L0 + c < nbk) S.Rk[(L0 + tid) * LDP + L0 + c] = S.Rl[tid * (LEAF + 1) + c];
+    } else if (tid >= 32 && tid < 32 + LEAF) {
+      const int i = tid - 32;
+      float Tr[LEAF];
+#pragma unroll
+      for (int jj = 0; jj < LEAF; ++jj) {
+        const float tj = S.tau[L0 + jj];
+        float acc = 0.f;
+#pragma unroll
+        for (int l = 0; l < jj; ++l) acc += Tr[l] * S.G[(L0 + l) * LDP + L0 + jj];
+        Tr[jj] = (i == jj) ? tj : (i < jj ? -tj * acc : 0.f);
       }
+#pragma unroll
+      for (int jj = 0; jj < LEAF; ++jj) S.Tm[(L0 + i) * LDP + L0 + jj] = Tr[jj];
+    }
+    __syncthreads();
+    // apply the leaf's block reflector to the remaining panel columns
+    const int C0 = L0 + LEAF;
+    const int wcI = nbk - C0;
+    if (wcI > 0 && L0 < nact) {
+      // Z = Rk[leaf rows, C] + Y_leaf^T P[:, C] -> Tmp[0..15][C]
+      for (int o = tid; o < LEAF * wcI; o += PT2) {
+        const int jj = o % LEAF, c = C0 + o / LEAF;
+        float z0 = 0.f, z1 = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < SUB; i += 2) {
+          z0 += S.P[i * LDP + L0 + jj] * S.P[i * LDP + c];
+          z1 += S.P[(i + 1) * LDP + L0 + jj] * S.P[(i + 1) * LDP + c];
+        }
+        S.Tmp[jj * LDP + c] = z0 + z1 + S.Rk[(L0 + jj) * LDP + c];
+      }
+      __syncthreads();
+      // W = T_leaf^T Z ; Rk[leaf rows, C] -= W ; W -> Tmp rows 16..31
+      for (int o = tid; o < LEAF * wcI; o += PT2) {
+        const int jj = o % LEAF, c = C0 + o / LEAF;
+        float w = 0.f;
+#pragma unroll
+        for (int l = 0; l < LEAF; ++l) w += S.Tm[(L0 + l) * LDP + L0 + jj] * S.Tmp[l * LDP + c];
+        S.Tmp[(LEAF + jj) * LDP + c] = w;
+        S.Rk[(L0 + jj) * LDP + c] -= w;
+      }
+      __syncthreads();
+      // P[:, C] -= Y_leaf W
+      for (int c = C0; c < nbk; ++c) {
+        float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int l = 0; l < LEAF; ++l) {
+          const float w = S.Tmp[(LEAF + l) * LDP + c];
+          d0 += S.P[r0 * LDP + L0 + l] * w;
+          d1 += S.P[r1 * LDP + L0 + l] * w;
+        }
+        S.P[r0 * LDP + c] -= d0;
+        S.P[r1 * LDP + c] -= d1;
+      }
+      __syncthreads();
     }
   }
+
+  // off-diagonal leaf blocks of G = Y^T Y
+  for (int o = tid; o < 6 * LEAF * LEAF; o += PT2) {
+    const int blk = o / (LEAF * LEAF), e = o % (LEAF * LEAF);
+    const int ab[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+    const int ca = ab[blk][0] * LEAF + e / LEAF, cb = ab[blk][1] * LEAF + e % LEAF;
+    float g0 = 0.f, g1 = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < SUB; i += 2) {
+      g0 += S.P[i * LDP + ca] * S.P[i * LDP + cb];
+      g1 += S.P[(i + 1) * LDP + ca] * S.P[(i + 1) * LDP + cb];
+    }
+    S.G[ca * LDP + cb] = g0 + g1;
+  }
+  __syncthreads();
+  // T assembly: T_{01} = -T_0 G_{01} T_1, T_{23} likewise, then the 32 x 32 coupling
+  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, 16, 16, 16, tid);     // T0 G01
+  matmul(S.Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, 16, 16, 16, tid); // T2 G23
+  __syncthreads();
+  neg_matmul(S.Tm, 0, 16, S.Tmp, 0, 0, S.Tm, 16, 16, 16, 16, 16, tid);   // T01
+  neg_matmul(S.Tm, 32, 48, S.Tmp, 16, 32, S.Tm, 48, 48, 16, 16, 16, tid); // T23
+  __syncthreads();
+  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, 32, 32, 32, tid);   // T_A G_AB (32 x 32)
+  __syncthreads();
+  neg_matmul(S.Tm, 0, 32, S.Tmp, 0, 0, S.Tm, 32, 32, 32, 32, 32, tid);  // T_AB
   __syncthreads();
 
+  // T stored column-major (Tb[j*NB + i] = T[i][j]) for the trailing update
   float* Tb = a.Tb + (size_t)t * NB * NB;
-  for (int idx = tid; idx < NB * NB; idx += PT) Tb[idx] = Tm[(idx / NB) * LDP + (idx % NB)];
-  for (int idx = tid; idx < SUB * NB; idx += PT) {
-    const int i = idx / NB, j = idx % NB;
-    if (i < h && j < nbk) a.X[(row0 + i) * a.ldX + c0 + j] = P[i * LDP + j];
+  for (int idx = tid; idx < NB * NB; idx += PT2) Tb[idx] = S.Tm[(idx % NB) * LDP + idx / NB];
+  for (int q = tid; q < SUB * NB / 4; q += PT2) {
+    const int i = q / (NB / 4), j4 = (q % (NB / 4)) * 4;
+    if (i < h) {
+      const float* sp = S.P + i * LDP + j4;
+      st4(a.X + (row0 + i) * a.ldX + c0 + j4, make_float4(sp[0], sp[1], sp[2], sp[3]), nbk - j4);
+    }
   }
-  for (int idx = tid; idx < NB * NB; idx += PT) {
+  for (int idx = tid; idx < NB * NB; idx += PT2) {
     const int i = idx / NB, j = idx % NB;
-    if (i < nbk && j < nbk && j >= i) a.R[(c0 + i) * a.ldR + c0 + j] = Rk[i * LDP + j];
+    if (i < nbk && j < nbk && j >= i) a.R[(c0 + i) * a.ldR + c0 + j] = S.Rk[i * LDP + j];
   }
 }
 
@@ -168,7 +371,8 @@ constexpr size_t upd_smem_bytes() {
 }
 
 // fp32 trailing update of one (sub-tile, panel, column block) per block.
-__global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldArgs a, int wave) {
+__global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int wave) {
+  const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
   int64_t lim;
@@ -355,7 +559,7 @@ bool set_smem_attr_once() {
 }  // namespace
 
 // Defined in tsqr_tc.cu: tensor-core trailing update of one wave.
-int fold_update_tc_launch(const FoldArgs& a, int wave, cudaStream_t s);
+int fold_update_tc_launch(const FoldBatch& b, int tiles, int64_t ncols, int wave, cudaStream_t s);
 
 int64_t xw_ld(int64_t n) { return cdiv(n, 4) * 4; }
 size_t xw_bytes(int64_t rows, int64_t n) { return (size_t)rows * xw_ld(n) * sizeof(float); }
@@ -398,22 +602,38 @@ int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t
   return IFK_OK;
 }
 
-int fold_run(const FoldArgs& a, int prec, cudaStream_t s) {
-  if (a.rows == 0) return IFK_OK;
+int fold_run_batch(const FoldBatch& b, int prec, cudaStream_t s) {
+  if (b.nf <= 0) return IFK_OK;
   if (!set_smem_attr_once()) return IFK_ERR_CUDA;
-  const int waves = a.tiles + a.K - 1;
-  const dim3 ugrid(a.tiles, (unsigned)cdiv(a.n, WC));
+  int waves = 0, tiles = 0;
+  int64_t ncols = 0;
+  for (int f = 0; f < b.nf; ++f) {
+    if (b.f[f].rows == 0) continue;
+    waves = (int)mx<int64_t>(waves, b.f[f].tiles + b.f[f].K - 1);
+    tiles = (int)mx<int64_t>(tiles, b.f[f].tiles);
+    ncols = mx<int64_t>(ncols, b.f[f].n);
+  }
+  if (waves == 0) return IFK_OK;
+  const dim3 pgrid(tiles, 1, b.nf);
+  const dim3 ugrid(tiles, (unsigned)cdiv(ncols, WC), b.nf);
   for (int w = 0; w < waves; ++w) {
-    fold_panel_kernel<<<a.tiles, PT, panel_smem_bytes(), s>>>(a, w);
+    fold_panel_kernel<<<pgrid, PT2, panel_smem_bytes(), s>>>(b, w);
     if (prec == IFK_PREC_BF16) {
-      const int rc = fold_update_tc_launch(a, w, s);
+      const int rc = fold_update_tc_launch(b, tiles, ncols, w, s);
       if (rc != IFK_OK) return rc;
     } else {
-      fold_update_simt_kernel<<<ugrid, PT, upd_smem_bytes(), s>>>(a, w);
+      fold_update_simt_kernel<<<ugrid, PT, upd_smem_bytes(), s>>>(b, w);
     }
   }
   IFK_CUDA_TRY(cudaGetLastError());
   return IFK_OK;
+}
+
+int fold_run(const FoldArgs& a, int prec, cudaStream_t s) {
+  FoldBatch b;
+  b.f[0] = a;
+  b.nf = 1;
+  return fold_run_batch(b, prec, s);
 }
 
 }  // namespace ifk

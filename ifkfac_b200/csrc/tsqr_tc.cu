@@ -67,7 +67,8 @@ __device__ __forceinline__ void store8(uint32_t addr, const float (&v)[8]) {
                tc::pack_bf16(v[6], v[7]));
 }
 
-__global__ void __launch_bounds__(TPB, 1) fold_update_tc_kernel(FoldArgs a, int wave) {
+__global__ void __launch_bounds__(TPB, 1) fold_update_tc_kernel(FoldBatch fb, int wave) {
+  const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
   if (!task_active_tc(a, t, k)) return;
@@ -92,31 +93,51 @@ __global__ void __launch_bounds__(TPB, 1) fold_update_tc_kernel(FoldArgs a, int 
   if (tid == 0) tc::mbar_init(bar, 1);
 
   // ---- stage operands: X_t^T (A1), Y, T hi/lo ----
-  for (int q = tid; q < SUB * (WT / 8); q += TPB) {  // item: row i, 8 columns
-    const int i = (q & 7) + 8 * (q >> 7), c8 = (q >> 3) & 15;
-    float v[8];
+  constexpr int UN = 4;  // items in flight per thread (2 x 16-byte loads each)
+  for (int q0 = tid; q0 < SUB * (WT / 8); q0 += UN * TPB) {  // item: row i, 8 columns
+    float4 v[UN][2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int c = c8 * 8 + e;
-      v[e] = (i < h && c < wc) ? Xt[(int64_t)i * a.ldX + cs + c] : 0.f;
+    for (int u = 0; u < UN; ++u) {
+      const int q = q0 + u * TPB, i = (q & 7) + 8 * (q >> 7), c8 = (q >> 3) & 15;
+      const float* src = Xt + (int64_t)i * a.ldX + cs + c8 * 8;
+      const bool in = i < h;
+      v[u][0] = in ? ld4(src, wc - c8 * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u][1] = in ? ld4(src + 4, wc - c8 * 8 - 4) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    store8(sbase + OFF_A1 + tc::cm_off<false>(c8 * 8, i, A1_MN, A1_K), v);
+#pragma unroll
+    for (int u = 0; u < UN; ++u) {
+      const int q = q0 + u * TPB, i = (q & 7) + 8 * (q >> 7), c8 = (q >> 3) & 15;
+      const float e8[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                           v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+      store8(sbase + OFF_A1 + tc::cm_off<false>(c8 * 8, i, A1_MN, A1_K), e8);
+    }
   }
-  for (int q = tid; q < SUB * (NB / 8); q += TPB) {  // item: row i, 8 panel columns
-    const int i = (q & 7) + 8 * (q >> 6), j8 = (q >> 3) & 7;
-    float v[8];
+  for (int q0 = tid; q0 < SUB * (NB / 8); q0 += UN * TPB) {  // item: row i, 8 panel columns
+    float4 v[UN][2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int j = j8 * 8 + e;
-      v[e] = (i < h && j < nbk) ? Xt[(int64_t)i * a.ldX + c0 + j] : 0.f;
+    for (int u = 0; u < UN; ++u) {
+      const int q = q0 + u * TPB, i = (q & 7) + 8 * (q >> 6), j8 = (q >> 3) & 7;
+      const float* src = Xt + (int64_t)i * a.ldX + c0 + j8 * 8;
+      const bool in = i < h;
+      v[u][0] = in ? ld4(src, nbk - j8 * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u][1] = in ? ld4(src + 4, nbk - j8 * 8 - 4) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    store8(sbase + OFF_Y + tc::cm_off<true>(i, j8 * 8, Y_I, Y_J), v);
+#pragma unroll
+    for (int u = 0; u < UN; ++u) {
+      const int q = q0 + u * TPB, i = (q & 7) + 8 * (q >> 6), j8 = (q >> 3) & 7;
+      const float e8[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                           v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+      store8(sbase + OFF_Y + tc::cm_off<true>(i, j8 * 8, Y_I, Y_J), e8);
+    }
   }
   for (int q = tid; q < NB * (NB / 8); q += TPB) {  // item: column j of T, 8 rows l
     const int j = (q & 7) + 8 * (q >> 6), l8 = (q >> 3) & 7;
+    const float4 t0 = *reinterpret_cast<const float4*>(Tb + j * NB + l8 * 8);
+    const float4 t1 = *reinterpret_cast<const float4*>(Tb + j * NB + l8 * 8 + 4);
+    const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
     float hi[8], lo[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) tc::split_bf16(Tb[j * NB + l8 * 8 + e], hi[e], lo[e]);
+    for (int e = 0; e < 8; ++e) tc::split_bf16(tv[e], hi[e], lo[e]);
     const uint32_t off = tc::cm_off<true>(j, l8 * 8, B2_MN, B2_K);
     store8(sbase + OFF_B2H + off, hi);
     store8(sbase + OFF_B2L + off, lo);
@@ -234,10 +255,16 @@ __global__ void __launch_bounds__(TPB, 1) fold_update_tc_kernel(FoldArgs a, int 
       float d[32];
       tc::tmem_ld32(lane_base + TM_D3 + mh * WT + q * 32, d);
       if (i < h) {
+        float4 x[8];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int cc = q * 32 + e;
-          if (cc < wc) xrow[cc] -= d[e];
+        for (int e = 0; e < 8; ++e) x[e] = ld4(xrow + q * 32 + 4 * e, wc - q * 32 - 4 * e);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          x[e].x -= d[4 * e];
+          x[e].y -= d[4 * e + 1];
+          x[e].z -= d[4 * e + 2];
+          x[e].w -= d[4 * e + 3];
+          st4(xrow + q * 32 + 4 * e, x[e], wc - q * 32 - 4 * e);
         }
       }
     }
@@ -265,13 +292,13 @@ bool tc_attr_once() {
 
 }  // namespace
 
-int fold_update_tc_launch(const FoldArgs& a, int wave, cudaStream_t s) {
+int fold_update_tc_launch(const FoldBatch& b, int tiles, int64_t ncols, int wave, cudaStream_t s) {
   if (!tc_attr_once()) return IFK_ERR_CUDA;
   // trailing blocks of WT columns start right after the panel of task (t, wave - t);
   // the widest case is panel 0
-  const unsigned gy = (unsigned)cdiv(mx<int64_t>(0, a.n - NB), WT);
+  const unsigned gy = (unsigned)cdiv(mx<int64_t>(0, ncols - NB), WT);
   if (gy == 0) return IFK_OK;
-  fold_update_tc_kernel<<<dim3(a.tiles, gy), TPB, SMEM, s>>>(a, wave);
+  fold_update_tc_kernel<<<dim3(tiles, gy, b.nf), TPB, SMEM, s>>>(b, wave);
   return IFK_OK;
 }
 

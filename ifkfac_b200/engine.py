@@ -10,7 +10,8 @@ reference's hooks (``_n_rows_X`` / ``_n_rows_G``, ifkfac/activation_hooks.py:205
 """
 from __future__ import annotations
 
-from typing import Optional
+import ctypes
+from typing import Optional, Sequence
 
 import torch
 
@@ -70,6 +71,42 @@ class Factor:
         self.rows_seen = 0
 
 
+def _arr(ctype, vals):
+    return (ctype * len(vals))(*vals)
+
+
+def fold_batched(factors: Sequence[Factor], chunks: Sequence[torch.Tensor], ws: torch.Tensor,
+                 trapezoidal: bool = False) -> torch.Tensor:
+    """Fold chunks[i] into factors[i], all in one wave schedule (ifk_tsqr_fold_batched).
+
+    Returns the workspace actually used (grown if ``ws`` was too small)."""
+    L = _lib.lib()
+    cs = []
+    for f, c in zip(factors, chunks):
+        if c.dim() != 2 or c.shape[1] != f.n:
+            raise ValueError(f"chunk of shape {tuple(c.shape)} for a factor of width {f.n}")
+        cs.append(c if c.stride(1) == 1 else c.contiguous())
+    dts = {c.dtype for c in cs}
+    if len(dts) != 1:
+        raise TypeError("all chunks of a batched fold must share one dtype")
+    nf = len(factors)
+    rows = _arr(ctypes.c_int64, [c.shape[0] for c in cs])
+    ns = _arr(ctypes.c_int64, [f.n for f in factors])
+    need = L.ifk_tsqr_fold_batched_workspace(nf, rows, ns)
+    if ws is None or ws.numel() < need:
+        ws = _ws(need, factors[0].device)
+    check(L.ifk_tsqr_fold_batched(
+        nf, _arr(ctypes.c_void_p, [f.R.data_ptr() for f in factors]), ns,
+        _arr(ctypes.c_int64, [f.rows_R for f in factors]), _arr(ctypes.c_void_p, [c.data_ptr() for c in cs]),
+        _arr(ctypes.c_int64, [c.stride(0) for c in cs]), rows, ns, _DT[cs[0].dtype], factors[0].prec,
+        _lib.FOLD_TRAPEZOIDAL_CHUNK if trapezoidal else 0, factors[0].status.data_ptr(), ws.data_ptr(),
+        ws.numel(), _stream()), "ifk_tsqr_fold_batched")
+    for f, c in zip(factors, cs):
+        f.rows_R = min(f.n, f.rows_R + c.shape[0])
+        f.rows_seen += c.shape[0]
+    return ws
+
+
 class LayerCurvature:
     """Device state of one layer's curvature path (factors, natgrad, momentum)."""
 
@@ -85,13 +122,22 @@ class LayerCurvature:
         self.RX = torch.empty(n_in, n_in, dtype=factor_dtype, device=self.device)
         self.RG = torch.empty(n_out, n_out, dtype=factor_dtype, device=self.device)
         self.have_factors = False
-        self.ws_fin = _ws(max(L.ifk_finalize_workspace(n_in), L.ifk_finalize_workspace(n_out)),
+        self.ws_fin = _ws(L.ifk_finalize_batched_workspace(2, _arr(ctypes.c_int64, [n_in, n_out])),
                           self.device)
         self.ws_nat = _ws(L.ifk_natgrad_workspace(n_out, n_in), self.device)
         self.ws_upd = _ws(L.ifk_update_workspace(n_out * n_in), self.device)
         self.nat = torch.empty(n_out, n_in, dtype=torch.float32, device=self.device)
         self.buf: Optional[torch.Tensor] = None
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.fx.status = self.status
+        self.fg.status = self.status
+        rows = max(chunk_rows, 1)
+        self.ws_pair = _ws(L.ifk_tsqr_fold_batched_workspace(
+            2, _arr(ctypes.c_int64, [rows, rows]), _arr(ctypes.c_int64, [n_in, n_out])), self.device)
+
+    def fold(self, x_chunk: torch.Tensor, g_chunk: torch.Tensor) -> None:
+        """Fold an activation chunk into R_X and a gradient chunk into R_G together."""
+        self.ws_pair = fold_batched((self.fx, self.fg), (x_chunk, g_chunk), self.ws_pair)
 
     # ---- factor refresh: get_factors + _update_factors (finite check, dtype) ----
     def refresh(self, damping: float, solve_prec: Optional[int] = None) -> bool:
@@ -101,11 +147,14 @@ class LayerCurvature:
             return False
         L = _lib.lib()
         prec = self.prec if solve_prec is None else solve_prec
-        for f, out in ((self.fx, self.RX), (self.fg, self.RG)):
-            check(L.ifk_finalize(f.R.data_ptr(), f.n, f.rows_R, f.n, float(f.rows_seen),
-                                 float(damping), out.data_ptr(), f.n, _DT[out.dtype], prec,
-                                 self.status.data_ptr(), self.ws_fin.data_ptr(),
-                                 self.ws_fin.numel(), _stream()), "ifk_finalize")
+        fs, outs = (self.fx, self.fg), (self.RX, self.RG)
+        check(L.ifk_finalize_batched(
+            2, _arr(ctypes.c_void_p, [f.R.data_ptr() for f in fs]), _arr(ctypes.c_int64, [f.n for f in fs]),
+            _arr(ctypes.c_int64, [f.rows_R for f in fs]), _arr(ctypes.c_int64, [f.n for f in fs]),
+            _arr(ctypes.c_double, [float(f.rows_seen) for f in fs]), float(damping),
+            _arr(ctypes.c_void_p, [o.data_ptr() for o in outs]), _arr(ctypes.c_int64, [f.n for f in fs]),
+            _DT[self.factor_dtype], prec, self.status.data_ptr(), self.ws_fin.data_ptr(),
+            self.ws_fin.numel(), _stream()), "ifk_finalize_batched")
         self.have_factors = True
         return True
 

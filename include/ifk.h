@@ -106,6 +106,27 @@ IFK_API int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R,
                   int chunk_dtype, int prec, int flags, int* d_status,
                   void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
+/* Workspace bytes for ifk_tsqr_fold_batched. */
+IFK_API size_t ifk_tsqr_fold_batched_workspace(int nfolds, const int64_t* rows, const int64_t* n);
+
+/*
+ * nfolds independent folds in one wave schedule: fold f absorbs rows[f] rows
+ * of chunk[f] (n[f] columns, leading dimension ld_chunk[f]) into R[f]
+ * (n[f] x n[f], leading dimension ldR[f], rows_R[f] meaningful rows), with
+ * the semantics of ifk_tsqr_fold.  The R[f] must not overlap.  Host arrays of
+ * length nfolds; folds of zero rows are skipped.
+ *
+ * Replaces batched_streaming_tsqr_update (ifkfac/triangular.py:331-379) and
+ * the bucketed flush of the hooks (ifkfac/activation_hooks.py:370-457),
+ * without the zero padding: every fold keeps its own row count.  Also used to
+ * fold X and delta of one layer together.
+ */
+IFK_API int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR,
+                          const int64_t* rows_R, const void* const* chunk,
+                          const int64_t* ld_chunk, const int64_t* rows, const int64_t* n,
+                          int chunk_dtype, int prec, int flags, int* d_status,
+                          void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
 /* ---- damping fold ------------------------------------------------------ */
 
 /* Workspace bytes for ifk_finalize on an n x n factor. */
@@ -132,6 +153,20 @@ IFK_API int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t
                  void* R_out, int64_t ld_out, int out_dtype, int prec,
                  int* d_status, void* workspace, size_t workspace_bytes,
                  ifk_stream_t stream);
+
+/* Workspace bytes for ifk_finalize_batched. */
+IFK_API size_t ifk_finalize_batched_workspace(int nfactors, const int64_t* n);
+
+/*
+ * ifk_finalize on nfactors factors in one wave schedule (host arrays of
+ * length nfactors; every factor must be square).  Used to refresh R_X and
+ * R_G of a layer together.
+ */
+IFK_API int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
+                         const int64_t* rows_R, const int64_t* n, const double* rows_total,
+                         double damping, void* const* R_out, const int64_t* ld_out,
+                         int out_dtype, int prec, int* d_status, void* workspace,
+                         size_t workspace_bytes, ifk_stream_t stream);
 
 /* ---- natural gradient ---------------------------------------------------- */
 

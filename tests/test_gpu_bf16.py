@@ -135,3 +135,22 @@ def test_bf16_end_to_end_vs_bf16_linalg_composition():
     assert e_ours < e_ref
     assert rel(nat, g["comp_nat"]) <= e_ref + e_ours + 1e-6
     assert e_ours < 2e-2
+
+
+def test_batched_fold_and_finalize_match_single():
+    """X and delta folded in one wave schedule give the same factors as separate folds."""
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import LayerCurvature
+    from ifkfac_b200 import triangular as T
+    rng = np.random.default_rng(11)
+    n_in, n_out, lam = 320, 200, 1e-2
+    X = _scaled_bf16(rng, 900, n_in)
+    D = _scaled_bf16(rng, 900, n_out)
+    for prec in (FP32, BF16):
+        lc = LayerCurvature(n_in, n_out, DEV, prec, torch.float32, 300)
+        for lo in range(0, 900, 300):
+            lc.fold(_t(X[lo:lo + 300], torch.bfloat16), _t(D[lo:lo + 300], torch.bfloat16))
+        assert lc.refresh(lam)
+        tol = 1e-5 if prec == FP32 else 1e-2
+        assert rel(lc.RX.cpu().numpy(), O.get_factor(O.streaming_tsqr_update(None, X), 900, lam)) < tol
+        assert rel(lc.RG.cpu().numpy(), O.get_factor(O.streaming_tsqr_update(None, D), 900, lam)) < tol
