@@ -16,7 +16,8 @@ LIB_PATH = os.path.join(PKG_DIR, "libifk.so")
 HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "ifk.h")
 
 OK, ERR_RANK, ERR_NONFINITE, ERR_SHAPE, ERR_TIMEOUT, ERR_CUDA, ERR_WORKSPACE, ERR_DTYPE, \
-    ERR_ARG, ERR_DEVICE = range(10)
+    ERR_ARG, ERR_DEVICE, ERR_LIMIT = range(11)
+NOALLOC_MAX_N = 4096
 F32, BF16 = 0, 1
 PREC_AUTO, PREC_FP32, PREC_BF16 = 0, 1, 2
 FOLD_TRAPEZOIDAL_CHUNK = 1
@@ -43,6 +44,8 @@ SIGNATURES = {
     "ifk_natgrad_workspace": (_sz, [_i64, _i64]),
     "ifk_natgrad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
                            _vp, _sz, _vp]),
+    "ifk_natgrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int,
+                                   _vp, _vp]),
     "ifk_natgrad_bias": (_int, [_vp, _vp, _i64, _int, _vp, _i64, _int, _vp, _sz, _vp]),
     "ifk_update_workspace": (_sz, [_i64]),
     "ifk_update": (_int, [_vp, _vp, _vp, _i64, _dbl, _dbl, _dbl, _dbl, _int, _vp, _sz, _vp]),

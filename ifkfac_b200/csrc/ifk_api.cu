@@ -37,6 +37,7 @@ const char* ifk_status_string(int status) {
     case IFK_ERR_DTYPE: return "unsupported element type";
     case IFK_ERR_ARG: return "invalid argument";
     case IFK_ERR_DEVICE: return "current device is not compute capability 10.0 (sm_100a)";
+    case IFK_ERR_LIMIT: return "size above the fixed scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }

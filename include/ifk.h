@@ -52,6 +52,7 @@ extern "C" {
 #define IFK_ERR_DTYPE      7  /* unsupported element type */
 #define IFK_ERR_ARG        8  /* other invalid argument (null pointer, bad flag) */
 #define IFK_ERR_DEVICE     9  /* current device is not an sm_100 part */
+#define IFK_ERR_LIMIT     10  /* size above the fixed scratch of ifk_natgrad_noalloc */
 
 /* ---- element types ---------------------------------------------------- */
 #define IFK_F32   0
@@ -190,6 +191,30 @@ IFK_API int ifk_natgrad(const float* grad_W, int64_t ld_g,
                 int r_dtype, float* nat, int64_t ld_nat,
                 int64_t n_out, int64_t n_in, int prec, int* d_status,
                 void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/* Largest factor order ifk_natgrad_noalloc accepts. */
+#define IFK_NOALLOC_MAX_N 4096
+
+/*
+ * ifk_natgrad for callers that cannot allocate device memory where they call
+ * it (a step run inside another framework's operator whose memory belongs to
+ * that framework's pool, or a host runtime that only works with buffers it was
+ * given up front).  It takes no workspace: the scratch of the tensor-core
+ * solves is a fixed 2 MiB array inside the library, held on every GPU that
+ * loads the library until the process exits.  Same arguments and results as
+ * ifk_natgrad; n_out and n_in above IFK_NOALLOC_MAX_N give IFK_ERR_LIMIT
+ * before anything is queued.  The first call on a device looks up that
+ * device's address of the array (make it before any stream capture).  All
+ * calls share the one array, so calls that overlap on the GPU (different
+ * streams, or different host threads on one device) race and must be ordered
+ * by the caller.  No cudaMalloc or cudaFree is made.
+ * This entry point has no counterpart in the reference.
+ */
+IFK_API int ifk_natgrad_noalloc(const float* grad_W, int64_t ld_g,
+                        const void* R_X, int64_t ld_rx, const void* R_G, int64_t ld_rg,
+                        int r_dtype, float* nat, int64_t ld_nat,
+                        int64_t n_out, int64_t n_in, int prec, int* d_status,
+                        ifk_stream_t stream);
 
 /*
  * nat_b = R_G^-1 R_G^-T grad_b (vectors of n_out fp32; may alias).

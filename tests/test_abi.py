@@ -22,7 +22,7 @@ def test_library_exports_header_symbols():
 
 def test_status_strings_and_version():
     assert b"sm_100a" in _lib.lib().ifk_version()
-    for s in range(10):
+    for s in range(11):
         assert _lib.status_string(s)
     assert "rank" in _lib.status_string(_lib.ERR_RANK)
 
