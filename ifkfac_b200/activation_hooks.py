@@ -1,0 +1,346 @@
+"""Forward/backward hooks that stream captured activations into device R factors.
+
+Mirror of the reference's ``RawActivationHooks`` (ifkfac/activation_hooks.py):
+same constructor, same lifecycle (enable / get_factors / clear / remove /
+flush / pause / resume / capture / n_samples_accumulated), same chunk
+preprocessing (3-D reshape with random row subsampling, Conv2d im2col with
+subsampling, optional ones column, optional chunk transforms) and the same
+three accumulation modes (streaming, batched flush, deferred window).  The
+folds, the damping fold and the checks run in libifk.so: each factor keeps an
+n x n fp32 buffer on the device plus the host row counts, and
+``_R_X[module]`` / ``_R_G[module]`` are views of the reference's trapezoidal
+running R (``R[:min(rows, n)]``).  Chunks may be bf16 (autocast): they are
+folded natively on the tensor cores, where the reference's geqrf has no bf16
+kernel.
+"""
+from __future__ import annotations
+
+import logging
+import warnings
+from contextlib import contextmanager
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .engine import Factor, fold_batched
+
+logger = logging.getLogger(__name__)
+
+warnings.filterwarnings("ignore", message="Full backward hook is firing", category=UserWarning)
+
+
+class IFKFACRankError(RuntimeError):
+    """Raised when accumulated p < n for a layer, making QR rank-deficient."""
+
+
+def unfold_conv_input(x: torch.Tensor, module: nn.Conv2d) -> torch.Tensor:
+    """im2col rows (B*L, C_in*kH*kW) (ifkfac/activation_hooks.py:489-499)."""
+    x_unf = F.unfold(x, kernel_size=module.kernel_size, dilation=module.dilation,
+                     padding=module.padding, stride=module.stride)
+    B, C_kk, L = x_unf.shape
+    return x_unf.permute(0, 2, 1).reshape(B * L, C_kk)
+
+
+def reshape_conv_grad(delta: torch.Tensor) -> torch.Tensor:
+    """(B*H_out*W_out, C_out) rows (ifkfac/activation_hooks.py:501-504)."""
+    B, C_out, H, W = delta.shape
+    return delta.permute(0, 2, 3, 1).reshape(B * H * W, C_out)
+
+
+def prepare_x(x: torch.Tensor, module: nn.Module, max_conv_rows: int, max_seq_rows: int,
+              augment_bias: bool, transform=None) -> torch.Tensor:
+    """Activation chunk of one forward call (ifkfac/activation_hooks.py:519-548)."""
+    if isinstance(module, nn.Conv2d):
+        x = unfold_conv_input(x, module)
+        if max_conv_rows > 0 and x.shape[0] > max_conv_rows:
+            x = x[torch.randperm(x.shape[0], device=x.device)[:max_conv_rows]]
+    elif x.ndim > 2:
+        x = x.reshape(-1, x.shape[-1])
+        if max_seq_rows > 0 and x.shape[0] > max_seq_rows:
+            x = x[torch.randperm(x.shape[0], device=x.device)[:max_seq_rows]]
+    if augment_bias and isinstance(module, nn.Linear) and module.bias is not None:
+        x = torch.cat([x, torch.ones(x.shape[0], 1, device=x.device, dtype=x.dtype)], dim=1)
+    if transform is not None:
+        x = transform(x)
+    return x
+
+
+def prepare_g(delta: torch.Tensor, module: nn.Module, max_seq_rows: int, transform=None) -> torch.Tensor:
+    """Gradient chunk of one backward call (ifkfac/activation_hooks.py:601-615)."""
+    if isinstance(module, nn.Conv2d):
+        delta = reshape_conv_grad(delta)
+    elif delta.ndim > 2:
+        delta = delta.reshape(-1, delta.shape[-1])
+        if max_seq_rows > 0 and delta.shape[0] > max_seq_rows:
+            delta = delta[torch.randperm(delta.shape[0], device=delta.device)[:max_seq_rows]]
+    if transform is not None:
+        delta = transform(delta)
+    return delta
+
+
+def _chunk_for_fold(c: torch.Tensor) -> torch.Tensor:
+    if c.dtype not in (torch.float32, torch.bfloat16):
+        c = c.float()
+    return c if c.stride(-1) == 1 else c.contiguous()
+
+
+class RawActivationHooks:
+    """Forward/backward hooks that maintain streaming-TSQR R factors on the device.
+
+    Parameters are those of the reference (ifkfac/activation_hooks.py:128-216);
+    ``precision`` selects the fold arithmetic (``_lib.PREC_AUTO``: tensor cores
+    for bf16 chunks, fp32 CUDA cores for fp32 chunks).
+    """
+
+    _SEQ_SUBSAMPLE: int = 2048
+
+    def __init__(self, model: nn.Module, damping: float = 1e-2, max_out_dim: int = 0,
+                 augment_bias: bool = False, max_conv_rows: int = 512,
+                 max_seq_rows: Optional[int] = None, batched: bool = False, deferred: bool = False,
+                 deferred_window: int = 5, precision: int = _lib.PREC_AUTO):
+        if batched and deferred:
+            raise ValueError("batched and deferred modes are mutually exclusive")
+        self.model = model
+        self.damping = damping
+        self.augment_bias = augment_bias
+        self.max_conv_rows = max_conv_rows
+        self.max_seq_rows = self._SEQ_SUBSAMPLE if max_seq_rows is None else max_seq_rows
+        self.batched = batched
+        self.deferred = deferred
+        self.deferred_window = deferred_window
+        self.precision = precision
+        self.chunk_transform_X = None
+        self.chunk_transform_G = None
+        self._handles: List = []
+        self._enabled = False
+        self._fx: Dict[nn.Module, Optional[Factor]] = {}
+        self._fg: Dict[nn.Module, Optional[Factor]] = {}
+        self._n_rows_X: Dict[nn.Module, int] = {}
+        self._n_rows_G: Dict[nn.Module, int] = {}
+        self._pending_X: Dict[nn.Module, List[torch.Tensor]] = {}
+        self._pending_G: Dict[nn.Module, List[torch.Tensor]] = {}
+        self._raw_X: Dict[nn.Module, List[torch.Tensor]] = {}
+        self._raw_G: Dict[nn.Module, List[torch.Tensor]] = {}
+        self._ws: Dict[Tuple, torch.Tensor] = {}
+        self._linear_layers: List[nn.Module] = []
+        for module in model.modules():
+            if not isinstance(module, (nn.Linear, nn.Conv2d)):
+                continue
+            if max_out_dim > 0:
+                out_dim = module.out_features if isinstance(module, nn.Linear) else module.out_channels
+                if out_dim > max_out_dim:
+                    continue
+            self._linear_layers.append(module)
+            self._fx[module] = None
+            self._fg[module] = None
+            self._n_rows_X[module] = 0
+            self._n_rows_G[module] = 0
+            self._pending_X[module] = []
+            self._pending_G[module] = []
+            self._raw_X[module] = []
+            self._raw_G[module] = []
+
+    # ---- estimator interface ----
+    @property
+    def linear_layers(self) -> List[nn.Module]:
+        return self._linear_layers
+
+    @property
+    def is_enabled(self) -> bool:
+        return self._enabled
+
+    @property
+    def _R_X(self) -> Dict[nn.Module, Optional[torch.Tensor]]:
+        """Running R_X per layer in the reference's shape (min(rows, n), n), or None."""
+        return {m: (None if f is None or f.rows_seen == 0 else f.R[: f.rows_R]) for m, f in self._fx.items()}
+
+    @property
+    def _R_G(self) -> Dict[nn.Module, Optional[torch.Tensor]]:
+        return {m: (None if f is None or f.rows_seen == 0 else f.R[: f.rows_R]) for m, f in self._fg.items()}
+
+    def enable(self) -> None:
+        if self._enabled:
+            return
+        for module in self._linear_layers:
+            self._handles.append(module.register_forward_hook(self._forward_hook))
+            self._handles.append(module.register_full_backward_hook(self._backward_hook))
+        self._enabled = True
+
+    def pause(self) -> None:
+        self._enabled = False
+
+    def resume(self) -> None:
+        self._enabled = True
+
+    @contextmanager
+    def capture(self):
+        previous = getattr(self, "_enabled", False)
+        self._enabled = True
+        try:
+            yield self
+        finally:
+            self._enabled = previous
+
+    def n_samples_accumulated(self, module: Optional[nn.Module] = None) -> int:
+        target = module or (self._linear_layers[0] if self._linear_layers else None)
+        return 0 if target is None else self._n_rows_X.get(target, 0)
+
+    # ---- device state ----
+    def _factor(self, table, module, n: int, device) -> Factor:
+        f = table[module]
+        if f is None or f.n != n:
+            f = Factor(n, device, self.precision)
+            table[module] = f
+        return f
+
+    def _workspace(self, key, nbytes, device) -> torch.Tensor:
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def _fold_now(self, table, module, chunk: torch.Tensor) -> None:
+        if not chunk.is_cuda:
+            raise ValueError("ifkfac_b200 hooks need CUDA activations (no CPU path)")
+        chunk = _chunk_for_fold(chunk)
+        f = self._factor(table, module, chunk.shape[1], chunk.device)
+        key = ("fold", chunk.device)
+        self._ws[key] = fold_batched([f], [chunk], self._ws.get(key))
+
+    def _fold_many(self, table, items) -> None:
+        """Fold (module, chunk) pairs in batched wave schedules of up to 8 folds
+        (the bucketed flush of ifkfac/activation_hooks.py:370-457)."""
+        by_dt: Dict[Tuple, List] = {}
+        for module, chunk in items:
+            chunk = _chunk_for_fold(chunk)
+            by_dt.setdefault((chunk.dtype, chunk.device), []).append((module, chunk))
+        for (dt, dev), lst in by_dt.items():
+            for i in range(0, len(lst), 8):
+                grp = lst[i:i + 8]
+                fs = [self._factor(table, m, c.shape[1], c.device) for m, c in grp]
+                key = ("fold", dev)
+                self._ws[key] = fold_batched(fs, [c for _, c in grp], self._ws.get(key))
+
+    # ---- hooks ----
+    def _forward_hook(self, module, inp, out):
+        if not self._enabled:
+            return
+        x = prepare_x(inp[0].detach(), module, self.max_conv_rows, self.max_seq_rows,
+                      self.augment_bias, self.chunk_transform_X)
+        self._accumulate(module, x, self._fx, self._n_rows_X, self._pending_X, self._raw_X)
+
+    def _backward_hook(self, module, grad_input, grad_output):
+        if not self._enabled:
+            return
+        d = prepare_g(grad_output[0].detach(), module, self.max_seq_rows, self.chunk_transform_G)
+        self._accumulate(module, d, self._fg, self._n_rows_G, self._pending_G, self._raw_G)
+
+    def _accumulate(self, module, chunk, table, nrows, pending, raw):
+        if self.deferred:
+            raw[module].append(chunk)
+            nrows[module] += chunk.shape[0]
+            if len(raw[module]) >= self.deferred_window:
+                c = raw[module][0] if len(raw[module]) == 1 else torch.cat(raw[module], 0)
+                self._fold_now(table, module, c)
+                raw[module] = []
+            return
+        if self.batched:
+            pending[module].append(chunk)
+            nrows[module] += chunk.shape[0]
+            return
+        self._fold_now(table, module, chunk)
+        nrows[module] += chunk.shape[0]
+
+    def flush(self) -> None:
+        """Batched mode: fold every pending chunk (no-op otherwise)."""
+        if not self.batched:
+            return
+        for pending, table in ((self._pending_X, self._fx), (self._pending_G, self._fg)):
+            items = []
+            for m, chunks in pending.items():
+                if chunks:
+                    items.append((m, chunks[0] if len(chunks) == 1 else torch.cat(chunks, 0)))
+                    pending[m] = []
+            if items:
+                self._fold_many(table, items)
+
+    def _drain_deferred(self) -> None:
+        for raw, table in ((self._raw_X, self._fx), (self._raw_G, self._fg)):
+            items = []
+            for m, chunks in raw.items():
+                if chunks:
+                    items.append((m, chunks[0] if len(chunks) == 1 else torch.cat(chunks, 0)))
+                    raw[m] = []
+            if items:
+                self._fold_many(table, items)
+
+    # ---- factors ----
+    def get_factors(self, out_dtype: torch.dtype = torch.float32,
+                    status: Optional[torch.Tensor] = None) -> Dict[nn.Module, Tuple[torch.Tensor, torch.Tensor]]:
+        """Damped R factors per layer with data: finalize_R(R / sqrt(rows), damping)
+        (ifkfac/activation_hooks.py:240-341).  Layers whose R is still trapezoidal
+        are skipped; in batched mode they raise IFKFACRankError, as in the reference."""
+        if self.deferred:
+            self._drain_deferred()
+        factors = {}
+        L = _lib.lib()
+        self.last_status = None
+        self.status_index = {}
+        for module in self._linear_layers:
+            fx, fg = self._fx[module], self._fg[module]
+            if fx is None or fg is None or fx.rows_seen == 0 or fg.rows_seen == 0:
+                continue
+            if fx.rows_R < fx.n or fg.rows_R < fg.n:
+                continue
+            rows_X, rows_G = self._n_rows_X[module], self._n_rows_G[module]
+            if self.batched:
+                if rows_X < fx.n:
+                    raise IFKFACRankError(f"Layer {module}: accumulated {rows_X} rows for X, "
+                                          f"but need >= n_in={fx.n} (batched mode).")
+                if rows_G < fg.n:
+                    raise IFKFACRankError(f"Layer {module}: accumulated {rows_G} rows for δ, "
+                                          f"but need >= n_out={fg.n} (batched mode).")
+            dev = fx.R.device
+            if self.last_status is None:
+                # one device status word per layer: the fused finite check of the damping fold
+                self.last_status = torch.zeros(len(self._linear_layers), dtype=torch.int32, device=dev)
+            self.status_index[module] = len(self.status_index)
+            outs = [torch.empty(f.n, f.n, dtype=out_dtype, device=dev) for f in (fx, fg)]
+            import ctypes
+            arr = lambda t, v: (t * len(v))(*v)
+            ns = [fx.n, fg.n]
+            ws = self._workspace(("fin", dev), L.ifk_finalize_batched_workspace(2, arr(ctypes.c_int64, ns)), dev)
+            st = status if status is not None else self.last_status[self.status_index[module]:]
+            prec = _lib.PREC_BF16 if (out_dtype == torch.bfloat16 or fx.prec == _lib.PREC_BF16) else self.precision
+            _lib.check(L.ifk_finalize_batched(
+                2, arr(ctypes.c_void_p, [fx.R.data_ptr(), fg.R.data_ptr()]), arr(ctypes.c_int64, ns),
+                arr(ctypes.c_int64, [fx.rows_R, fg.rows_R]), arr(ctypes.c_int64, ns),
+                arr(ctypes.c_double, [float(rows_X), float(rows_G)]), float(self.damping),
+                arr(ctypes.c_void_p, [o.data_ptr() for o in outs]), arr(ctypes.c_int64, ns),
+                _lib.BF16 if out_dtype == torch.bfloat16 else _lib.F32, prec, st.data_ptr(),
+                ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream), "ifk_finalize_batched")
+            factors[module] = (outs[0], outs[1])
+        return factors
+
+    def clear(self) -> None:
+        for module in self._linear_layers:
+            for f in (self._fx[module], self._fg[module]):
+                if f is not None:
+                    f.clear()
+            self._n_rows_X[module] = 0
+            self._n_rows_G[module] = 0
+            self._pending_X[module] = []
+            self._pending_G[module] = []
+            self._raw_X[module] = []
+            self._raw_G[module] = []
+
+    def remove(self) -> None:
+        for h in self._handles:
+            h.remove()
+        self._handles.clear()
+        self._enabled = False
+        self.clear()

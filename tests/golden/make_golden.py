@@ -25,7 +25,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _np(t):
-    return t.detach().cpu().float().numpy() if t.dtype == torch.bfloat16 else t.detach().cpu().numpy()
+    # a copy: .numpy() of a CPU tensor shares its storage, and parameters keep changing
+    t = t.detach().cpu()
+    return (t.float() if t.dtype == torch.bfloat16 else t).numpy().copy()
 
 
 def _scaled(g, p, n, dtype, lo=0.0, hi=math.log(100.0)):
