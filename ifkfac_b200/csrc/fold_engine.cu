@@ -1,0 +1,712 @@
+// Persistent streaming-TSQR fold on the tensor cores (IFK_PREC_BF16 path).
+//
+// The fold R <- qr([R; X]).R is cut into tasks COL(f, t, cb): fold f, row
+// sub-tile t (SUB = 256 rows) and column block cb (WB = 128 columns, i.e. two
+// panels of NB = 64).  One CTA per SM takes tickets from a global counter in
+// wave order (t + cb), which is a topological order of the dependencies:
+//   COL(f, t, cb) starts after COL(f, t-1, cb) is done (R rows of every panel
+//   in column block cb are final for sub-tile t-1), and applies panel k < 2cb
+//   of sub-tile t once that panel is published by COL(f, t, k/2).
+// A task only waits for lower tickets, which were handed to CTAs already
+// running, so the schedule cannot deadlock; every wait is bounded anyway and
+// reports IFK_ERR_TIMEOUT.
+//
+// A task keeps its 256 x 128 block of X in TMEM as an fp32 master (D3) and a
+// bf16 operand image of it in shared memory.  Applying panel k (compact WY:
+// Y_k, T_k published as ready-to-copy shared-memory images) is
+//   D1 = X^T Y (tcgen05, K = 256)  ->  W^T = D1 + R[k rows, cb]^T
+//   D2 = W^T T (3-term bf16 split) ->  R[k rows, cb] -= D2^T
+//   D3 += -Y W2 (accumulates into the fp32 master in TMEM)
+// After the applies the task factors its own two panels (panel.cuh) from the
+// fp32 master, publishes their Y / T images and R diagonal blocks, applies the
+// first to the second half of the block, and marks itself done.  X is read
+// from the caller's chunk once; there is no working copy in global memory.
+#include "ifk_common.cuh"
+#include "ifk_internal.h"
+#include "panel.cuh"
+#include "tc.cuh"
+
+namespace ifk {
+
+namespace {
+
+constexpr int WB = 128;   // columns of a task
+constexpr int TPB = 256;  // 8 warps; warps w and w + 4 share TMEM lanes 32(w%4)..+31
+static_assert(TPB == panel::PT2, "the persistent fold runs the panel with all its threads");
+constexpr int MAXW = 384; // waves per launch
+using panel::LDP;
+using panel::PanelSmem;
+
+// published per (fold, sub-tile, panel): Y image (32 KB) + T hi / lo images (8 KB each)
+constexpr uint32_t YIMG = SUB * NB * 2;
+constexpr uint32_t TIMG = NB * NB * 2;
+constexpr uint32_t PIMG = YIMG + 2 * TIMG;
+
+// shared memory: a union of the apply operands and the panel workspace, then the images
+constexpr uint32_t SZ_A1 = WB * SUB * 2;     // X^T bf16, MN-major (mn = column c, k = row i)
+constexpr uint32_t SZ_A2 = WB * NB * 2;      // W^T hi / lo, K-major (mn = c, k = j)
+constexpr uint32_t OFF_A1 = 0;
+constexpr uint32_t OFF_A2H = OFF_A1 + SZ_A1;
+constexpr uint32_t OFF_A2L = OFF_A2H + SZ_A2;
+constexpr uint32_t OFF_B3 = OFF_A2L + SZ_A2;  // W2 bf16, K-major (mn = c, k = j)
+constexpr uint32_t APPLY_END = OFF_B3 + SZ_A2;
+constexpr uint32_t UNION = ((sizeof(PanelSmem) > APPLY_END ? sizeof(PanelSmem) : APPLY_END) + 1023) / 1024 * 1024;
+constexpr uint32_t OFF_Y = UNION;             // Y image: B of GEMM1 (MN-major), A of GEMM3 (K-major)
+constexpr uint32_t OFF_TH = OFF_Y + YIMG;     // T hi / lo images, K-major (mn = j, k = l)
+constexpr uint32_t OFF_TL = OFF_TH + TIMG;
+constexpr uint32_t OFF_BAR = OFF_TL + TIMG;
+constexpr uint32_t SMEM = OFF_BAR + 64;
+
+constexpr uint32_t A1_MN = 128, A1_K = (WB / 8) * 128;  // 128, 2048
+constexpr uint32_t Y_I = 1024, Y_J = 128;
+constexpr uint32_t A2_MN = 128, A2_K = (WB / 8) * 128;  // 128, 2048
+constexpr uint32_t B2_MN = 128, B2_K = (NB / 8) * 128;  // 128, 1024
+constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
+
+enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2 };
+
+#ifdef IFK_TRACE
+// Diagnostic build only: per-task timestamps (globaltimer, ns), 16 int64 per task.
+__device__ long long g_trace[1 << 18];
+__device__ int g_trace_n;
+__device__ __forceinline__ long long gtime() {
+  long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define TR_DECL long long tr[16] = {};
+#define TR_SET(i, v) tr[i] = (v)
+#define TR_ADD(i, v) tr[i] += (v)
+#define TR_NOW() gtime()
+#define TR_FLUSH()                                                     \
+  if (threadIdx.x == 0) {                                              \
+    const int slot = atomicAdd(&g_trace_n, 1);                         \
+    if (slot < (1 << 14))                                              \
+      for (int q_ = 0; q_ < 16; ++q_) g_trace[slot * 16 + q_] = tr[q_]; \
+  }
+#else
+#define TR_DECL
+#define TR_SET(i, v)
+#define TR_ADD(i, v)
+#define TR_NOW() 0
+#define TR_FLUSH()
+#endif
+
+struct PFold {
+  float* R;
+  int64_t ldR;
+  const void* X;
+  int64_t ldX;
+  int xkind;
+  float ident;  // diagonal value when xkind == XK_IDENT
+  int64_t n, rows, rows_R;
+  int T, K, CB, tri;
+  int* done;     // [T][CB]
+  int* pflag;    // [T][K]
+  uint8_t* img;  // [T][K][PIMG]
+};
+
+struct PFBatch {
+  PFold f[MAX_FOLDS];
+  int nf;
+  int nwaves;
+  int ntasks;
+  int* ctr;     // ticket counter
+  int* abort_;  // set when a wait gave up: every CTA stops
+  int* status;  // caller's status word (may be null)
+  int wave_off[MAXW + 1];
+};
+
+__device__ __forceinline__ void st16(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void store8(uint32_t addr, const float (&v)[8]) {
+  st16(addr, make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]), tc::pack_bf16(v[4], v[5]),
+                        tc::pack_bf16(v[6], v[7])));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Thread 0 waits for *flag != 0 (bounded); the CTA learns the outcome through smem.
+__device__ __forceinline__ bool cta_wait_flag(const int* flag, const PFBatch& b, int* s_ok) {
+  if (threadIdx.x == 0) {
+    int ok = 0;
+    for (uint32_t it = 0; it < (1u << 24); ++it) {
+      if (ld_acquire(flag)) {
+        ok = 1;
+        break;
+      }
+      if ((it & 31) == 31 && *((volatile int*)b.abort_)) break;
+      __nanosleep(64);
+    }
+    if (!ok) {
+      atomicExch(b.abort_, 1);
+      if (b.status) atomicExch(b.status, IFK_ERR_TIMEOUT);
+    }
+    *s_ok = ok;
+  }
+  __syncthreads();
+  const bool ok = *(volatile int*)s_ok != 0;
+  __syncthreads();
+  return ok;
+}
+
+__device__ __forceinline__ void cta_publish(int* flag) {
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) st_release(flag, 1);
+}
+
+// fp32 value of chunk element (i, j) (rows/cols already bounds-checked)
+__device__ __forceinline__ void load_row32(const PFold& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
+  if (F.xkind == XK_IDENT) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = (e < valid && gi == gj + e) ? F.ident : 0.f;
+  } else if (F.xkind == XK_BF16) {
+    const __nv_bfloat16* p = (const __nv_bfloat16*)F.X + gi * F.ldX + gj;
+    const bool vec = valid >= 32 && ((((uintptr_t)p) & 15) == 0);
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = reinterpret_cast<const uint4*>(p)[q];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[q * 8 + 2 * e] = __uint_as_float(w[e] << 16);
+          v[q * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = e < valid ? __bfloat162float(p[e]) : 0.f;
+    }
+  } else {
+    const float* p = (const float*)F.X + gi * F.ldX + gj;
+    const bool vec = ((((uintptr_t)p) & 15) == 0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 x;
+      if (vec) {
+        x = ld4(p + 4 * q, valid - 4 * q);
+      } else {
+        x.x = 4 * q < valid ? p[4 * q] : 0.f;
+        x.y = 4 * q + 1 < valid ? p[4 * q + 1] : 0.f;
+        x.z = 4 * q + 2 < valid ? p[4 * q + 2] : 0.f;
+        x.w = 4 * q + 3 < valid ? p[4 * q + 3] : 0.f;
+      }
+      v[4 * q] = x.x;
+      v[4 * q + 1] = x.y;
+      v[4 * q + 2] = x.z;
+      v[4 * q + 3] = x.w;
+    }
+  }
+}
+
+struct Ctx {
+  uint8_t* sm;
+  uint32_t sb;
+  uint32_t tm;
+  uint64_t* bar;
+  uint32_t phase;
+  bool ok;
+};
+
+__device__ __forceinline__ void mma_wait(Ctx& c) {
+  c.ok = tc::mbar_wait(c.bar, c.phase) && c.ok;
+  c.phase ^= 1;
+  tc::fence_after();
+}
+
+__device__ __forceinline__ void sync_for_mma() {
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+}
+
+// bf16 operand image A1 (X^T) from the fp32 master in TMEM (all 128 columns, both halves)
+__device__ void refresh_a1(Ctx& c) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  {
+    const int h = tid >> 7;  // warps 0-3: rows 0..127, warps 4-7: rows 128..255
+    const int r = tid;
+    const uint32_t base = c.tm + ((uint32_t)((warp & 3) * 32) << 16) + TM_D3 + h * WB;
+#pragma unroll 1
+    for (int q = 0; q < WB / 32; ++q) {
+      float v[32];
+      tc::tmem_ld32(base + q * 32, v);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float e8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) e8[e] = v[g * 8 + e];
+        store8(c.sb + OFF_A1 + tc::cm_off<false>(q * 32 + g * 8, r, A1_MN, A1_K), e8);
+      }
+    }
+  }
+}
+
+// Apply panel k (Y / T images in smem, A1 current) to the task's block; when
+// skip_half0 the first 64 columns are the panel itself and are left alone in R.
+__device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t cs, int wc, bool skip_half0) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int col = tid & 127;   // trailing column of this thread == TMEM lane
+  const int jh = tid >> 7;     // which 32 of the 64 panel columns this thread handles
+  const uint32_t lane_base = c.tm + ((uint32_t)((warp & 3) * 32) << 16);
+  if (tid == 0) {
+    constexpr uint32_t id1 = tc::idesc_bf16(128, NB, true, true);
+#pragma unroll 1
+    for (int s = 0; s < SUB / 16; ++s) {
+      const uint64_t ad = tc::sdesc(c.sb + OFF_A1 + s * 2 * A1_K, A1_K, A1_MN);
+      const uint64_t bd = tc::sdesc(c.sb + OFF_Y + s * 2 * Y_I, Y_I, Y_J);
+      tc::mma_bf16(c.tm + TM_D1, ad, bd, id1, s > 0);
+    }
+    tc::commit(c.bar);
+  }
+  mma_wait(c);
+  const bool rcol = col < wc && !(skip_half0 && col < NB);
+  {
+    const int half = jh;
+    float w[32];
+    tc::tmem_ld32(lane_base + TM_D1 + half * 32, w);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float hi[8], lo[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = half * 32 + g * 8 + e;
+        const float r = (j < nbk && col < wc) ? F.R[(k0 + j) * F.ldR + cs + col] : 0.f;
+        tc::split_bf16(w[g * 8 + e] + r, hi[e], lo[e]);
+      }
+      const uint32_t off = tc::cm_off<true>(col, half * 32 + g * 8, A2_MN, A2_K);
+      store8(c.sb + OFF_A2H + off, hi);
+      store8(c.sb + OFF_A2L + off, lo);
+    }
+  }
+  sync_for_mma();
+  if (tid == 0) {
+    constexpr uint32_t id2 = tc::idesc_bf16(128, NB, false, false);
+#pragma unroll 1
+    for (int s = 0; s < NB / 16; ++s) {
+      const uint64_t ah = tc::sdesc(c.sb + OFF_A2H + s * 2 * A2_K, A2_K, A2_MN);
+      const uint64_t al = tc::sdesc(c.sb + OFF_A2L + s * 2 * A2_K, A2_K, A2_MN);
+      const uint64_t bh = tc::sdesc(c.sb + OFF_TH + s * 2 * B2_K, B2_K, B2_MN);
+      const uint64_t bl = tc::sdesc(c.sb + OFF_TL + s * 2 * B2_K, B2_K, B2_MN);
+      tc::mma_bf16(c.tm + TM_D2, ah, bh, id2, s > 0);
+      tc::mma_bf16(c.tm + TM_D2, ah, bl, id2, 1);
+      tc::mma_bf16(c.tm + TM_D2, al, bh, id2, 1);
+    }
+    tc::commit(c.bar);
+  }
+  mma_wait(c);
+  {
+    const int half = jh;
+    float w[32];
+    tc::tmem_ld32(lane_base + TM_D2 + half * 32, w);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = half * 32 + g * 8 + e;
+        v[e] = w[g * 8 + e];
+        if (j < nbk && rcol) F.R[(k0 + j) * F.ldR + cs + col] -= v[e];
+      }
+      store8(c.sb + OFF_B3 + tc::cm_off<true>(col, half * 32 + g * 8, A2_MN, A2_K), v);
+    }
+  }
+  sync_for_mma();
+  if (tid == 0) {
+    // D3 += (-Y) W2: negate-A bit of the instruction descriptor
+    constexpr uint32_t id3 = tc::idesc_bf16(128, WB, false, false) | (1u << 13);
+#pragma unroll 1
+    for (int mh = 0; mh < 2; ++mh) {
+#pragma unroll 1
+      for (int s = 0; s < NB / 16; ++s) {
+        const uint64_t ad = tc::sdesc(c.sb + OFF_Y + mh * 16 * Y_I + s * 2 * Y_J, Y_J, Y_I);
+        const uint64_t bd = tc::sdesc(c.sb + OFF_B3 + s * 2 * A2_K, A2_K, A2_MN);
+        tc::mma_bf16(c.tm + TM_D3 + mh * WB, ad, bd, id3, 1);
+      }
+    }
+    tc::commit(c.bar);
+  }
+  mma_wait(c);
+}
+
+// Y, T hi and T lo images (contiguous in smem as in global): 16-byte cp.async, all in flight.
+__device__ void copy_images_in(Ctx& c, const uint8_t* src) {
+  for (int i = threadIdx.x; i < (int)(PIMG / 16); i += TPB)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(c.sb + OFF_Y + i * 16), "l"(src + i * 16)
+                 : "memory");
+  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+}
+
+__device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_ok) {
+  const PFold& F = b.f[f];
+  TR_DECL
+  TR_SET(0, f);
+  TR_SET(1, t);
+  TR_SET(2, cb);
+  TR_SET(3, TR_NOW());
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t row0 = (int64_t)t * SUB;
+  const int h = (int)mn<int64_t>(SUB, F.rows - row0);
+  const int64_t cs = (int64_t)cb * WB;
+  const int wc = (int)mn<int64_t>(WB, F.n - cs);
+  const int64_t lim = mn<int64_t>(F.n, F.rows_R + row0 + h);
+  const int kfirst = F.tri ? (int)(row0 / NB) : 0;
+  int* done = F.done + (size_t)t * F.CB + cb;
+
+  if (F.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
+    cta_publish(done);
+    return;
+  }
+  if (t > 0 && !cta_wait_flag(F.done + (size_t)(t - 1) * F.CB + cb, b, s_ok)) return;
+  TR_SET(4, TR_NOW());
+
+  // ---- X block -> fp32 master in TMEM (D3) + bf16 image A1 ----
+  tc::fence_after();
+  {
+    const int hh = tid >> 7;
+    const int r = tid;
+    const uint32_t base = c.tm + ((uint32_t)((warp & 3) * 32) << 16) + TM_D3 + hh * WB;
+#pragma unroll 1
+    for (int q = 0; q < WB / 32; ++q) {
+      float v[32];
+      if (r < h) {
+        load_row32(F, row0 + r, cs + q * 32, wc - q * 32, v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0.f;
+      }
+      tmem_st32(base + q * 32, v);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float e8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) e8[e] = v[g * 8 + e];
+        store8(c.sb + OFF_A1 + tc::cm_off<false>(q * 32 + g * 8, r, A1_MN, A1_K), e8);
+      }
+    }
+  }
+  tmem_st_wait();
+  bool a1_valid = true;
+  TR_SET(5, TR_NOW());
+
+  // ---- apply the panels of sub-tile t left of this block ----
+  const int kend = (int)mn<int64_t>(2 * cb, cdiv(lim, NB));
+#pragma unroll 1
+  for (int k = kfirst; k < kend; ++k) {
+#ifdef IFK_TRACE
+    const long long w0 = TR_NOW();
+#endif
+    if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
+    TR_ADD(9, TR_NOW() - w0);
+    TR_ADD(10, 1);
+    copy_images_in(c, F.img + ((size_t)t * F.K + k) * PIMG);
+    if (!a1_valid) {
+      tc::fence_before();
+      __syncthreads();
+      tc::fence_after();
+      refresh_a1(c);
+    }
+    sync_for_mma();
+    apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false);
+    a1_valid = false;
+  }
+
+  TR_SET(6, TR_NOW());
+  // ---- factor the block's own panels ----
+  PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
+#pragma unroll 1
+  for (int q = 0; q < 2; ++q) {
+    const int kk = 2 * cb + q;
+    const int64_t c0 = (int64_t)kk * NB;
+    if (kk >= F.K || c0 >= lim || kk < kfirst) continue;
+    const int nbk = (int)mn<int64_t>(NB, F.n - c0);
+    const int nact = (int)mn<int64_t>(nbk, lim - c0);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    // panel columns from the fp32 master (rows beyond the sub-tile are zero there)
+    {
+      const int hh = tid >> 7;
+      const int r = tid;
+      const uint32_t base = c.tm + ((uint32_t)((warp & 3) * 32) << 16) + TM_D3 + hh * WB + q * NB;
+#pragma unroll 1
+      for (int g = 0; g < 2; ++g) {
+        float v[32];
+        tc::tmem_ld32(base + g * 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) S.P[(g * 32 + e) * panel::SP + r] = v[e];
+      }
+    }
+    for (int idx = tid; idx < NB * NB; idx += TPB) {
+      const int i = idx / NB, j = idx % NB;
+      S.Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? F.R[(c0 + i) * F.ldR + c0 + j] : 0.f;
+    }
+    __syncthreads();
+#ifdef IFK_TRACE
+    const long long p0 = TR_NOW();
+#endif
+    panel::panel_factor(S, nbk, nact);
+    TR_ADD(11, TR_NOW() - p0);
+    TR_ADD(12, 1);
+    // Y image (bf16, K-major for GEMM3 / MN-major for GEMM1) and T hi / lo images
+    for (int it = tid; it < SUB * (NB / 8); it += TPB) {
+      const int i = it >> 3, j8 = it & 7;
+      float e8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) e8[e] = S.P[(j8 * 8 + e) * panel::SP + i];
+      store8(c.sb + OFF_Y + tc::cm_off<true>(i, j8 * 8, Y_I, Y_J), e8);
+    }
+    for (int it = tid; it < NB * (NB / 8); it += TPB) {
+      const int j = it >> 3, l8 = it & 7;
+      float hi[8], lo[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tc::split_bf16(S.Tm[(l8 * 8 + e) * LDP + j], hi[e], lo[e]);
+      const uint32_t off = tc::cm_off<true>(j, l8 * 8, B2_MN, B2_K);
+      store8(c.sb + OFF_TH + off, hi);
+      store8(c.sb + OFF_TL + off, lo);
+    }
+    for (int idx = tid; idx < NB * NB; idx += TPB) {
+      const int i = idx / NB, j = idx % NB;
+      if (i < nbk && j < nbk && j >= i) F.R[(c0 + i) * F.ldR + c0 + j] = S.Rk[i * LDP + j];
+    }
+    __syncthreads();
+    {
+      uint4* dst = reinterpret_cast<uint4*>(F.img + ((size_t)t * F.K + kk) * PIMG);
+      const uint4* srcs = reinterpret_cast<const uint4*>(c.sm + OFF_Y);
+      for (int i = tid; i < (int)(PIMG / 16); i += TPB) dst[i] = srcs[i];
+    }
+    cta_publish(F.pflag + (size_t)t * F.K + kk);
+    if (q == 0 && wc > NB) {
+      // the first panel also acts on the block's second half
+      refresh_a1(c);
+      sync_for_mma();
+      apply_panel(c, F, c0, nbk, cs, wc, true);
+    }
+  }
+  tc::fence_before();
+  cta_publish(done);
+  TR_SET(7, TR_NOW());
+  TR_FLUSH();
+}
+
+__device__ __forceinline__ void decode(const PFBatch& b, int tk, int* f, int* t, int* cb) {
+  int lo = 0, hi = b.nwaves;  // wave_off[lo] <= tk < wave_off[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (b.wave_off[mid] <= tk) lo = mid;
+    else hi = mid;
+  }
+  const int d = lo;
+  int r = tk - b.wave_off[d];
+  for (int q = 0; q < b.nf; ++q) {
+    const PFold& F = b.f[q];
+    const int tlo = d - F.CB + 1 > 0 ? d - F.CB + 1 : 0;
+    const int thi = d < F.T - 1 ? d : F.T - 1;
+    const int cnt = thi >= tlo ? thi - tlo + 1 : 0;
+    if (r < cnt) {
+      *f = q;
+      *t = tlo + r;
+      *cb = d - *t;
+      return;
+    }
+    r -= cnt;
+  }
+  *f = -1;
+}
+
+__global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_constant__ PFBatch b) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
+  int* s_tk = reinterpret_cast<int*>(sm + OFF_BAR + 16);
+  int* s_ok = reinterpret_cast<int*>(sm + OFF_BAR + 20);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (warp == 0) tc::tmem_alloc(tslot, TM_COLS);
+  if (tid == 0) tc::mbar_init(bar, 1);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  Ctx c;
+  c.sm = sm;
+  c.sb = tc::smem_u32(sm);
+  c.tm = *tslot;
+  c.bar = bar;
+  c.phase = 0;
+  c.ok = true;
+#pragma unroll 1
+  for (;;) {
+    if (tid == 0) *s_tk = *((volatile int*)b.abort_) ? b.ntasks : atomicAdd(b.ctr, 1);
+    __syncthreads();
+    const int tk = *s_tk;
+    __syncthreads();
+    if (tk >= b.ntasks) break;
+    int f, t, cb;
+    decode(b, tk, &f, &t, &cb);
+    if (f < 0) break;
+    run_task(c, b, f, t, cb, s_ok);
+    if (!c.ok) {
+      if (tid == 0) {
+        atomicExch(b.abort_, 1);
+        if (b.status) atomicExch(b.status, IFK_ERR_TIMEOUT);
+      }
+      break;
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_free(c.tm, TM_COLS);
+  }
+}
+
+int num_sms() {
+  static thread_local int dev_cached = -1, sms = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev != dev_cached) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(fold_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM) != cudaSuccess)
+      return 0;
+    dev_cached = dev;
+  }
+  return sms;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+}  // namespace
+
+#ifdef IFK_TRACE
+extern "C" __attribute__((visibility("default"))) int ifk_trace_read(long long* dst, int max_tasks) {
+  int n = 0;
+  if (cudaMemcpyFromSymbol(&n, g_trace_n, sizeof(int)) != cudaSuccess) return -1;
+  n = n < max_tasks ? n : max_tasks;
+  if (n > (1 << 14)) n = 1 << 14;
+  if (cudaMemcpyFromSymbol(dst, g_trace, (size_t)n * 16 * sizeof(long long)) != cudaSuccess) return -1;
+  const int zero = 0;
+  cudaMemcpyToSymbol(g_trace_n, &zero, sizeof(int));
+  return n;
+}
+extern "C" __attribute__((visibility("default"))) int ifk_trace_panel_phases(unsigned long long* dst) {
+  if (cudaMemcpyFromSymbol(dst, panel::g_panel_phase, 16 * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  unsigned long long z[16] = {};
+  cudaMemcpyToSymbol(panel::g_panel_phase, z, sizeof(z));
+  return 0;
+}
+#endif
+
+size_t pfold_workspace(int nf, const PFoldDesc* d) {
+  size_t b = 256;
+  for (int f = 0; f < nf; ++f) {
+    if (d[f].rows <= 0) continue;
+    const int64_t T = cdiv(d[f].rows, SUB), K = cdiv(d[f].n, NB), CB = cdiv(d[f].n, WB);
+    b += align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
+  }
+  return b;
+}
+
+int64_t pfold_max_rows(int64_t n) { return (int64_t)(MAXW - cdiv(n, WB) + 1) * SUB; }
+
+int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s) {
+  const int sms = num_sms();
+  if (sms <= 0) return IFK_ERR_CUDA;
+  int first = 0;
+  while (first < nf) {
+    // a group of up to MAX_FOLDS folds shares one launch; groups run one after another
+    // and reuse the workspace from its start
+    PFBatch b;
+    b.nf = 0;
+    b.status = status;
+    b.ctr = (int*)ws;
+    b.abort_ = (int*)ws + 1;
+    int idx[MAX_FOLDS];
+    int q = first;
+    for (; q < nf && b.nf < MAX_FOLDS; ++q)
+      if (d[q].rows > 0) idx[b.nf++] = q;
+    char* w = (char*)ws + 256;
+    int maxw = 0;
+    for (int g = 0; g < b.nf; ++g) {  // flags first, so one memset clears them all
+      const PFoldDesc& D = d[idx[g]];
+      PFold& F = b.f[g];
+      F.R = D.R;
+      F.ldR = D.ldR;
+      F.X = D.X;
+      F.ldX = D.ldX;
+      F.xkind = D.xkind;
+      F.ident = D.ident;
+      F.n = D.n;
+      F.rows = D.rows;
+      F.rows_R = D.rows_R;
+      F.T = (int)cdiv(F.rows, SUB);
+      F.K = (int)cdiv(F.n, NB);
+      F.CB = (int)cdiv(F.n, WB);
+      F.tri = D.tri;
+      if (F.T + F.CB - 1 > MAXW) return IFK_ERR_SHAPE;  // callers split chunks (pfold_max_rows)
+      F.done = (int*)w;
+      w += align256((size_t)F.T * F.CB * 4);
+      F.pflag = (int*)w;
+      w += align256((size_t)F.T * F.K * 4);
+      maxw = maxw > F.T + F.CB - 1 ? maxw : F.T + F.CB - 1;
+    }
+    const size_t flag_bytes = (size_t)(w - (char*)ws);
+    for (int g = 0; g < b.nf; ++g) {
+      b.f[g].img = (uint8_t*)w;
+      w += (size_t)b.f[g].T * b.f[g].K * PIMG;
+    }
+    if (b.nf > 0) {
+      b.nwaves = maxw;
+      int acc = 0;
+      for (int dd = 0; dd < maxw; ++dd) {
+        b.wave_off[dd] = acc;
+        for (int g = 0; g < b.nf; ++g) {
+          const int tlo = dd - b.f[g].CB + 1 > 0 ? dd - b.f[g].CB + 1 : 0;
+          const int thi = dd < b.f[g].T - 1 ? dd : b.f[g].T - 1;
+          if (thi >= tlo) acc += thi - tlo + 1;
+        }
+      }
+      b.wave_off[maxw] = acc;
+      b.ntasks = acc;
+      IFK_CUDA_TRY(cudaMemsetAsync(ws, 0, flag_bytes, s));
+      const int grid = acc < sms ? acc : sms;
+      fold_persistent_kernel<<<grid, TPB, SMEM, s>>>(b);
+      IFK_CUDA_TRY(cudaGetLastError());
+    }
+    first = q;
+  }
+  return IFK_OK;
+}
+
+}  // namespace ifk

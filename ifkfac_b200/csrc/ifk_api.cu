@@ -17,7 +17,49 @@ bool dtype_ok(int d) { return d == IFK_F32 || d == IFK_BF16; }
 bool prec_ok(int p) { return p == IFK_PREC_AUTO || p == IFK_PREC_FP32 || p == IFK_PREC_BF16; }
 cudaStream_t S(ifk_stream_t s) { return (cudaStream_t)s; }
 
-size_t fold_ws(int64_t rows, int64_t n) { return align_up(xw_bytes(rows, n)) + align_up(fold_tbuf_bytes(rows)); }
+size_t wave_ws(int64_t rows, int64_t n) { return align_up(xw_bytes(rows, n)) + align_up(fold_tbuf_bytes(rows)); }
+size_t pers_ws(int64_t rows, int64_t n) {
+  PFoldDesc d{};
+  d.n = n;
+  d.rows = std::min<int64_t>(rows, pfold_max_rows(n));
+  return align_up(pfold_workspace(1, &d));
+}
+// per-fold workspace: enough for either schedule (fp32 waves or the persistent tensor-core fold)
+size_t fold_ws(int64_t rows, int64_t n) { return std::max(wave_ws(rows, n), pers_ws(rows, n)); }
+
+// Persistent tensor-core folds, splitting chunks taller than one launch allows.
+int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStream_t s) {
+  PFoldDesc d[MAX_FOLDS];
+  int64_t done_rows[MAX_FOLDS] = {};
+  for (int base = 0; base < nf; base += MAX_FOLDS) {
+    const int cnt = std::min(MAX_FOLDS, nf - base);
+    for (;;) {
+      bool any = false;
+      for (int q = 0; q < cnt; ++q) {
+        const PFoldDesc& D = in[base + q];
+        d[q] = D;
+        const int64_t left = D.rows - done_rows[q];
+        const int64_t take = std::min<int64_t>(left, pfold_max_rows(D.n));
+        d[q].rows = take > 0 ? take : 0;
+        if (take > 0) {
+          any = true;
+          d[q].rows_R = std::min<int64_t>(D.n, D.rows_R + done_rows[q]);
+          if (D.xkind == 1)
+            d[q].X = (const char*)D.X + done_rows[q] * D.ldX * 2;
+          else if (D.xkind == 0)
+            d[q].X = (const char*)D.X + done_rows[q] * D.ldX * 4;
+          if (D.tri && done_rows[q] > 0) return IFK_ERR_SHAPE;  // trapezoidal chunks come in one piece
+          done_rows[q] += take;
+        }
+      }
+      if (!any) break;
+      const int rc = pfold_run(cnt, d, ws, status, s);
+      if (rc != IFK_OK) return rc;
+    }
+    for (int q = 0; q < cnt; ++q) done_rows[q] = 0;
+  }
+  return IFK_OK;
+}
 
 }  // namespace
 
@@ -69,6 +111,11 @@ int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int6
   if (!workspace || !aligned(workspace) || workspace_bytes < fold_ws(rows, n))
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  if (prec == IFK_PREC_BF16) {
+    PFoldDesc d{R, ldR, chunk, ld_chunk, chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, n, rows, rows_R,
+                (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0};
+    return run_persistent(1, &d, workspace, d_status, S(stream));
+  }
   FoldArgs a;
   a.R = R;
   a.ldR = ldR;
@@ -115,6 +162,21 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   cudaStream_t s = S(stream);
+  if (prec == IFK_PREC_BF16) {
+    PFoldDesc d[MAX_FOLDS];
+    int cnt = 0;
+    for (int f = 0; f < nfolds; ++f) {
+      if (rows[f] == 0) continue;
+      d[cnt++] = PFoldDesc{R[f], ldR[f], chunk[f], ld_chunk[f], chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, n[f],
+                           rows[f], rows_R[f], (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0};
+      if (cnt == MAX_FOLDS) {
+        const int rc = run_persistent(cnt, d, workspace, d_status, s);
+        if (rc != IFK_OK) return rc;
+        cnt = 0;
+      }
+    }
+    return cnt ? run_persistent(cnt, d, workspace, d_status, s) : IFK_OK;
+  }
   char* ws = (char*)workspace;
   FoldBatch b;
   b.nf = 0;
@@ -167,7 +229,11 @@ int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, doub
   void* fws = (char*)workspace + align_up((size_t)n * ldF * sizeof(float));
   int rc = scale_upper(Rf, ldF, R_in, ldR, n, (float)std::sqrt(rows_total), s);
   if (rc != IFK_OK) return rc;
-  if (damping > 0) {
+  if (damping > 0 && prec == IFK_PREC_BF16) {
+    PFoldDesc d{Rf, ldF, nullptr, 0, 2, (float)std::sqrt(damping), n, n, n, 1};
+    rc = run_persistent(1, &d, fws, d_status, s);
+    if (rc != IFK_OK) return rc;
+  } else if (damping > 0) {
     FoldArgs a;
     a.R = Rf;
     a.ldR = ldF;
@@ -217,47 +283,59 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = out_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   cudaStream_t s = S(stream);
-  char* ws = (char*)workspace;
-  float* Rf[MAX_FOLDS];
-  int base = 0;
-  while (base < nfactors) {
-    FoldBatch b;
-    b.nf = 0;
+  // workspace: [fp32 copies of up to MAX_FOLDS factors | one fold area], reused per group
+  for (int base = 0; base < nfactors; base += MAX_FOLDS) {
     const int cnt = std::min(MAX_FOLDS, nfactors - base);
+    char* ws = (char*)workspace;
+    float* Rf[MAX_FOLDS];
     for (int q = 0; q < cnt; ++q) {
       const int f = base + q;
-      const int64_t ldF = xw_ld(n[f]);
       Rf[q] = (float*)ws;
-      char* fws = ws + align_up((size_t)n[f] * ldF * sizeof(float));
-      ws += ifk_finalize_workspace(n[f]);
-      int rc = scale_upper(Rf[q], ldF, R_in[f], ldR[f], n[f], (float)std::sqrt(rows_total[f]), s);
+      ws += align_up((size_t)n[f] * xw_ld(n[f]) * sizeof(float));
+      int rc = scale_upper(Rf[q], xw_ld(n[f]), R_in[f], ldR[f], n[f], (float)std::sqrt(rows_total[f]), s);
       if (rc != IFK_OK) return rc;
-      if (damping > 0) {
-        FoldArgs& a = b.f[b.nf++];
-        a.R = Rf[q];
-        a.ldR = ldF;
-        a.X = (float*)fws;
-        a.ldX = xw_ld(n[f]);
-        a.Tb = (float*)(fws + align_up(xw_bytes(n[f], n[f])));
-        a.n = n[f];
-        a.rows = n[f];
-        a.rows_R = n[f];
-        a.tiles = (int)cdiv(n[f], SUB);
-        a.K = (int)cdiv(n[f], NB);
-        a.tri = 1;
-        a.err = d_status;
-        rc = fill_scaled_identity(a.X, a.ldX, n[f], (float)std::sqrt(damping), s);
-        if (rc != IFK_OK) return rc;
-      }
     }
-    int rc = fold_run_batch(b, prec, s);
-    if (rc != IFK_OK) return rc;
+    if (damping > 0) {
+      int rc;
+      if (prec == IFK_PREC_BF16) {
+        PFoldDesc pd[MAX_FOLDS];
+        for (int q = 0; q < cnt; ++q) {
+          const int f = base + q;
+          pd[q] = PFoldDesc{Rf[q], xw_ld(n[f]), nullptr, 0, 2, (float)std::sqrt(damping), n[f], n[f], n[f], 1};
+        }
+        rc = run_persistent(cnt, pd, ws, d_status, s);
+      } else {
+        FoldBatch b;
+        b.nf = 0;
+        char* fw = ws;
+        for (int q = 0; q < cnt; ++q) {
+          const int f = base + q;
+          FoldArgs& a = b.f[b.nf++];
+          a.R = Rf[q];
+          a.ldR = xw_ld(n[f]);
+          a.X = (float*)fw;
+          a.ldX = xw_ld(n[f]);
+          a.Tb = (float*)(fw + align_up(xw_bytes(n[f], n[f])));
+          fw += fold_ws(n[f], n[f]);
+          a.n = n[f];
+          a.rows = n[f];
+          a.rows_R = n[f];
+          a.tiles = (int)cdiv(n[f], SUB);
+          a.K = (int)cdiv(n[f], NB);
+          a.tri = 1;
+          a.err = d_status;
+          rc = fill_scaled_identity(a.X, a.ldX, n[f], (float)std::sqrt(damping), s);
+          if (rc != IFK_OK) return rc;
+        }
+        rc = fold_run_batch(b, prec, s);
+      }
+      if (rc != IFK_OK) return rc;
+    }
     for (int q = 0; q < cnt; ++q) {
       const int f = base + q;
-      rc = finish_factor(R_out[f], ld_out[f], out_dtype, Rf[q], xw_ld(n[f]), n[f], d_status, s);
+      const int rc = finish_factor(R_out[f], ld_out[f], out_dtype, Rf[q], xw_ld(n[f]), n[f], d_status, s);
       if (rc != IFK_OK) return rc;
     }
-    base += cnt;
   }
   return IFK_OK;
 }

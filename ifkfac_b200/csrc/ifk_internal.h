@@ -35,6 +35,22 @@ size_t fold_tbuf_bytes(int64_t rows);
 size_t xw_bytes(int64_t rows, int64_t n);
 int64_t xw_ld(int64_t n);
 
+// One fold of the persistent tensor-core path (fold_engine.cu): the chunk is
+// read in place (fp32, bf16, or generated as ident * I for the damping fold).
+struct PFoldDesc {
+  float* R;
+  int64_t ldR;
+  const void* X;
+  int64_t ldX;
+  int xkind;     // 0 fp32, 1 bf16, 2 ident * I (X unused)
+  float ident;
+  int64_t n, rows, rows_R;
+  int tri;
+};
+size_t pfold_workspace(int nf, const PFoldDesc* d);
+int64_t pfold_max_rows(int64_t n);
+int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s);
+
 // chunk (bf16 or fp32, rows x n) -> X fp32
 int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows,
                int64_t n, int dtype, cudaStream_t s);

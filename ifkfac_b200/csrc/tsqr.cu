@@ -19,6 +19,7 @@
 // trailing-update launch per wave.
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
+#include "panel.cuh"
 
 namespace ifk {
 
@@ -39,104 +40,10 @@ __device__ __forceinline__ bool task_active(const FoldArgs& a, int t, int k, int
   return true;
 }
 
-// ---- panel factorisation ----------------------------------------------------
-// 128 threads; thread t owns rows t and t + 128 of the sub-tile.  The NB = 64
-// panel columns are processed in 4 leaves of 16: a leaf's two rows per thread
-// live in registers and each column step needs one reduction of 16 dot
-// products (x_j . x_c for every leaf column c: c == j gives the squared norm,
-// c > j the inputs of w, c < j the entries of Y^T Y for T) and one
-// __syncthreads.  The reduction is a warp butterfly that halves the payload
-// each round (8+4+2+1+1 shuffles), then 4 warp partials from shared memory.
-// After a leaf, its compact-WY block reflector is applied to the remaining
-// panel columns; after the panel, T is assembled from the leaf T's by
-// T_AB = -T_A (Y_A^T Y_B) T_B.
-constexpr int PT2 = 128;
-constexpr int LEAF = 16;
-constexpr int NLEAF = NB / LEAF;
-static_assert(SUB == 2 * PT2, "panel kernel maps two rows to each thread");
-
-struct PanelSmem {
-  float P[SUB * LDP];        // X_t[:, panel] -> Y
-  float Rk[NB * LDP];        // diagonal block of R
-  float G[NB * LDP];         // strict upper part of Y^T Y
-  float Tm[NB * LDP];        // T, row-major
-  float Tmp[NB * LDP];       // scratch of the T assembly / inner-update W
-  float Rl[LEAF * (LEAF + 1)];
-  float part[2][PT2 / 32][LEAF];
-  float tau[NB];
-};
-
+// ---- panel factorisation: see panel.cuh -----------------------------------------
+using panel::PT2;
+using panel::PanelSmem;
 constexpr size_t panel_smem_bytes() { return sizeof(PanelSmem); }
-
-__device__ __forceinline__ void reflector(float aj, float xn2, float& tj, float& beta, float& inv_v0) {
-  if (xn2 == 0.f) {
-    // nothing to annihilate; flip the row if its diagonal is negative
-    tj = aj >= 0.f ? 0.f : 2.f;
-    beta = fabsf(aj);
-    inv_v0 = 0.f;
-  } else {
-    const float nrm = sqrtf(aj * aj + xn2);
-    const float v0 = aj > 0.f ? -xn2 / (aj + nrm) : aj - nrm;
-    beta = nrm;
-    tj = -v0 / nrm;
-    inv_v0 = 1.f / v0;
-  }
-}
-
-// Butterfly reduce-scatter of 16 values over a warp: returns the warp total of
-// value index ((lane>>4)&1)*8 + ((lane>>3)&1)*4 + ((lane>>2)&1)*2 + ((lane>>1)&1).
-__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
-  const unsigned F = 0xffffffffu;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const bool hi = lane & 16;
-    const float send = hi ? v[k] : v[k + 8];
-    const float keep = hi ? v[k + 8] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 16);
-  }
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const bool hi = lane & 8;
-    const float send = hi ? v[k] : v[k + 4];
-    const float keep = hi ? v[k + 4] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 8);
-  }
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const bool hi = lane & 4;
-    const float send = hi ? v[k] : v[k + 2];
-    const float keep = hi ? v[k + 2] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 4);
-  }
-  {
-    const bool hi = lane & 2;
-    const float send = hi ? v[0] : v[1];
-    const float keep = hi ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(F, send, 2);
-  }
-  return v[0] + __shfl_xor_sync(F, v[0], 1);
-}
-
-// C (m x n block at Cr, Cc of dst) = -A (m x k) * M (k x n) for row-major smem
-// blocks with stride LDP; done by all PT2 threads.  Used for T assembly.
-__device__ __forceinline__ void neg_matmul(float* dst, int dr, int dc, const float* A, int ar, int ac,
-                                           const float* M, int mr, int mc, int m, int k, int n, int tid) {
-  for (int o = tid; o < m * n; o += PT2) {
-    const int i = o / n, j = o % n;
-    float s = 0.f;
-    for (int l = 0; l < k; ++l) s += A[(ar + i) * LDP + ac + l] * M[(mr + l) * LDP + mc + j];
-    dst[(dr + i) * LDP + dc + j] = -s;
-  }
-}
-__device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* A, int ar, int ac,
-                                       const float* M, int mr, int mc, int m, int k, int n, int tid) {
-  for (int o = tid; o < m * n; o += PT2) {
-    const int i = o / n, j = o % n;
-    float s = 0.f;
-    for (int l = 0; l < k; ++l) s += A[(ar + i) * LDP + ac + l] * M[(mr + l) * LDP + mc + j];
-    dst[(dr + i) * LDP + dc + j] = s;
-  }
-}
 
 // One panel factorisation per block: block t handles task (t, wave - t).
 __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave) {
@@ -146,10 +53,10 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
   int64_t lim;
   if (!task_active(a, t, k, &lim)) return;
 
-  extern __shared__ float smraw[];
+  extern __shared__ __align__(1024) float smraw[];
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(smraw);
   const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
+
   const int64_t row0 = (int64_t)t * SUB;
   const int h = (int)mn<int64_t>(SUB, a.rows - row0);
   const int64_t c0 = (int64_t)k * NB;
@@ -167,8 +74,10 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int q = q0 + u * PT2, i = q / (NB / 4), j4 = (q % (NB / 4)) * 4;
-      float* d = S.P + i * LDP + j4;
-      d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+      S.P[(j4 + 0) * panel::SP + i] = v[u].x;
+      S.P[(j4 + 1) * panel::SP + i] = v[u].y;
+      S.P[(j4 + 2) * panel::SP + i] = v[u].z;
+      S.P[(j4 + 3) * panel::SP + i] = v[u].w;
     }
   }
   for (int q0 = tid; q0 < NB * NB; q0 += 8 * PT2) {
@@ -182,172 +91,10 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
     for (int u = 0; u < 8; ++u) {
       const int idx = q0 + u * PT2, i = idx / NB, j = idx % NB;
       S.Rk[i * LDP + j] = v[u];
-      S.G[i * LDP + j] = 0.f;
-      S.Tm[i * LDP + j] = 0.f;
-    }
-  }
-  if (tid < NB) S.tau[tid] = 0.f;
-  __syncthreads();
-
-  const int r0 = tid, r1 = tid + PT2;
-  const int vidx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-  int buf = 0;
-#pragma unroll 1
-  for (int s = 0; s < NLEAF; ++s) {
-    const int L0 = s * LEAF;
-    if (L0 >= nbk) break;
-    float a0[LEAF], a1[LEAF];
-#pragma unroll
-    for (int c = 0; c < LEAF; ++c) {
-      a0[c] = S.P[r0 * LDP + L0 + c];
-      a1[c] = S.P[r1 * LDP + L0 + c];
-    }
-#pragma unroll
-    for (int jj = 0; jj < LEAF; ++jj) {
-      const int j = L0 + jj;
-      if (j < nact) {
-        float v[LEAF];
-#pragma unroll
-        for (int c = 0; c < LEAF; ++c) v[c] = a0[jj] * a0[c] + a1[jj] * a1[c];
-        const float part = warp_reduce16(v, lane);
-        if ((lane & 1) == 0) S.part[buf][warp][vidx] = part;
-        __syncthreads();
-        float tl = 0.f;
-        if (lane < LEAF) {
-#pragma unroll
-          for (int w = 0; w < PT2 / 32; ++w) tl += S.part[buf][w][lane];
-        }
-        float tot[LEAF];
-#pragma unroll
-        for (int c = 0; c < LEAF; ++c) tot[c] = __shfl_sync(0xffffffffu, tl, c);
-        buf ^= 1;
-        float tj, beta, inv_v0;
-        reflector(S.Rk[j * LDP + j], tot[jj], tj, beta, inv_v0);
-        float wv[LEAF];
-#pragma unroll
-        for (int c = jj + 1; c < LEAF; ++c) {
-          const float r = S.Rk[j * LDP + L0 + c];
-          wv[c] = r + tot[c] * inv_v0;
-          if (tid == 0) S.Rl[jj * (LEAF + 1) + c] = r - tj * wv[c];
-        }
-        if (tid == 0) {
-          S.Rl[jj * (LEAF + 1) + jj] = beta;
-          S.tau[j] = tj;
-#pragma unroll
-          for (int c = 0; c < jj; ++c) S.G[(L0 + c) * LDP + j] = tot[c] * inv_v0;
-        }
-        const float y0 = a0[jj] * inv_v0, y1 = a1[jj] * inv_v0;
-        a0[jj] = y0;
-        a1[jj] = y1;
-        const float ty0 = tj * y0, ty1 = tj * y1;
-#pragma unroll
-        for (int c = jj + 1; c < LEAF; ++c) {
-          a0[c] -= ty0 * wv[c];
-          a1[c] -= ty1 * wv[c];
-        }
-      } else {
-        // beyond the rank bound: identity reflector, zero Householder vector
-        a0[jj] = 0.f;
-        a1[jj] = 0.f;
-        if (tid == 0) {
-#pragma unroll
-          for (int c = jj; c < LEAF; ++c) S.Rl[jj * (LEAF + 1) + c] = S.Rk[j * LDP + L0 + c];
-        }
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < LEAF; ++c) {
-      S.P[r0 * LDP + L0 + c] = a0[c];
-      S.P[r1 * LDP + L0 + c] = a1[c];
-    }
-    __syncthreads();
-    // leaf R block back into Rk; leaf T by the column recursion, one row per lane of warp 0
-    if (tid < LEAF) {
-#pragma unroll
-      for (int c = 0; c < LEAF; ++c)
-        if (c >= tid && L0 + c < nbk) S.Rk[(L0 + tid) * LDP + L0 + c] = S.Rl[tid * (LEAF + 1) + c];
-    } else if (tid >= 32 && tid < 32 + LEAF) {
-      const int i = tid - 32;
-      float Tr[LEAF];
-#pragma unroll
-      for (int jj = 0; jj < LEAF; ++jj) {
-        const float tj = S.tau[L0 + jj];
-        float acc = 0.f;
-#pragma unroll
-        for (int l = 0; l < jj; ++l) acc += Tr[l] * S.G[(L0 + l) * LDP + L0 + jj];
-        Tr[jj] = (i == jj) ? tj : (i < jj ? -tj * acc : 0.f);
-      }
-#pragma unroll
-      for (int jj = 0; jj < LEAF; ++jj) S.Tm[(L0 + i) * LDP + L0 + jj] = Tr[jj];
-    }
-    __syncthreads();
-    // apply the leaf's block reflector to the remaining panel columns
-    const int C0 = L0 + LEAF;
-    const int wcI = nbk - C0;
-    if (wcI > 0 && L0 < nact) {
-      // Z = Rk[leaf rows, C] + Y_leaf^T P[:, C] -> Tmp[0..15][C]
-      for (int o = tid; o < LEAF * wcI; o += PT2) {
-        const int jj = o % LEAF, c = C0 + o / LEAF;
-        float z0 = 0.f, z1 = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < SUB; i += 2) {
-          z0 += S.P[i * LDP + L0 + jj] * S.P[i * LDP + c];
-          z1 += S.P[(i + 1) * LDP + L0 + jj] * S.P[(i + 1) * LDP + c];
-        }
-        S.Tmp[jj * LDP + c] = z0 + z1 + S.Rk[(L0 + jj) * LDP + c];
-      }
-      __syncthreads();
-      // W = T_leaf^T Z ; Rk[leaf rows, C] -= W ; W -> Tmp rows 16..31
-      for (int o = tid; o < LEAF * wcI; o += PT2) {
-        const int jj = o % LEAF, c = C0 + o / LEAF;
-        float w = 0.f;
-#pragma unroll
-        for (int l = 0; l < LEAF; ++l) w += S.Tm[(L0 + l) * LDP + L0 + jj] * S.Tmp[l * LDP + c];
-        S.Tmp[(LEAF + jj) * LDP + c] = w;
-        S.Rk[(L0 + jj) * LDP + c] -= w;
-      }
-      __syncthreads();
-      // P[:, C] -= Y_leaf W
-      for (int c = C0; c < nbk; ++c) {
-        float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-        for (int l = 0; l < LEAF; ++l) {
-          const float w = S.Tmp[(LEAF + l) * LDP + c];
-          d0 += S.P[r0 * LDP + L0 + l] * w;
-          d1 += S.P[r1 * LDP + L0 + l] * w;
-        }
-        S.P[r0 * LDP + c] -= d0;
-        S.P[r1 * LDP + c] -= d1;
-      }
-      __syncthreads();
     }
   }
 
-  // off-diagonal leaf blocks of G = Y^T Y
-  for (int o = tid; o < 6 * LEAF * LEAF; o += PT2) {
-    const int blk = o / (LEAF * LEAF), e = o % (LEAF * LEAF);
-    const int ab[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
-    const int ca = ab[blk][0] * LEAF + e / LEAF, cb = ab[blk][1] * LEAF + e % LEAF;
-    float g0 = 0.f, g1 = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < SUB; i += 2) {
-      g0 += S.P[i * LDP + ca] * S.P[i * LDP + cb];
-      g1 += S.P[(i + 1) * LDP + ca] * S.P[(i + 1) * LDP + cb];
-    }
-    S.G[ca * LDP + cb] = g0 + g1;
-  }
-  __syncthreads();
-  // T assembly: T_{01} = -T_0 G_{01} T_1, T_{23} likewise, then the 32 x 32 coupling
-  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, 16, 16, 16, tid);     // T0 G01
-  matmul(S.Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, 16, 16, 16, tid); // T2 G23
-  __syncthreads();
-  neg_matmul(S.Tm, 0, 16, S.Tmp, 0, 0, S.Tm, 16, 16, 16, 16, 16, tid);   // T01
-  neg_matmul(S.Tm, 32, 48, S.Tmp, 16, 32, S.Tm, 48, 48, 16, 16, 16, tid); // T23
-  __syncthreads();
-  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, 32, 32, 32, tid);   // T_A G_AB (32 x 32)
-  __syncthreads();
-  neg_matmul(S.Tm, 0, 32, S.Tmp, 0, 0, S.Tm, 32, 32, 32, 32, 32, tid);  // T_AB
-  __syncthreads();
+  panel::panel_factor(S, nbk, nact);
 
   // T stored column-major (Tb[j*NB + i] = T[i][j]) for the trailing update
   float* Tb = a.Tb + (size_t)t * NB * NB;
@@ -355,8 +102,11 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
   for (int q = tid; q < SUB * NB / 4; q += PT2) {
     const int i = q / (NB / 4), j4 = (q % (NB / 4)) * 4;
     if (i < h) {
-      const float* sp = S.P + i * LDP + j4;
-      st4(a.X + (row0 + i) * a.ldX + c0 + j4, make_float4(sp[0], sp[1], sp[2], sp[3]), nbk - j4);
+      const float* sp = S.P + i;
+      st4(a.X + (row0 + i) * a.ldX + c0 + j4,
+          make_float4(sp[(j4 + 0) * panel::SP], sp[(j4 + 1) * panel::SP], sp[(j4 + 2) * panel::SP],
+                      sp[(j4 + 3) * panel::SP]),
+          nbk - j4);
     }
   }
   for (int idx = tid; idx < NB * NB; idx += PT2) {
