@@ -4,9 +4,11 @@
 // sub-tile t (SUB = 256 rows) and column block cb (WB = 128 columns, i.e. two
 // panels of NB = 64).  One CTA per SM takes tickets from a global counter in
 // wave order (t + cb), which is a topological order of the dependencies:
-//   COL(f, t, cb) starts after COL(f, t-1, cb) is done (R rows of every panel
-//   in column block cb are final for sub-tile t-1), and applies panel k < 2cb
-//   of sub-tile t once that panel is published by COL(f, t, k/2).
+//   COL(f, t, cb) applies panel k < 2cb of sub-tile t once that panel is
+//   published by COL(f, t, k/2) and COL(f, t-1, cb) has applied its own panel
+//   k (the R rows of panel k in block cb are then final for sub-tile t-1: a
+//   progress counter per task), and factors its own panels once COL(f, t-1, cb)
+//   is done.  Sub-tile t so trails sub-tile t-1 by one apply.
 // A task only waits for lower tickets, which were handed to CTAs already
 // running, so the schedule cannot deadlock; every wait is bounded anyway and
 // reports IFK_ERR_TIMEOUT.
@@ -102,6 +104,7 @@ struct PFold {
   int64_t n, rows, rows_R;
   int T, K, CB, tri;
   int* done;     // [T][CB]
+  int* prog;     // [T][CB]: panels k < prog applied to the block's R rows
   int* pflag;    // [T][K]
   uint8_t* img;  // [T][K][PIMG]
 };
@@ -154,12 +157,12 @@ __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Thread 0 waits for *flag != 0 (bounded); the CTA learns the outcome through smem.
-__device__ __forceinline__ bool cta_wait_flag(const int* flag, const PFBatch& b, int* s_ok) {
+// Thread 0 waits for *flag >= target (bounded); the CTA learns the outcome through smem.
+__device__ __forceinline__ bool cta_wait_ge(const int* flag, int target, const PFBatch& b, int* s_ok) {
   if (threadIdx.x == 0) {
     int ok = 0;
     for (uint32_t it = 0; it < (1u << 24); ++it) {
-      if (ld_acquire(flag)) {
+      if (ld_acquire(flag) >= target) {
         ok = 1;
         break;
       }
@@ -177,12 +180,20 @@ __device__ __forceinline__ bool cta_wait_flag(const int* flag, const PFBatch& b,
   __syncthreads();
   return ok;
 }
-
-__device__ __forceinline__ void cta_publish(int* flag) {
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) st_release(flag, 1);
+__device__ __forceinline__ bool cta_wait_flag(const int* flag, const PFBatch& b, int* s_ok) {
+  return cta_wait_ge(flag, 1, b, s_ok);
 }
+
+// Publish v at *flag once every thread's global writes so far are visible:
+// the barrier orders them before thread 0's fence, whose release is cumulative.
+__device__ __forceinline__ void cta_publish_value(int* flag, int v) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    st_release(flag, v);
+  }
+}
+__device__ __forceinline__ void cta_publish(int* flag) { cta_publish_value(flag, 1); }
 
 // fp32 value of chunk element (i, j) (rows/cols already bounds-checked)
 __device__ __forceinline__ void load_row32(const PFold& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
@@ -383,12 +394,14 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   const int64_t lim = mn<int64_t>(F.n, F.rows_R + row0 + h);
   const int kfirst = F.tri ? (int)(row0 / NB) : 0;
   int* done = F.done + (size_t)t * F.CB + cb;
+  int* prog = F.prog + (size_t)t * F.CB + cb;
+  const int* prev_prog = t > 0 ? F.prog + (size_t)(t - 1) * F.CB + cb : nullptr;
 
   if (F.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
+    cta_publish_value(prog, F.K);
     cta_publish(done);
     return;
   }
-  if (t > 0 && !cta_wait_flag(F.done + (size_t)(t - 1) * F.CB + cb, b, s_ok)) return;
   TR_SET(4, TR_NOW());
 
   // ---- X block -> fp32 master in TMEM (D3) + bf16 image A1 ----
@@ -428,6 +441,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     const long long w0 = TR_NOW();
 #endif
     if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
+    if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
     TR_ADD(9, TR_NOW() - w0);
     TR_ADD(10, 1);
     copy_images_in(c, F.img + ((size_t)t * F.K + k) * PIMG);
@@ -440,10 +454,14 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     sync_for_mma();
     apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false);
     a1_valid = false;
+    cta_publish_value(prog, k + 1);
   }
+  // panels this sub-tile does not reach leave their R rows as they are
+  cta_publish_value(prog, F.K);
 
+  // ---- factor the block's own panels: R diagonal blocks final for sub-tile t-1 ----
+  if (t > 0 && !cta_wait_flag(F.done + (size_t)(t - 1) * F.CB + cb, b, s_ok)) return;
   TR_SET(6, TR_NOW());
-  // ---- factor the block's own panels ----
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
 #pragma unroll 1
   for (int q = 0; q < 2; ++q) {
@@ -633,7 +651,7 @@ size_t pfold_workspace(int nf, const PFoldDesc* d) {
   for (int f = 0; f < nf; ++f) {
     if (d[f].rows <= 0) continue;
     const int64_t T = cdiv(d[f].rows, SUB), K = cdiv(d[f].n, NB), CB = cdiv(d[f].n, WB);
-    b += align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
+    b += 2 * align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
   }
   return b;
 }
@@ -676,6 +694,8 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
       F.tri = D.tri;
       if (F.T + F.CB - 1 > MAXW) return IFK_ERR_SHAPE;  // callers split chunks (pfold_max_rows)
       F.done = (int*)w;
+      w += align256((size_t)F.T * F.CB * 4);
+      F.prog = (int*)w;
       w += align256((size_t)F.T * F.CB * 4);
       F.pflag = (int*)w;
       w += align256((size_t)F.T * F.K * 4);

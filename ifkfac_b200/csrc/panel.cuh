@@ -8,117 +8,251 @@ namespace ifk {
 namespace panel {
 
 #ifdef IFK_TRACE
-// Diagnostic build only: time spent in each phase of panel_factor (ns, summed over panels).
+// Diagnostic build only: slot for per-phase panel times (filled when
+// IFK_TRACE_PANEL is also defined; the phase marks slow the Gram steps down
+// severely, so task-level traces leave them out).
 __device__ unsigned long long g_panel_phase[16];
+#endif
+#ifdef IFK_TRACE_PANEL
+// Time spent in each phase of panel_factor (ns, summed over panels; slot 8
+// counts panels).  Thread 0 keeps the sums in registers.
 __device__ __forceinline__ long long ptime() {
   long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-#define PH_MARK(i)                                                                      \
-  do {                                                                                  \
-    if (threadIdx.x == 0) {                                                             \
-      const long long t_ = ptime();                                                     \
-      atomicAdd(&g_panel_phase[i], (unsigned long long)(t_ - ph_last));                  \
-      ph_last = t_;                                                                     \
-    }                                                                                   \
+#define PH_DECL                  \
+  long long ph_last = ptime();   \
+  long long ph_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define PH_MARK(i)                     \
+  do {                                 \
+    if (threadIdx.x == 0) {            \
+      const long long t_ = ptime();    \
+      ph_acc[i] += t_ - ph_last;       \
+      ph_last = t_;                    \
+    }                                  \
   } while (0)
+#define PH_FLUSH()                                                                   \
+  if (threadIdx.x == 0) {                                                            \
+    for (int q_ = 0; q_ < 8; ++q_) atomicAdd(&g_panel_phase[q_], (unsigned long long)ph_acc[q_]); \
+    atomicAdd(&g_panel_phase[8], 1ull);                                              \
+  }
 #else
+#define PH_DECL
 #define PH_MARK(i) do { } while (0)
+#define PH_FLUSH()
 #endif
 
 constexpr int LDP = NB + 1;   // row stride of the small NB x NB blocks
-constexpr int SP = SUB + 4;    // column stride of the panel: column-major, 16-byte aligned columns
-constexpr int LDW2 = 52;       // row stride of the inner-update W (16-byte aligned rows)
-
-// ---- panel factorisation ----------------------------------------------------
-// 256 threads; thread t owns row t of the sub-tile.  The NB = 64 panel columns
-// are processed in 4 leaves of 16: a leaf's row lives in 16 registers per
-// thread and each column step needs one reduction of 16 dot products
-// (x_j . x_c for every leaf column c: c == j gives the squared norm, c > j the
-// inputs of w, c < j the entries of Y^T Y for T) and one __syncthreads.  The
-// reduction is a warp butterfly that halves the payload each round
-// (8+4+2+1+1 shuffles), then 8 warp partials from shared memory.  After a
-// leaf, its compact-WY block reflector is applied to the remaining panel
-// columns with register-tiled micro-GEMMs on the column-major panel; after the
-// panel, T is assembled from the leaf T's by T_AB = -T_A (Y_A^T Y_B) T_B.
+constexpr int SP = SUB + 4;   // column stride of the panel (column-major; 16-byte aligned columns,
+                              // column c starts at bank 4c mod 32)
 constexpr int PT2 = 256;
 constexpr int NWARP = PT2 / 32;
 constexpr int LEAF = 16;
 constexpr int NLEAF = NB / LEAF;
+constexpr int ZST = 20;       // stride per output column of the block-product partials (bank-conflict free)
+constexpr int LDW = NB;       // row stride of W
 static_assert(SUB == PT2, "the panel maps one row to each thread");
 
+// A column's squared norm may shrink to this fraction of its value at the last
+// Gram evaluation before the Gram matrix is evaluated again from the data.
+constexpr float GRAM_KEEP = 0.5f;
+
+// ---- method --------------------------------------------------------------------
+// 256 threads; thread t owns row t of the sub-tile.  The NB = 64 panel columns
+// are factored in 4 leaves of 16 Householder reflectors (TPQRT: reflector j acts
+// on row j of the R block and on the sub-tile rows).
+//  * Leaf: the Gram matrix M = X_leaf^T X_leaf of the leaf's current columns is
+//    formed once (block product over the 256 rows).  One warp then computes the
+//    16 reflectors in sequence from M and the leaf's R rows: reflector j needs
+//    |x_j|^2 = M[j][j] and the dot products M[j][c]; applying it updates M by a
+//    rank-2 term and row j of R.  No block-wide reduction is needed per column.
+//    If a column's squared norm falls below GRAM_KEEP of its value at the last
+//    evaluation (cancellation in the update), the warp stops, the reflectors so
+//    far are applied to the data and M is evaluated again.  Each thread then
+//    applies the reflectors to its row, which yields Y_leaf.
+//  * Y_leaf^T P[:, 0:nbk] (one block product) gives the leaf's blocks of Y^T Y
+//    and Z = Y_leaf^T P[:, trailing]; W = T_leaf^T (R + Z) by forward
+//    substitution with T^-T = diag(1/tau) + strict_lower(Y^T Y); then
+//    R[leaf rows, trailing] -= W and P[:, trailing] -= Y_leaf W.
+//  * T is assembled from the leaf T's by T_AB = -T_A (Y_A^T Y_B) T_B.
 struct PanelSmem {
   float P[NB * SP];          // X_t[:, panel] -> Y, column-major: element (i, c) at P[c * SP + i]
   float Rk[NB * LDP];        // diagonal block of R
   float G[NB * LDP];         // strict upper part of Y^T Y
   float Tm[NB * LDP];        // T, row-major
-  float Tmp[NB * LDP];       // scratch: inner-update Z, G partial sums, T assembly
-  float Rl[LEAF * (LEAF + 1)];
-  float Wb[LEAF * LDW2];     // W of the inner update (row-major)
-  float part[2][NWARP][LEAF];
+  float Zp[4 * NB * ZST];    // block-product partials [row quarter][column][16]; T assembly scratch
+  float Wb[LEAF * LDW];      // Z, then W, of the leaf update (row-major)
+  float Wr[LEAF * LEAF];     // tau_j w_jc of the leaf's reflectors (row j)
+  float ivv[LEAF];           // 1 / v0_j of the leaf's reflectors
   float tau[NB];
+  int jend;
 };
+static_assert(4 * NB * ZST >= NB * LDP, "T assembly scratch fits the partials block");
 
+// Reflector of xLARFGP form (beta >= 0) for the column (aj; x) with |x|^2 = xn2:
+// H = I - tj v v^T, v = (1; x / v0), v0 = aj - beta formed without cancellation.
+// With u = aj + beta (aj > 0) or u = v0 (aj <= 0), one reciprocal of u depends on
+// beta; 1/xn2 is taken alongside the square root:
+//   aj > 0:  v0 = -xn2 / u, 1/v0 = -u / xn2, tj = -v0 / beta = xn2 / (u beta)
+//   aj <= 0: 1/v0 = 1/u, tj = -u / beta.
 __device__ __forceinline__ void reflector(float aj, float xn2, float& tj, float& beta, float& inv_v0) {
+  const float s = fmaf(aj, aj, xn2);
+  const float rs = rsqrtf(s);
+  const float rx = __fdividef(1.f, xn2);
+  const float nrm = s * rs;
+  const bool pos = aj > 0.f;
+  const float u = pos ? aj + nrm : aj - nrm;
+  const float ru = __fdividef(1.f, u);
   if (xn2 == 0.f) {
     // nothing to annihilate; flip the row if its diagonal is negative
     tj = aj >= 0.f ? 0.f : 2.f;
     beta = fabsf(aj);
     inv_v0 = 0.f;
   } else {
-    const float nrm = __fsqrt_rn(aj * aj + xn2);
-    const float v0 = aj > 0.f ? -xn2 * __frcp_rn(aj + nrm) : aj - nrm;
     beta = nrm;
-    tj = -v0 * __frcp_rn(nrm);
-    inv_v0 = __frcp_rn(v0);
+    tj = pos ? (xn2 * rs) * ru : -u * rs;
+    inv_v0 = pos ? -u * rx : ru;
   }
 }
 
-// Butterfly reduce-scatter of 16 values over a warp: returns the warp total of
-// value index ((lane>>4)&1)*8 + ((lane>>3)&1)*4 + ((lane>>2)&1)*2 + ((lane>>1)&1).
-__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
-  const unsigned F = 0xffffffffu;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const bool hi = lane & 16;
-    const float send = hi ? v[k] : v[k + 8];
-    const float keep = hi ? v[k + 8] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 16);
-  }
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const bool hi = lane & 8;
-    const float send = hi ? v[k] : v[k + 4];
-    const float keep = hi ? v[k + 4] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 8);
-  }
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const bool hi = lane & 4;
-    const float send = hi ? v[k] : v[k + 2];
-    const float keep = hi ? v[k + 2] : v[k];
-    v[k] = keep + __shfl_xor_sync(F, send, 4);
-  }
-  {
-    const bool hi = lane & 2;
-    const float send = hi ? v[0] : v[1];
-    const float keep = hi ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(F, send, 2);
-  }
-  return v[0] + __shfl_xor_sync(F, v[0], 1);
+__device__ __forceinline__ float dot4(const float4 a, const float4 b, float acc) {
+  acc = fmaf(a.x, b.x, acc);
+  acc = fmaf(a.y, b.y, acc);
+  acc = fmaf(a.z, b.z, acc);
+  return fmaf(a.w, b.w, acc);
 }
 
-// dst block (m x n at dr, dc) = (neg ? -1 : 1) * A (m x k at ar, ac) * M (k x n at mr, mc),
+// Block product partials: for the 16 panel columns a0.. and the nb (1..64)
+// columns b0.., Zp[(q * NB + c) * ZST + i] = sum over the rows of quarter q
+// of P[r][a0 + i] * P[r][b0 + c].  Warps w and w + 4 share row quarter w % 4 and
+// split the output columns; lane (i4 = lane & 3, g = lane >> 2) accumulates rows
+// i4 + 4u of A against columns g + 8e of B, so every 16-byte load of a warp
+// touches distinct banks or broadcasts.  E = output-column groups of 8 (even).
+template <int E>
+__device__ __forceinline__ void block_product(PanelSmem& S, int a0, int b0, int nb) {
+  constexpr int EH = E / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int i4 = lane & 3, g = lane >> 2;
+  const int rq = warp & 3, oh = warp >> 2;
+  const float* pa[4];
+  const float* pb[EH];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) pa[u] = S.P + (a0 + i4 + 4 * u) * SP + rq * (SUB / 4);
+#pragma unroll
+  for (int e = 0; e < EH; ++e) {
+    const int c = g + 8 * (oh * EH + e);
+    pb[e] = S.P + (b0 + (c < nb ? c : nb - 1)) * SP + rq * (SUB / 4);
+  }
+  float acc[4][EH];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int e = 0; e < EH; ++e) acc[u][e] = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < SUB / 4; i += 4) {
+    float4 ya[4], pv[EH];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) ya[u] = *reinterpret_cast<const float4*>(pa[u] + i);
+#pragma unroll
+    for (int e = 0; e < EH; ++e) pv[e] = *reinterpret_cast<const float4*>(pb[e] + i);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int e = 0; e < EH; ++e) acc[u][e] = dot4(ya[u], pv[e], acc[u][e]);
+  }
+#pragma unroll
+  for (int e = 0; e < EH; ++e) {
+    const int c = g + 8 * (oh * EH + e);
+    if (c < nb) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) S.Zp[(rq * NB + c) * ZST + i4 + 4 * u] = acc[u][e];
+    }
+  }
+}
+
+// Sum of the four row-quarter partials of output (i, c)
+__device__ __forceinline__ float zsum(const PanelSmem& S, int i, int c) {
+  const float* z = S.Zp + c * ZST + i;
+  return (z[0] + z[NB * ZST]) + (z[2 * NB * ZST] + z[3 * NB * ZST]);
+}
+
+// dst block (M x N at dr, dc) = (NEG ? -1 : 1) * A (M x K at ar, ac) * B (K x N at br, bc),
 // row-major LDP-stride blocks in shared memory; all PT2 threads.  Used for T assembly.
-__device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* A, int ar, int ac,
-                                       const float* M, int mr, int mc, int m, int k, int n, int tid, bool neg) {
-  for (int o = tid; o < m * n; o += PT2) {
-    const int i = o / n, j = o % n;
-    float s = 0.f;
-    for (int l = 0; l < k; ++l) s += A[(ar + i) * LDP + ac + l] * M[(mr + l) * LDP + mc + j];
-    dst[(dr + i) * LDP + dc + j] = neg ? -s : s;
+template <int M, int K, int N, bool NEG>
+__device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* A, int ar, int ac, const float* B,
+                                       int br, int bc, int tid) {
+#pragma unroll
+  for (int o = tid; o < M * N; o += PT2) {
+    const int i = o / N, j = o % N;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int l = 0; l < K; l += 2) {
+      s0 = fmaf(A[(ar + i) * LDP + ac + l], B[(br + l) * LDP + bc + j], s0);
+      s1 = fmaf(A[(ar + i) * LDP + ac + l + 1], B[(br + l + 1) * LDP + bc + j], s1);
+    }
+    dst[(dr + i) * LDP + dc + j] = NEG ? -(s0 + s1) : (s0 + s1);
   }
+}
+
+// Warp 0: reflectors jl .. of the leaf at L0 from the Gram matrix in Zp (columns
+// L0..L0+15 against themselves) and the leaf's R rows in Rk, up to nl or until a
+// column's norm has shrunk past GRAM_KEEP.  Writes the R rows, tau, 1/v0 and
+// tau_j w_jc, and the end of the run to S.jend.
+__device__ __forceinline__ void gram_steps(PanelSmem& S, int L0, int jl, int nl, int nbk) {
+  const unsigned F = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int c = lane & 15;  // lanes 16..31 repeat lanes 0..15
+  float Mc[LEAF], Rc[LEAF];
+#pragma unroll
+  for (int d = 0; d < LEAF; ++d) Mc[d] = zsum(S, c, d);
+#pragma unroll
+  for (int j = 0; j < LEAF; ++j) Rc[j] = S.Rk[(L0 + j) * LDP + L0 + c];
+  float dc = zsum(S, c, c);  // M[c][c], kept by its own recurrence
+  const float m0 = GRAM_KEEP * dc;
+  // Steps run to nl; a step whose update shrank a norm past GRAM_KEEP ends the
+  // run after it (steps computed beyond that point are discarded).
+  unsigned badmask = 0u;
+#pragma unroll
+  for (int j = 0; j < LEAF; ++j) {
+    if (j >= jl && j < nl) {
+      const float xn2 = __shfl_sync(F, Mc[j], j);
+      const float al = __shfl_sync(F, Rc[j], j);
+      float Mj[LEAF];
+#pragma unroll
+      for (int d = j + 1; d < LEAF; ++d) Mj[d] = __shfl_sync(F, Mc[d], j);
+      float tj, beta, iv;
+      reflector(al, xn2, tj, beta, iv);
+      const float w = fmaf(Mc[j], iv, Rc[j]);
+      float wd[LEAF];
+#pragma unroll
+      for (int d = j + 1; d < LEAF; ++d) wd[d] = __shfl_sync(F, w, d);
+      const float p = tj * iv;
+      const float qw = p * p * xn2 * w;
+      const float mcj = Mc[j];
+      // rows of finished columns (c <= j) are dead: update every lane's row
+#pragma unroll
+      for (int d = j + 1; d < LEAF; ++d) Mc[d] = fmaf(qw, wd[d], fmaf(-p, fmaf(w, Mj[d], wd[d] * mcj), Mc[d]));
+      // own diagonal M[c][c] (c > j): -2 p w M[c][j] + p^2 xn2 w^2
+      dc = fmaf(qw, w, fmaf(-2.f * p * w, mcj, dc));
+      Rc[j] = (c == j) ? beta : fmaf(-tj, w, Rc[j]);
+      if (c > j && lane < LEAF) S.Wr[j * LEAF + c] = tj * w;
+      if (lane == j) {
+        S.ivv[j] = iv;
+        S.tau[L0 + j] = tj;
+      }
+      const bool bad = c > j && c < nl && !(dc >= m0);
+      badmask |= __ballot_sync(F, bad) ? (1u << j) : 0u;
+    }
+  }
+  const int jend = badmask ? __ffs(badmask) : nl;  // last good step + 1
+  // rows jl .. jend-1 of the leaf's R block (upper part, columns inside the block)
+  if (lane < LEAF && L0 + c < nbk) {
+#pragma unroll
+    for (int j = 0; j < LEAF; ++j)
+      if (j >= jl && j < jend && j <= c) S.Rk[(L0 + j) * LDP + L0 + c] = Rc[j];
+  }
+  if (lane == 0) S.jend = jend;
 }
 
 // Factor the panel in S.P (SUB x NB fp32, column-major; rows beyond the
@@ -129,220 +263,166 @@ __device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* 
 // tau's.  All PT2 threads call it; it begins and ends with a __syncthreads.
 static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, const int nact) {
   const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-#ifdef IFK_TRACE
-  long long ph_last = ptime();
-#endif
+  const int warp = tid >> 5;
+  PH_DECL
   for (int idx = tid; idx < NB * LDP; idx += PT2) {
     S.G[idx] = 0.f;
     S.Tm[idx] = 0.f;
   }
   if (tid < NB) S.tau[tid] = 0.f;
-  __syncthreads();
   const int r = tid;
-  const int vidx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-  int buf = 0;
+  for (int c = nbk; c < NB; ++c) S.P[c * SP + r] = 0.f;  // columns past the block: zero
+  __syncthreads();
 #pragma unroll 1
   for (int s = 0; s < NLEAF; ++s) {
     const int L0 = s * LEAF;
     if (L0 >= nbk) break;
+    const int nl = nact - L0 < LEAF ? nact - L0 : LEAF;  // reflectors of this leaf (may be <= 0)
     float a[LEAF];
 #pragma unroll
     for (int c = 0; c < LEAF; ++c) a[c] = S.P[(L0 + c) * SP + r];
+    // ---- leaf: Gram runs ----
+    int jl = 0;
+#pragma unroll 1
+    while (jl < nl) {
+      block_product<2>(S, L0, L0, LEAF);
+      __syncthreads();
+      PH_MARK(0);
+      if (warp == 0) gram_steps(S, L0, jl, nl, nbk);
+      __syncthreads();
+      PH_MARK(1);
+      const int jend = S.jend;
+      // apply reflectors jl .. jend-1 to this thread's row
 #pragma unroll
-    for (int jj = 0; jj < LEAF; ++jj) {
-      const int j = L0 + jj;
-      if (j < nact) {
-        float v[LEAF];
+      for (int j = 0; j < LEAF; ++j) {
+        if (j >= jl && j < jend) {
+          const float y = a[j] * S.ivv[j];
+          a[j] = y;
+          const float4* wr = reinterpret_cast<const float4*>(S.Wr + j * LEAF);
 #pragma unroll
-        for (int c = 0; c < LEAF; ++c) v[c] = a[jj] * a[c];
-        const float part = warp_reduce16(v, lane);
-        if ((lane & 1) == 0) S.part[buf][warp][vidx] = part;
-        __syncthreads();
-        float tl = 0.f;
-        if (lane < LEAF) {
-#pragma unroll
-          for (int w = 0; w < NWARP; ++w) tl += S.part[buf][w][lane];
-        }
-        float tot[LEAF];
-#pragma unroll
-        for (int c = 0; c < LEAF; ++c) tot[c] = __shfl_sync(0xffffffffu, tl, c);
-        buf ^= 1;
-        float tj, beta, inv_v0;
-        reflector(S.Rk[j * LDP + j], tot[jj], tj, beta, inv_v0);
-        float wv[LEAF];
-#pragma unroll
-        for (int c = jj + 1; c < LEAF; ++c) {
-          const float rr = S.Rk[j * LDP + L0 + c];
-          wv[c] = rr + tot[c] * inv_v0;
-          if (tid == 0) S.Rl[jj * (LEAF + 1) + c] = rr - tj * wv[c];
-        }
-        if (tid == 0) {
-          S.Rl[jj * (LEAF + 1) + jj] = beta;
-          S.tau[j] = tj;
-#pragma unroll
-          for (int c = 0; c < jj; ++c) S.G[(L0 + c) * LDP + j] = tot[c] * inv_v0;
-        }
-        const float y = a[jj] * inv_v0;
-        a[jj] = y;
-        const float ty = tj * y;
-#pragma unroll
-        for (int c = jj + 1; c < LEAF; ++c) a[c] -= ty * wv[c];
-      } else {
-        // beyond the rank bound: identity reflector, zero Householder vector
-        a[jj] = 0.f;
-        if (tid == 0) {
-#pragma unroll
-          for (int c = jj; c < LEAF; ++c) S.Rl[jj * (LEAF + 1) + c] = S.Rk[j * LDP + L0 + c];
+          for (int c4 = 0; c4 < LEAF / 4; ++c4) {
+            if (4 * c4 + 3 <= j) continue;
+            const float4 t = wr[c4];
+            if (4 * c4 + 0 > j) a[4 * c4 + 0] = fmaf(-y, t.x, a[4 * c4 + 0]);
+            if (4 * c4 + 1 > j) a[4 * c4 + 1] = fmaf(-y, t.y, a[4 * c4 + 1]);
+            if (4 * c4 + 2 > j) a[4 * c4 + 2] = fmaf(-y, t.z, a[4 * c4 + 2]);
+            if (4 * c4 + 3 > j) a[4 * c4 + 3] = fmaf(-y, t.w, a[4 * c4 + 3]);
+          }
         }
       }
+      jl = jend;
+      if (jl < nl) {
+#pragma unroll
+        for (int c = 0; c < LEAF; ++c) S.P[(L0 + c) * SP + r] = a[c];
+      }
+      __syncthreads();  // Wr / ivv / jend are rewritten by the next run
+      PH_MARK(2);
     }
+    // columns beyond the rank bound carry no reflector
 #pragma unroll
-    for (int c = 0; c < LEAF; ++c) S.P[(L0 + c) * SP + r] = a[c];
+    for (int c = 0; c < LEAF; ++c) {
+      if (L0 + c >= nact) a[c] = 0.f;
+      S.P[(L0 + c) * SP + r] = a[c];
+    }
     __syncthreads();
-    PH_MARK(0);
-    // leaf R block back into Rk; leaf T by the column recursion, one row per lane of warp 1
-    if (tid < LEAF) {
+    if (L0 >= nact) continue;  // no reflectors: R rows, T and trailing columns unchanged
+    // ---- Y_leaf^T P[:, 0:nbk]: leaf blocks of Y^T Y and Z ----
+    block_product<8>(S, L0, 0, nbk);
+    __syncthreads();
+    PH_MARK(3);
+    const int C0 = L0 + LEAF;
+    const int wcI = nbk - C0;
+    for (int o = tid; o < LEAF * nbk; o += PT2) {
+      const int i = o & 15, c = o >> 4;
+      const float v = zsum(S, i, c);
+      if (c < L0) S.G[c * LDP + L0 + i] = v;                    // (Y_c-leaf)^T Y_leaf
+      else if (c < C0) { if (c > L0 + i) S.G[(L0 + i) * LDP + c] = v; }  // strict upper of the leaf block
+      else S.Wb[i * LDW + (c - C0)] = v + S.Rk[(L0 + i) * LDP + c];     // Z + R rows
+    }
+    __syncthreads();
+    PH_MARK(4);
+    // W = T_leaf^T Z by forward substitution; leaf T by the column recursion (warp 7)
+    if (tid < wcI) {
+      const int c = tid;
+      float wv[LEAF];
 #pragma unroll
-      for (int c = 0; c < LEAF; ++c)
-        if (c >= tid && L0 + c < nbk) S.Rk[(L0 + tid) * LDP + L0 + c] = S.Rl[tid * (LEAF + 1) + c];
-    } else if (tid >= 32 && tid < 32 + LEAF) {
-      const int i = tid - 32;
+      for (int j = 0; j < LEAF; ++j) {
+        float acc0 = S.Wb[j * LDW + c], acc1 = 0.f;
+#pragma unroll
+        for (int l = 0; l < j; l += 2) {
+          acc0 = fmaf(-S.G[(L0 + l) * LDP + L0 + j], wv[l], acc0);
+          if (l + 1 < j) acc1 = fmaf(-S.G[(L0 + l + 1) * LDP + L0 + j], wv[l + 1], acc1);
+        }
+        wv[j] = S.tau[L0 + j] * (acc0 + acc1);
+      }
+#pragma unroll
+      for (int j = 0; j < LEAF; ++j) {
+        S.Wb[j * LDW + c] = wv[j];
+        S.Rk[(L0 + j) * LDP + C0 + c] -= wv[j];
+      }
+    } else if (tid < ((wcI + 3) & ~3)) {
+#pragma unroll
+      for (int j = 0; j < LEAF; ++j) S.Wb[j * LDW + tid] = 0.f;
+    }
+    if (warp == NWARP - 1 && (tid & 31) < LEAF) {
+      const int i = tid & 31;
       float Tr[LEAF];
 #pragma unroll
       for (int jj = 0; jj < LEAF; ++jj) {
         const float tj = S.tau[L0 + jj];
-        float acc = 0.f;
+        float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-        for (int l = 0; l < jj; ++l) acc += Tr[l] * S.G[(L0 + l) * LDP + L0 + jj];
-        Tr[jj] = (i == jj) ? tj : (i < jj ? -tj * acc : 0.f);
+        for (int l = 0; l < jj; l += 2) {
+          acc0 = fmaf(Tr[l], S.G[(L0 + l) * LDP + L0 + jj], acc0);
+          if (l + 1 < jj) acc1 = fmaf(Tr[l + 1], S.G[(L0 + l + 1) * LDP + L0 + jj], acc1);
+        }
+        Tr[jj] = (i == jj) ? tj : (i < jj ? -tj * (acc0 + acc1) : 0.f);
       }
 #pragma unroll
       for (int jj = 0; jj < LEAF; ++jj) S.Tm[(L0 + i) * LDP + L0 + jj] = Tr[jj];
     }
+    if (wcI <= 0) {
+      __syncthreads();
+      continue;
+    }
     __syncthreads();
-    PH_MARK(1);
-    // apply the leaf's block reflector to the remaining panel columns
-    const int C0 = L0 + LEAF;
-    const int wcI = nbk - C0;
-    if (wcI > 0 && L0 < nact) {
-      // Z = Rk[leaf rows, C] + Y_leaf^T P[:, C] -> Tmp[0..15][C]; 1 x 4 register tiles,
-      // 16-byte loads of 4 consecutive rows of a column
-      const int nq = (wcI + 3) / 4;
-      for (int o = tid; o < LEAF * nq; o += PT2) {
-        const int jj = o / nq, cq = o % nq;
-        const int j0 = L0 + jj, cc0 = C0 + 4 * cq;
-        float z[4] = {};
-        const float* yp = S.P + j0 * SP;
-        const float* pc[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) pc[e] = S.P + (cc0 + e < nbk ? cc0 + e : cc0) * SP;
-#pragma unroll 4
-        for (int i = 0; i < SUB; i += 4) {
-          const float4 ya = *reinterpret_cast<const float4*>(yp + i);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float4 x = *reinterpret_cast<const float4*>(pc[e] + i);
-            z[e] += ya.x * x.x + ya.y * x.y + ya.z * x.z + ya.w * x.w;
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = cc0 + e;
-          if (c < nbk) S.Tmp[jj * LDP + c] = z[e] + S.Rk[j0 * LDP + c];
-        }
-      }
-      __syncthreads();
-      PH_MARK(2);
-      // W = T_leaf^T Z -> Wb (columns relative to C0) ; Rk[leaf rows, C] -= W
-      for (int o = tid; o < LEAF * wcI; o += PT2) {
-        const int jj = o % LEAF, cr = o / LEAF, c = C0 + cr;
-        float w = 0.f;
-#pragma unroll
-        for (int l = 0; l < LEAF; ++l) w += S.Tm[(L0 + l) * LDP + L0 + jj] * S.Tmp[l * LDP + c];
-        S.Wb[jj * LDW2 + cr] = w;
-        S.Rk[(L0 + jj) * LDP + c] -= w;
-      }
-      for (int o = tid; o < LEAF * 4; o += PT2) {  // zero the padding columns of the last quad
-        const int jj = o / 4, cr = wcI + o % 4;
-        if (cr < nq * 4) S.Wb[jj * LDW2 + cr] = 0.f;
-      }
-      __syncthreads();
-      PH_MARK(3);
-      // P[:, C] -= Y_leaf W; this thread's Y_leaf row is still in a[]
+    PH_MARK(5);
+    // P[:, C] -= Y_leaf W; this thread's Y_leaf row is still in a[]
+    const int nq = (wcI + 3) / 4;
 #pragma unroll 1
-      for (int cq = 0; cq < nq; ++cq) {
-        float d[4] = {};
+    for (int cq = 0; cq < nq; ++cq) {
+      float d[4] = {};
 #pragma unroll
-        for (int l = 0; l < LEAF; ++l) {
-          const float4 w = *reinterpret_cast<const float4*>(S.Wb + l * LDW2 + 4 * cq);
-          d[0] += a[l] * w.x; d[1] += a[l] * w.y; d[2] += a[l] * w.z; d[3] += a[l] * w.w;
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = C0 + 4 * cq + e;
-          if (c < nbk) S.P[c * SP + r] -= d[e];
-        }
+      for (int l = 0; l < LEAF; ++l) {
+        const float4 w = *reinterpret_cast<const float4*>(S.Wb + l * LDW + 4 * cq);
+        d[0] = fmaf(a[l], w.x, d[0]);
+        d[1] = fmaf(a[l], w.y, d[1]);
+        d[2] = fmaf(a[l], w.z, d[2]);
+        d[3] = fmaf(a[l], w.w, d[3]);
       }
-      __syncthreads();
-      PH_MARK(4);
-    }
-  }
-
-  // off-diagonal leaf blocks of G = Y^T Y: 6 blocks of 16 x 16 as 96 tiles of 4 x 4;
-  // threads 0..95 sum rows 0..127, threads 128..223 rows 128..255
-  {
-    const int half = tid >> 7, tt = tid & 127;
-    const bool act = tt < 96;
-    const int blk = tt >> 4, tile = tt & 15;
-    const int la = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-    const int lb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-    const int a0c = la * LEAF + 4 * (tile >> 2), b0c = lb * LEAF + 4 * (tile & 3);
-    float g[4][4] = {};
-    if (act) {
-#pragma unroll 2
-      for (int i = half * (SUB / 2); i < (half + 1) * (SUB / 2); i += 4) {
-        float4 ya[4], yb[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          ya[e] = *reinterpret_cast<const float4*>(S.P + (a0c + e) * SP + i);
-          yb[e] = *reinterpret_cast<const float4*>(S.P + (b0c + e) * SP + i);
-        }
-#pragma unroll
-        for (int p = 0; p < 4; ++p)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            g[p][q] += ya[p].x * yb[q].x + ya[p].y * yb[q].y + ya[p].z * yb[q].z + ya[p].w * yb[q].w;
-      }
-      if (half == 1) {
-#pragma unroll
-        for (int p = 0; p < 4; ++p)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) S.Tmp[tt * 16 + p * 4 + q] = g[p][q];
+      for (int e = 0; e < 4; ++e) {
+        const int c = C0 + 4 * cq + e;
+        if (c < nbk) S.P[c * SP + r] -= d[e];
       }
     }
     __syncthreads();
-    if (act && half == 0) {
-#pragma unroll
-      for (int p = 0; p < 4; ++p)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) S.G[(a0c + p) * LDP + b0c + q] = g[p][q] + S.Tmp[tt * 16 + p * 4 + q];
-    }
+    PH_MARK(6);
   }
-  __syncthreads();
-  PH_MARK(5);
   // T assembly: T_{01} = -T_0 G_{01} T_1, T_{23} likewise, then the 32 x 32 coupling
-  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, 16, 16, 16, tid, false);     // T0 G01
-  matmul(S.Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, 16, 16, 16, tid, false); // T2 G23
+  float* Tmp = S.Zp;
+  matmul<16, 16, 16, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, tid);     // T0 G01
+  matmul<16, 16, 16, false>(Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, tid); // T2 G23
   __syncthreads();
-  matmul(S.Tm, 0, 16, S.Tmp, 0, 0, S.Tm, 16, 16, 16, 16, 16, tid, true);    // T01
-  matmul(S.Tm, 32, 48, S.Tmp, 16, 32, S.Tm, 48, 48, 16, 16, 16, tid, true); // T23
+  matmul<16, 16, 16, true>(S.Tm, 0, 16, Tmp, 0, 0, S.Tm, 16, 16, tid);    // T01
+  matmul<16, 16, 16, true>(S.Tm, 32, 48, Tmp, 16, 32, S.Tm, 48, 48, tid); // T23
   __syncthreads();
-  matmul(S.Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, 32, 32, 32, tid, false);   // T_A G_AB (32 x 32)
+  matmul<32, 32, 32, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, tid);      // T_A G_AB (32 x 32)
   __syncthreads();
-  matmul(S.Tm, 0, 32, S.Tmp, 0, 0, S.Tm, 32, 32, 32, 32, 32, tid, true);  // T_AB
+  matmul<32, 32, 32, true>(S.Tm, 0, 32, Tmp, 0, 0, S.Tm, 32, 32, tid);    // T_AB
   __syncthreads();
-  PH_MARK(6);
+  PH_MARK(7);
+  PH_FLUSH()
 }
 
 }  // namespace panel
