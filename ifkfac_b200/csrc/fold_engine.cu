@@ -7,8 +7,8 @@
 //   COL(f, t, cb) applies panel k < 2cb of sub-tile t once that panel is
 //   published by COL(f, t, k/2) and COL(f, t-1, cb) has applied its own panel
 //   k (the R rows of panel k in block cb are then final for sub-tile t-1: a
-//   progress counter per task), and factors its own panels once COL(f, t-1, cb)
-//   is done.  Sub-tile t so trails sub-tile t-1 by one apply.
+//   progress counter per task), and factors its own panels as COL(f, t-1, cb)
+//   finishes the same R rows.  Sub-tile t so trails sub-tile t-1 by one step.
 // A task only waits for lower tickets, which were handed to CTAs already
 // running, so the schedule cannot deadlock; every wait is bounded anyway and
 // reports IFK_ERR_TIMEOUT.
@@ -103,8 +103,7 @@ struct PFold {
   float ident;  // diagonal value when xkind == XK_IDENT
   int64_t n, rows, rows_R;
   int T, K, CB, tri;
-  int* done;     // [T][CB]
-  int* prog;     // [T][CB]: panels k < prog applied to the block's R rows
+  int* prog;     // [T][CB]: k < K: panels < k applied to the block's R rows; K + s: own-panel stage s
   int* pflag;    // [T][K]
   uint8_t* img;  // [T][K][PIMG]
 };
@@ -393,13 +392,11 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   const int wc = (int)mn<int64_t>(WB, F.n - cs);
   const int64_t lim = mn<int64_t>(F.n, F.rows_R + row0 + h);
   const int kfirst = F.tri ? (int)(row0 / NB) : 0;
-  int* done = F.done + (size_t)t * F.CB + cb;
   int* prog = F.prog + (size_t)t * F.CB + cb;
   const int* prev_prog = t > 0 ? F.prog + (size_t)(t - 1) * F.CB + cb : nullptr;
 
   if (F.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
-    cta_publish_value(prog, F.K);
-    cta_publish(done);
+    cta_publish_value(prog, F.K + 3);
     return;
   }
   TR_SET(4, TR_NOW());
@@ -459,17 +456,26 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   // panels this sub-tile does not reach leave their R rows as they are
   cta_publish_value(prog, F.K);
 
-  // ---- factor the block's own panels: R diagonal blocks final for sub-tile t-1 ----
-  if (t > 0 && !cta_wait_flag(F.done + (size_t)(t - 1) * F.CB + cb, b, s_ok)) return;
+  // ---- factor the block's own panels ----
+  // Stages of this phase, published in prog and awaited from COL(t-1, cb):
+  //   K + 1: R diagonal block of panel 2cb written; K + 2: panel 2cb applied to
+  //   the block's second half (R rows of panel 2cb final); K + 3: R diagonal
+  //   block of panel 2cb + 1 written.  A panel this sub-tile skips (beyond its
+  //   rank bound, or left of its diagonal in a trapezoidal fold) is skipped by
+  //   every earlier sub-tile too, or by every later one, so its stage passes at once.
   TR_SET(6, TR_NOW());
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
 #pragma unroll 1
   for (int q = 0; q < 2; ++q) {
     const int kk = 2 * cb + q;
     const int64_t c0 = (int64_t)kk * NB;
-    if (kk >= F.K || c0 >= lim || kk < kfirst) continue;
+    if (kk >= F.K || c0 >= lim || kk < kfirst) {
+      cta_publish_value(prog, F.K + 1 + 2 * q);
+      continue;
+    }
     const int nbk = (int)mn<int64_t>(NB, F.n - c0);
     const int nact = (int)mn<int64_t>(nbk, lim - c0);
+    if (t > 0 && !cta_wait_ge(prev_prog, F.K + 1 + 2 * q, b, s_ok)) return;
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -518,22 +524,26 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       const int i = idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) F.R[(c0 + i) * F.ldR + c0 + j] = S.Rk[i * LDP + j];
     }
-    __syncthreads();
+    cta_publish_value(prog, F.K + 1 + 2 * q);
     {
       uint4* dst = reinterpret_cast<uint4*>(F.img + ((size_t)t * F.K + kk) * PIMG);
       const uint4* srcs = reinterpret_cast<const uint4*>(c.sm + OFF_Y);
       for (int i = tid; i < (int)(PIMG / 16); i += TPB) dst[i] = srcs[i];
     }
     cta_publish(F.pflag + (size_t)t * F.K + kk);
-    if (q == 0 && wc > NB) {
-      // the first panel also acts on the block's second half
-      refresh_a1(c);
-      sync_for_mma();
-      apply_panel(c, F, c0, nbk, cs, wc, true);
+    if (q == 0) {
+      if (wc > NB) {
+        // the first panel also acts on the block's second half
+        if (t > 0 && !cta_wait_ge(prev_prog, F.K + 2, b, s_ok)) return;
+        refresh_a1(c);
+        sync_for_mma();
+        apply_panel(c, F, c0, nbk, cs, wc, true);
+      }
+      cta_publish_value(prog, F.K + 2);
     }
   }
   tc::fence_before();
-  cta_publish(done);
+  cta_publish_value(prog, F.K + 3);
   TR_SET(7, TR_NOW());
   TR_FLUSH();
 }
@@ -651,7 +661,7 @@ size_t pfold_workspace(int nf, const PFoldDesc* d) {
   for (int f = 0; f < nf; ++f) {
     if (d[f].rows <= 0) continue;
     const int64_t T = cdiv(d[f].rows, SUB), K = cdiv(d[f].n, NB), CB = cdiv(d[f].n, WB);
-    b += 2 * align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
+    b += align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
   }
   return b;
 }
@@ -693,8 +703,6 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
       F.CB = (int)cdiv(F.n, WB);
       F.tri = D.tri;
       if (F.T + F.CB - 1 > MAXW) return IFK_ERR_SHAPE;  // callers split chunks (pfold_max_rows)
-      F.done = (int*)w;
-      w += align256((size_t)F.T * F.CB * 4);
       F.prog = (int*)w;
       w += align256((size_t)F.T * F.CB * 4);
       F.pflag = (int*)w;
