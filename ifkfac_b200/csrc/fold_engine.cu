@@ -300,22 +300,24 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
     }
     tc::commit(c.bar);
   }
-  mma_wait(c);
+  // this thread's 32 R entries, read once while GEMM1 runs
   const bool rcol = col < wc && !(skip_half0 && col < NB);
+  float rr[32];
   {
-    const int half = jh;
+    const float* rp = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) rr[e] = (jh * 32 + e < nbk && col < wc) ? rp[(int64_t)e * F.ldR] : 0.f;
+  }
+  mma_wait(c);
+  {
     float w[32];
-    tc::tmem_ld32(lane_base + TM_D1 + half * 32, w);
+    tc::tmem_ld32(lane_base + TM_D1 + jh * 32, w);
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       float hi[8], lo[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = half * 32 + g * 8 + e;
-        const float r = (j < nbk && col < wc) ? F.R[(k0 + j) * F.ldR + cs + col] : 0.f;
-        tc::split_bf16(w[g * 8 + e] + r, hi[e], lo[e]);
-      }
-      const uint32_t off = tc::cm_off<true>(col, half * 32 + g * 8, A2_MN, A2_K);
+      for (int e = 0; e < 8; ++e) tc::split_bf16(w[g * 8 + e] + rr[g * 8 + e], hi[e], lo[e]);
+      const uint32_t off = tc::cm_off<true>(col, jh * 32 + g * 8, A2_MN, A2_K);
       store8(c.sb + OFF_A2H + off, hi);
       store8(c.sb + OFF_A2L + off, lo);
     }
@@ -337,19 +339,19 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
   }
   mma_wait(c);
   {
-    const int half = jh;
     float w[32];
-    tc::tmem_ld32(lane_base + TM_D2 + half * 32, w);
+    tc::tmem_ld32(lane_base + TM_D2 + jh * 32, w);
+    float* rp = F.R + (k0 + jh * 32) * F.ldR + cs + col;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       float v[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int j = half * 32 + g * 8 + e;
-        v[e] = w[g * 8 + e];
-        if (j < nbk && rcol) F.R[(k0 + j) * F.ldR + cs + col] -= v[e];
+        const int j = g * 8 + e;
+        v[e] = w[j];
+        if (jh * 32 + j < nbk && rcol) rp[(int64_t)j * F.ldR] = rr[j] - v[e];
       }
-      store8(c.sb + OFF_B3 + tc::cm_off<true>(col, half * 32 + g * 8, A2_MN, A2_K), v);
+      store8(c.sb + OFF_B3 + tc::cm_off<true>(col, jh * 32 + g * 8, A2_MN, A2_K), v);
     }
   }
   sync_for_mma();
@@ -476,6 +478,9 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     const int nbk = (int)mn<int64_t>(NB, F.n - c0);
     const int nact = (int)mn<int64_t>(nbk, lim - c0);
     if (t > 0 && !cta_wait_ge(prev_prog, F.K + 1 + 2 * q, b, s_ok)) return;
+#ifdef IFK_TRACE
+    const long long l0 = TR_NOW();
+#endif
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -499,13 +504,18 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     __syncthreads();
 #ifdef IFK_TRACE
     const long long p0 = TR_NOW();
+    TR_ADD(8, p0 - l0);
 #endif
     panel::panel_factor(S, nbk, nact);
-    TR_ADD(11, TR_NOW() - p0);
+#ifdef IFK_TRACE
+    const long long p1 = TR_NOW();
+    TR_ADD(11, p1 - p0);
+#endif
     TR_ADD(12, 1);
-    // Y image (bf16, K-major for GEMM3 / MN-major for GEMM1) and T hi / lo images
+    // Y image (bf16, K-major for GEMM3 / MN-major for GEMM1) and T hi / lo images;
+    // lanes take consecutive rows, so the column reads of P are conflict-free
     for (int it = tid; it < SUB * (NB / 8); it += TPB) {
-      const int i = it >> 3, j8 = it & 7;
+      const int i = it % SUB, j8 = it / SUB;
       float e8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) e8[e] = S.P[(j8 * 8 + e) * panel::SP + i];
@@ -524,14 +534,24 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       const int i = idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) F.R[(c0 + i) * F.ldR + c0 + j] = S.Rk[i * LDP + j];
     }
-    cta_publish_value(prog, F.K + 1 + 2 * q);
+    __syncthreads();
     {
       uint4* dst = reinterpret_cast<uint4*>(F.img + ((size_t)t * F.K + kk) * PIMG);
       const uint4* srcs = reinterpret_cast<const uint4*>(c.sm + OFF_Y);
       for (int i = tid; i < (int)(PIMG / 16); i += TPB) dst[i] = srcs[i];
     }
-    cta_publish(F.pflag + (size_t)t * F.K + kk);
+    // one fence publishes both the R diagonal block (stage) and the panel images
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      st_release(prog, F.K + 1 + 2 * q);
+      st_release(F.pflag + (size_t)t * F.K + kk, 1);
+    }
+    TR_ADD(13, TR_NOW() - p1);
     if (q == 0) {
+#ifdef IFK_TRACE
+      const long long h0 = TR_NOW();
+#endif
       if (wc > NB) {
         // the first panel also acts on the block's second half
         if (t > 0 && !cta_wait_ge(prev_prog, F.K + 2, b, s_ok)) return;
@@ -540,6 +560,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
         apply_panel(c, F, c0, nbk, cs, wc, true);
       }
       cta_publish_value(prog, F.K + 2);
+      TR_ADD(14, TR_NOW() - h0);
     }
   }
   tc::fence_before();
