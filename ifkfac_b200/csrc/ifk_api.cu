@@ -340,9 +340,18 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
   return IFK_OK;
 }
 
+// Workspace of the persistent bf16 solves: inverses of R_G | inverses of R_X |
+// scratch of the larger solve (the left solves are n_out x n_out against n_in
+// right-hand sides, the right ones the reverse).
+static size_t natgrad_persist_bytes(int64_t n_out, int64_t n_in) {
+  return align_up(trsm_persist_inverse_bytes(n_out)) + align_up(trsm_persist_inverse_bytes(n_in)) +
+         align_up(std::max(trsm_persist_workspace(n_out, n_in), trsm_persist_workspace(n_in, n_out)));
+}
+
 size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {
   if (n_out <= 0 || n_in <= 0) return 0;
-  return align_up(std::max(trsm_tc_workspace(n_out), trsm_tc_workspace(n_in)));
+  return align_up(std::max(std::max(trsm_tc_workspace(n_out), trsm_tc_workspace(n_in)),
+                           natgrad_persist_bytes(n_out, n_in)));
 }
 
 int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
@@ -364,6 +373,24 @@ int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_r
                                    n_in * sizeof(float), n_out, cudaMemcpyDeviceToDevice, s));
   }
   int rc;
+  if (prec == IFK_PREC_BF16 && r_dtype == IFK_BF16 && trsm_persist_ok(R_G, ld_rg, n_out) &&
+      trsm_persist_ok(R_X, ld_rx, n_in)) {
+    // persistent tensor-core solves; the diagonal-block inverses of both factors in one launch
+    const __nv_bfloat16* rg = (const __nv_bfloat16*)R_G;
+    const __nv_bfloat16* rx = (const __nv_bfloat16*)R_X;
+    uint8_t* inv_g = (uint8_t*)workspace;
+    uint8_t* inv_x = inv_g + align_up(trsm_persist_inverse_bytes(n_out));
+    uint8_t* scratch = inv_x + align_up(trsm_persist_inverse_bytes(n_in));
+    rc = trsm_persist_prepare(rg, ld_rg, n_out, inv_g, rx, ld_rx, n_in, inv_x, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_run(rg, ld_rg, 1, nat, ld_nat, 1, n_out, n_in, inv_g, scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_run(rg, ld_rg, 0, nat, ld_nat, 1, n_out, n_in, inv_g, scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_run(rx, ld_rx, 1, nat, 1, ld_nat, n_in, n_out, inv_x, scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    return trsm_persist_run(rx, ld_rx, 0, nat, 1, ld_nat, n_in, n_out, inv_x, scratch, d_status, s);
+  }
   // left: R_G^T T1 = g ; R_G T2 = T1   (columns of nat are independent right-hand sides)
   rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s);
   if (rc != IFK_OK) return rc;

@@ -69,11 +69,23 @@ int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t
 // In-place triangular solve op(A) X = B on a strided view of B (n x N).
 // A is an n x n upper-triangular factor (fp32 or bf16); trans != 0 solves
 // with A^T (lower, forward order), trans == 0 with A (upper, backward).
-// ws: trsm_tc_workspace(n) bytes for the tensor-core path (inverses of the
-// diagonal blocks); err: device status word for bounded-wait timeouts.
+// ws: trsm_tc_workspace(n) bytes for the tensor-core path (one launch per block
+// row; inverses of the diagonal blocks); err: device status word for
+// bounded-wait timeouts.
 int trsm_run(const void* A, int64_t ldA, int a_dtype, int trans, float* B, int64_t rs,
              int64_t cs, int64_t n, int64_t N, int prec, void* ws, int* err, cudaStream_t s);
 size_t trsm_tc_workspace(int64_t n);
+// Persistent tensor-core solve (bf16 A that 16-byte copies can address: trsm_persist_ok).
+// trsm_persist_prepare writes the diagonal-block inverses of one or two factors
+// (trsm_persist_inverse_bytes(n) each, both operand layouts) in one launch;
+// trsm_persist_run then needs trsm_persist_workspace(n, N) bytes of scratch.
+bool trsm_persist_ok(const void* A, int64_t ldA, int64_t n);
+size_t trsm_persist_inverse_bytes(int64_t n);
+size_t trsm_persist_workspace(int64_t n, int64_t N);
+int trsm_persist_prepare(const __nv_bfloat16* A0, int64_t ld0, int64_t n0, void* inv0, const __nv_bfloat16* A1,
+                         int64_t ld1, int64_t n1, void* inv1, cudaStream_t s);
+int trsm_persist_run(const __nv_bfloat16* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t cs,
+                     int64_t n, int64_t N, const void* inv, void* ws, int* err, cudaStream_t s);
 
 int update_run(float* W, float* buf, const float* nat, int64_t count, double lr, double mom,
                double wd, double clip, int buf_is_new, double* norm_ws, cudaStream_t s);

@@ -1,0 +1,441 @@
+// Persistent tensor-core triangular solve, op(A) X = B in place (bf16 A).
+//
+// Right-hand-side columns are independent, so each CTA owns NT = 32 columns of
+// B and solves every block row (NB2 = 128 rows) for them in one launch, with no
+// synchronisation between CTAs.  Block row j (left-looking):
+//   D   = sum_{s solved} op(A)_{j,s} X_s        tcgen05, bf16 operands, fp32 TMEM
+//   Y   = B_j - D                               fp32
+//   X_j = inv(op(A)_{j,j}) Y                    tcgen05, 3-term bf16 split
+// Warp roles (192 threads):
+//   warps 0-3  epilogue: TMEM lanes 32w..32w+31 = rows of the block; Y, X_j, writes
+//   warp 4     producer: bulk copies (contiguous 32 KB / 8 KB images) of the
+//              packed op(A)_{j,s} tile, of this CTA's bf16 copy of X_s and of the
+//              inverses
+// Before the solve, pack_tiles_kernel writes every strictly upper 128 x 128
+// block of A once as the shared-memory image of the operand tile it becomes
+// (K-major for op = A, MN-major transposed for op = A^T), so every copy of the
+// K loop is one contiguous bulk transfer.
+//   warp 5     MMA issue
+// A three-stage full/empty mbarrier ring feeds the K loop; D is double-buffered
+// in TMEM so the next block row's products start while this row's epilogue runs.
+// The inverses inv(A_jj) (fp32 column substitution, 3-term bf16 split) are
+// written by diag_inverse_layout_kernel directly in the operand layout.
+// Every wait is bounded: a role that gives up raises the CTA's abort word, the
+// others stop at their next wait, and the launch reports IFK_ERR_TIMEOUT.
+#include "ifk_common.cuh"
+#include "ifk_internal.h"
+#include "tc.cuh"
+
+namespace ifk {
+
+namespace {
+
+constexpr int NB2 = 128;  // diagonal block
+constexpr int NT = 32;    // right-hand-side columns per CTA
+constexpr int NSTAGE = 3;
+constexpr int TPB = 192;
+
+constexpr uint32_t SZ_A = NB2 * NB2 * 2;  // 32 KB
+constexpr uint32_t SZ_X = NB2 * NT * 2;   // 8 KB
+constexpr uint32_t SZ_STAGE = SZ_A + SZ_X;
+constexpr uint32_t OFF_IH = NSTAGE * SZ_STAGE;
+constexpr uint32_t OFF_IL = OFF_IH + SZ_A;
+constexpr uint32_t OFF_YH = OFF_IL + SZ_A;
+constexpr uint32_t OFF_YL = OFF_YH + SZ_X;
+constexpr uint32_t OFF_BAR = OFF_YL + SZ_X;
+// barriers (8 bytes each): full[3], empty[3], inv_full, inv_empty, dfull, yready, xfull, xready
+enum { B_FULL = 0, B_EMPTY = NSTAGE, B_INVF = 2 * NSTAGE, B_INVE, B_DFULL, B_YRDY, B_XFULL, B_XRDY, B_COUNT };
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * B_COUNT;  // TMEM slot, abort word
+constexpr uint32_t SMEM = OFF_MISC + 16;
+static_assert(SZ_STAGE % 1024 == 0, "TMA destinations stay 1024-byte aligned");
+
+constexpr uint32_t A_MN = 128, A_K = (NB2 / 8) * 128;  // A tiles: core matrices 128 B apart along MN
+constexpr uint32_t X_N = 128, X_K = (NT / 8) * 128;    // X / Y tiles (MN-major)
+constexpr uint32_t TM_D0 = 0, TM_D1 = NT, TM_X = 2 * NT, TM_COLS = 128;
+constexpr size_t INV_SMEM = 2 * sizeof(float) * NB2 * (NB2 + 1);
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+__device__ __forceinline__ uint32_t bar_addr(uint32_t sb, int i) { return sb + OFF_BAR + 8u * (uint32_t)i; }
+
+__device__ __forceinline__ void arrive_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void commit_to(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+// Bounded wait on a barrier phase that also gives up once another role aborted.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_) {
+  for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255) == 255 && *abort_) return false;
+  }
+  *abort_ = 1;
+  return false;
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void st16(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  return make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]), tc::pack_bf16(v[4], v[5]),
+                    tc::pack_bf16(v[6], v[7]));
+}
+
+// Strictly upper block (a, b), a < b, of A as the image of an operand tile:
+// op = A: tile op(A)_{a,b} = A_ab, K-major (mn = row, k = column);
+// op = A^T: tile op(A)_{b,a} = A_ab^T, MN-major (mn = column, k = row).
+// Tile index b (b - 1) / 2 + a; one CTA per tile, staged through shared memory
+// so both the reads of A and the writes of the image are contiguous.
+__global__ void __launch_bounds__(256) pack_tiles_kernel(const __nv_bfloat16* A, int64_t ldA_, int64_t n, int trans,
+                                                         uint8_t* tiles) {
+  extern __shared__ __align__(16) uint8_t img[];
+  const int t = blockIdx.x;
+  int b = (int)((1.0 + sqrt(1.0 + 8.0 * t)) * 0.5);
+  while (b * (b - 1) / 2 > t) --b;
+  while ((b + 1) * b / 2 <= t) ++b;
+  const int a = t - b * (b - 1) / 2;
+  const int64_t a0 = (int64_t)a * NB2, b0 = (int64_t)b * NB2;
+  for (int it = threadIdx.x; it < NB2 * (NB2 / 8); it += 256) {
+    const int i = it >> 4, c = it & 15;  // row i of the block, 16-byte chunk c (columns 8c .. 8c + 7)
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (a0 + i < n && b0 + 8 * c < n) v = *reinterpret_cast<const uint4*>(A + (a0 + i) * ldA_ + b0 + 8 * c);
+    const uint32_t off = trans ? (uint32_t)(i >> 3) * A_K + (uint32_t)c * A_MN + (uint32_t)(i & 7) * 16u
+                               : (uint32_t)c * A_K + (uint32_t)(i >> 3) * A_MN + (uint32_t)(i & 7) * 16u;
+    *reinterpret_cast<uint4*>(img + off) = v;
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(tiles + (size_t)t * SZ_A);
+  for (int it = threadIdx.x; it < (int)(SZ_A / 16); it += 256) dst[it] = reinterpret_cast<const uint4*>(img)[it];
+}
+
+// inv(A_bb) of the upper-triangular diagonal blocks (fp32 column substitution),
+// written as bf16 hi / lo in both operand layouts: the K-major tile of inv(A_bb)
+// (op = A) and the MN-major tile of its transpose (op = A^T).  Block b of matrix
+// m in [hi K, lo K, hi MN, lo MN] order (SZ_A each) at inv_m + b * 4 * SZ_A.
+// One launch covers two matrices: blocks [0, nblk0) of A0, then those of A1.
+// Ragged last block: identity pad.
+__global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __nv_bfloat16* A0, int64_t ld0, int64_t n0,
+                                                                  uint8_t* inv0, const __nv_bfloat16* A1,
+                                                                  int64_t ld1, int64_t n1, uint8_t* inv1) {
+  extern __shared__ float dsm[];
+  float (*U)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm);
+  float (*Xs)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm + NB2 * (NB2 + 1));
+  const int nblk0 = (int)cdiv(n0, NB2);
+  const bool second = (int)blockIdx.x >= nblk0;
+  const __nv_bfloat16* A = second ? A1 : A0;
+  const int64_t ldA_ = second ? ld1 : ld0, n = second ? n1 : n0;
+  const int b = second ? (int)blockIdx.x - nblk0 : (int)blockIdx.x, q = threadIdx.x;
+  const int64_t b0 = (int64_t)b * NB2;
+  const int nb = (int)mn<int64_t>(NB2, n - b0);
+  for (int idx = q; idx < NB2 * NB2; idx += NB2) {
+    const int r = idx / NB2, l = idx % NB2;
+    float v = (r == l) ? 1.f : 0.f;
+    if (r < nb && l < nb) v = (l >= r) ? __bfloat162float(A[(b0 + r) * ldA_ + b0 + l]) : 0.f;
+    U[r][l] = v;
+  }
+  __syncthreads();
+  // column q of U^-1 by back substitution; four partial sums break the FMA chain
+  for (int r = NB2 - 1; r >= 0; --r) {
+    float s0 = (r == q) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int l = r + 1;
+    for (; l + 3 < NB2; l += 4) {
+      s0 -= U[r][l] * Xs[l][q];
+      s1 -= U[r][l + 1] * Xs[l + 1][q];
+      s2 -= U[r][l + 2] * Xs[l + 2][q];
+      s3 -= U[r][l + 3] * Xs[l + 3][q];
+    }
+    for (; l < NB2; ++l) s0 -= U[r][l] * Xs[l][q];
+    Xs[r][q] = ((s0 + s1) + (s2 + s3)) / U[r][r];
+  }
+  __syncthreads();
+  uint8_t* o = (second ? inv1 : inv0) + (size_t)b * 4 * SZ_A;
+  for (int it = q; it < NB2 * (NB2 / 8); it += NB2) {
+    // K-major: 8 consecutive k = l of row m; MN-major (transpose): 8 consecutive mn = l of k = m
+    const int m = it >> 4, l8 = it & 15;
+    float hi[8], lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tc::split_bf16(Xs[m][l8 * 8 + e], hi[e], lo[e]);
+    const uint32_t offk = (uint32_t)l8 * A_K + (uint32_t)(m >> 3) * A_MN + (uint32_t)(m & 7) * 16u;
+    const uint32_t offm = (uint32_t)(m >> 3) * A_K + (uint32_t)l8 * A_MN + (uint32_t)(m & 7) * 16u;
+    const uint4 vh = pack8(hi), vl = pack8(lo);
+    *reinterpret_cast<uint4*>(o + offk) = vh;
+    *reinterpret_cast<uint4*>(o + SZ_A + offk) = vl;
+    *reinterpret_cast<uint4*>(o + 2 * SZ_A + offm) = vh;
+    *reinterpret_cast<uint4*>(o + 3 * SZ_A + offm) = vl;
+  }
+}
+
+__global__ void __launch_bounds__(TPB, 1) trsm_persist_kernel(const uint8_t* tiles, int trans,
+                                                             float* B, int64_t rs, int64_t cs, int64_t n,
+                                                             int64_t N, const __nv_bfloat16* inv,
+                                                             __nv_bfloat16* xws, int* err, int vb) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const uint32_t sb = tc::smem_u32(sm);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
+  volatile int* abort_ = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nblk = (int)cdiv(n, NB2);
+  const int64_t c0 = (int64_t)blockIdx.x * NT;
+  const int nc = (int)mn<int64_t>(NT, N - c0);
+  // this CTA's bf16 copies of its solved blocks: nblk tiles of 8 KB (MN-major B operand)
+  uint8_t* xmine = reinterpret_cast<uint8_t*>(xws) + (size_t)blockIdx.x * nblk * SZ_X;
+
+  if (warp == 0) tc::tmem_alloc(tslot, TM_COLS);
+  if (tid == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_FULL + i, 1);
+      tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_EMPTY + i, 1);
+    }
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_INVF, 1);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_INVE, 1);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_DFULL, 1);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_YRDY, 4);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_XFULL, 1);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(sm + OFF_BAR) + B_XRDY, 4);
+    *abort_ = 0;
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tm = *tslot;
+
+  if (warp == 4) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int row = 0; row < nblk && ok; ++row) {
+        const int jb = trans ? row : nblk - 1 - row;
+        for (int i = 0; i < row && ok; ++i) {
+          // solved blocks, most recent last: forward s = 0.., backward s = nblk-1 ..
+          const int s = trans ? i : nblk - 1 - i;
+          if (i == row - 1) ok = wait_phase(bar_addr(sb, B_XRDY), (row - 1) & 1, abort_);
+          const int st = (int)(g % NSTAGE);
+          if (ok && g >= NSTAGE) ok = wait_phase(bar_addr(sb, B_EMPTY + st), ((g / NSTAGE) - 1) & 1, abort_);
+          if (!ok) break;
+          const uint32_t full = bar_addr(sb, B_FULL + st);
+          const uint32_t dst = sb + (uint32_t)st * SZ_STAGE;
+          arrive_expect(full, SZ_STAGE);
+          // op(A)_{j,s} is the packed image of A block (min, max) of (j, s)
+          const int ta = jb < s ? jb : s, tb = jb < s ? s : jb;
+          bulk_load(dst, tiles + (size_t)(tb * (tb - 1) / 2 + ta) * SZ_A, SZ_A, full);
+          bulk_load(dst + SZ_A, xmine + (size_t)s * SZ_X, SZ_X, full);
+          ++g;
+        }
+        if (!ok) break;
+        if (row > 0) ok = wait_phase(bar_addr(sb, B_INVE), (row - 1) & 1, abort_);
+        if (!ok) break;
+        const uint32_t invf = bar_addr(sb, B_INVF);
+        arrive_expect(invf, 2 * SZ_A);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(inv) + (size_t)jb * 4 * SZ_A + (trans ? 2 * SZ_A : 0);
+        bulk_load(sb + OFF_IH, src, SZ_A, invf);
+        bulk_load(sb + OFF_IL, src + SZ_A, SZ_A, invf);
+      }
+      // every copy issued was consumed by the MMA warp unless a wait gave up
+      if (!ok) {
+        for (uint32_t q = g > NSTAGE ? g - NSTAGE : 0; q < g; ++q)
+          wait_phase(bar_addr(sb, B_FULL + (int)(q % NSTAGE)), (q / NSTAGE) & 1, abort_);
+        if (err) atomicExch(err, IFK_ERR_TIMEOUT);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issue ----------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      const uint32_t idK = tc::idesc_bf16(128, NT, trans != 0, true);
+      const uint32_t idI = tc::idesc_bf16(128, NT, trans != 0, true);
+      for (int row = 0; row < nblk && ok; ++row) {
+        const uint32_t dbuf = (row & 1) ? TM_D1 : TM_D0;
+        for (int i = 0; i < row && ok; ++i) {
+          const int st = (int)(g % NSTAGE);
+          ok = wait_phase(bar_addr(sb, B_FULL + st), (g / NSTAGE) & 1, abort_);
+          if (!ok) break;
+          tc::fence_after();
+          const uint32_t a0 = sb + (uint32_t)st * SZ_STAGE, x0 = a0 + SZ_A;
+#pragma unroll 1
+          for (int k = 0; k < NB2 / 16; ++k) {
+            const uint64_t ad = tc::sdesc(a0 + k * 2 * A_K, A_K, A_MN);
+            const uint64_t bd = tc::sdesc(x0 + k * 2 * X_K, X_K, X_N);
+            tc::mma_bf16(tm + dbuf, ad, bd, idK, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          commit_to(bar_addr(sb, B_EMPTY + st));
+          ++g;
+        }
+        if (!ok) break;
+        commit_to(bar_addr(sb, B_DFULL));
+        ok = wait_phase(bar_addr(sb, B_YRDY), row & 1, abort_) && wait_phase(bar_addr(sb, B_INVF), row & 1, abort_);
+        if (!ok) break;
+        tc::fence_after();
+#pragma unroll 1
+        for (int k = 0; k < NB2 / 16; ++k) {
+          const uint64_t ah = tc::sdesc(sb + OFF_IH + k * 2 * A_K, A_K, A_MN);
+          const uint64_t al = tc::sdesc(sb + OFF_IL + k * 2 * A_K, A_K, A_MN);
+          const uint64_t bh = tc::sdesc(sb + OFF_YH + k * 2 * X_K, X_K, X_N);
+          const uint64_t bl = tc::sdesc(sb + OFF_YL + k * 2 * X_K, X_K, X_N);
+          tc::mma_bf16(tm + TM_X, ah, bh, idI, k > 0);
+          tc::mma_bf16(tm + TM_X, ah, bl, idI, 1);
+          tc::mma_bf16(tm + TM_X, al, bh, idI, 1);
+        }
+        commit_to(bar_addr(sb, B_XFULL));
+        commit_to(bar_addr(sb, B_INVE));
+      }
+      if (!ok && err) atomicExch(err, IFK_ERR_TIMEOUT);
+    }
+  } else {
+    // ---------------- epilogue: warps 0-3, thread r = row of the block ----------------
+    const int r = tid;
+    const uint32_t lane_base = tm + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    for (int row = 0; row < nblk && ok; ++row) {
+      const int jb = trans ? row : nblk - 1 - row;
+      const int64_t j0 = (int64_t)jb * NB2;
+      const int nj = (int)mn<int64_t>(NB2, n - j0);
+      ok = wait_phase(bar_addr(sb, B_DFULL), row & 1, abort_);
+      if (!ok) break;
+      tc::fence_after();
+      float d[32];
+      if (row > 0) {
+        tc::tmem_ld32(lane_base + ((row & 1) ? TM_D1 : TM_D0), d);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) d[e] = 0.f;
+      }
+      float bv[NT];
+      if (cs == 1 && vb) {
+#pragma unroll
+        for (int g = 0; g < NT / 4; ++g) {
+          const float4 x = r < nj ? ld4(B + (j0 + r) * rs + c0 + 4 * g, nc - 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
+          bv[4 * g] = x.x; bv[4 * g + 1] = x.y; bv[4 * g + 2] = x.z; bv[4 * g + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < NT; ++c) bv[c] = (r < nj && c < nc) ? B[(j0 + r) * rs + (c0 + c) * cs] : 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < NT / 8; ++g) {
+        float hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tc::split_bf16(bv[g * 8 + e] - d[g * 8 + e], hi[e], lo[e]);
+        const uint32_t off = tc::cm_off<false>(g * 8, r, X_N, X_K);
+        st16(sb + OFF_YH + off, pack8(hi));
+        st16(sb + OFF_YL + off, pack8(lo));
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) arrive(bar_addr(sb, B_YRDY));
+      ok = wait_phase(bar_addr(sb, B_XFULL), row & 1, abort_);
+      if (!ok) break;
+      tc::fence_after();
+      float x[32];
+      tc::tmem_ld32(lane_base + TM_X, x);
+      if (r < nj) {
+        if (cs == 1 && vb) {
+#pragma unroll
+          for (int g = 0; g < NT / 4; ++g)
+            st4(B + (j0 + r) * rs + c0 + 4 * g, make_float4(x[4 * g], x[4 * g + 1], x[4 * g + 2], x[4 * g + 3]),
+                nc - 4 * g);
+        } else {
+#pragma unroll
+          for (int c = 0; c < NT; ++c)
+            if (c < nc) B[(j0 + r) * rs + (c0 + c) * cs] = x[c];
+        }
+      }
+      // bf16 copy of X_j for the later block rows of this CTA (rows past n and
+      // columns past N are exact zeros: their Y is zero)
+      uint8_t* xo = xmine + (size_t)jb * SZ_X;
+#pragma unroll
+      for (int g = 0; g < NT / 8; ++g)
+        *reinterpret_cast<uint4*>(xo + tc::cm_off<false>(g * 8, r, X_N, X_K)) = pack8(x + g * 8);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) arrive(bar_addr(sb, B_XRDY));
+    }
+    if (!ok && err) atomicExch(err, IFK_ERR_TIMEOUT);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_free(tm, TM_COLS);
+  }
+}
+
+bool attr_once() {
+  static thread_local int done_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (done_dev == dev) return true;
+  if (cudaFuncSetAttribute(trsm_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM) !=
+      cudaSuccess)
+    return false;
+  if (cudaFuncSetAttribute(diag_inverse_layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)INV_SMEM) != cudaSuccess)
+    return false;
+  done_dev = dev;
+  return true;
+}
+
+}  // namespace
+
+size_t trsm_persist_inverse_bytes(int64_t n) { return (size_t)cdiv(n, NB2) * 4 * SZ_A; }
+
+size_t trsm_persist_workspace(int64_t n, int64_t N) {
+  const size_t nblk = (size_t)cdiv(n, NB2);
+  return (size_t)cdiv(N, NT) * nblk * SZ_X + nblk * (nblk - 1) / 2 * SZ_A;
+}
+
+bool trsm_persist_ok(const void* A, int64_t ldA, int64_t n) {
+  return ((uintptr_t)A % 16) == 0 && ldA % 8 == 0 && n % 8 == 0 && n >= 8;
+}
+
+int trsm_persist_prepare(const __nv_bfloat16* A0, int64_t ld0, int64_t n0, void* inv0, const __nv_bfloat16* A1,
+                         int64_t ld1, int64_t n1, void* inv1, cudaStream_t s) {
+  if (!attr_once()) return IFK_ERR_CUDA;
+  const int64_t blocks = cdiv(n0, NB2) + (A1 ? cdiv(n1, NB2) : 0);
+  diag_inverse_layout_kernel<<<(unsigned)blocks, NB2, INV_SMEM, s>>>(A0, ld0, n0, (uint8_t*)inv0, A1, ld1, n1,
+                                                                       (uint8_t*)inv1);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+int trsm_persist_run(const __nv_bfloat16* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t cs, int64_t n,
+                     int64_t N, const void* inv, void* ws, int* err, cudaStream_t s) {
+  if (!attr_once()) return IFK_ERR_CUDA;
+  const int64_t nblk = cdiv(n, NB2);
+  // workspace: bf16 X copies | packed tiles
+  uint8_t* w = (uint8_t*)ws;
+  __nv_bfloat16* xws = (__nv_bfloat16*)w;
+  w += (size_t)cdiv(N, NT) * nblk * SZ_X;
+  uint8_t* tiles = w;
+  const int64_t ntiles = nblk * (nblk - 1) / 2;
+  if (ntiles > 0) pack_tiles_kernel<<<(unsigned)ntiles, 256, SZ_A, s>>>(A, ldA, n, trans, tiles);
+  // 16-byte vector access to rows of B needs 16-byte aligned rows
+  const int vb = (((uintptr_t)B % 16) == 0 && (rs * 4) % 16 == 0) ? 1 : 0;
+  trsm_persist_kernel<<<(unsigned)cdiv(N, NT), TPB, SMEM, s>>>(tiles, trans, B, rs, cs, n, N,
+                                                               (const __nv_bfloat16*)inv, xws, err, vb);
+  IFK_CUDA_TRY(cudaGetLastError());
+  return IFK_OK;
+}
+
+}  // namespace ifk
