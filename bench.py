@@ -57,15 +57,31 @@ def peaks():
         return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
-def launch_count(n=N_DIM, p=P_ROWS, tile=TILE):
-    """libifk kernel launches of one step (mirrors the host schedule in csrc/)."""
-    sub, nb, nb2 = 256, 64, 128
-    K = -(-n // nb)
-    per_pair = 2 + 2 * (-(-tile // sub) + K - 1)      # two chunk copies + one panel/update pair per wave
-    folds = (p // tile) * per_pair
-    fin = 2 * 2 + 2 * (-(-n // sub) + K - 1) + 2      # scale + fill per factor, waves, two finish
-    trsm = 4 * (1 + -(-n // nb2))
-    return folds + fin + trsm + 1
+def graph_kernel_names(graph):
+    """Kernel names of the nodes of a captured torch CUDA graph (driver-API introspection)."""
+    import cuda.bindings.driver as drv
+    g = drv.CUgraph(graph.raw_cuda_graph())
+    err, _, n = drv.cuGraphGetNodes(g, 0)
+    err, nodes, n = drv.cuGraphGetNodes(g, n)
+    names = []
+    for nd in nodes[:n]:
+        err, t = drv.cuGraphNodeGetType(nd)
+        if t != drv.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+            continue
+        err, prm = drv.cuGraphKernelNodeGetParams(nd)
+        err, name = drv.cuFuncGetName(prm.func)
+        names.append(name.decode() if isinstance(name, bytes) else str(name))
+    return names
+
+
+def count_launches(graph):
+    """libifk kernels (namespace ifk) per captured step, and the other kernels in it."""
+    try:
+        names = graph_kernel_names(graph)
+    except Exception as e:  # introspection unavailable: report it instead of guessing
+        return None, None, f"graph introspection failed: {type(e).__name__}"
+    ours = [n for n in names if "3ifk" in n]
+    return len(ours), len(names) - len(ours), "kernel nodes of the captured step graph"
 
 
 class ClockSampler:
@@ -172,8 +188,9 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         return
     graph = None
-    if not args.no_graph:
-        graph = torch.cuda.CUDAGraph()
+    if True:
+        # the step graph is timed unless --no-graph; it is always captured to count launches
+        graph = torch.cuda.CUDAGraph(keep_graph=True)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -183,8 +200,13 @@ def run_ours(args, rank, world, local_rank):
                 step(X, D, gW, W)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
+        graph.instantiate()
         graph.replay()
         torch.cuda.synchronize()
+
+    n_ours, n_other, launch_src = count_launches(graph)
+    if args.no_graph:
+        graph = None
 
     def run_steps(k):
         for _ in range(k):
@@ -287,7 +309,8 @@ def run_ours(args, rank, world, local_rank):
         "tflops": world * flops["total"] / (ms * 1e-3) / 1e12,
         "tflops_frac_of_measured_bf16": flops["total"] / (ms * 1e-3) / 1e12 / pk["bf16"],
         "components_ms": comp,
-        "gpu_launches": launch_count() * args.steps,
+        "gpu_launches": (n_ours * args.steps) if n_ours is not None else None,
+        "gpu_launches_detail": {"libifk_per_step": n_ours, "torch_per_step": n_other, "source": launch_src},
         "clocks": clk.summary(),
         "e2e": e2e,
     }
@@ -382,7 +405,12 @@ def main():
     ap.add_argument("--cpu-sample-scale", type=float, default=1.0)
     ap.add_argument("--profile", action="store_true",
                     help="run --warmup eager steps and one more step, then exit (for ncu)")
+    ap.add_argument("--profile-size", choices=["full", "small"], default="full",
+                    help="with --profile: 'small' runs n=1024, p=4096, tiles of 1024 (short ncu captures)")
     args = ap.parse_args()
+    if args.profile and args.profile_size == "small":
+        global N_DIM, P_ROWS, TILE
+        N_DIM, P_ROWS, TILE = 1024, 4096, 1024
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
