@@ -504,12 +504,14 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     __syncthreads();
 #ifdef IFK_TRACE
     const long long p0 = TR_NOW();
+    const long long k0 = clock64();
     TR_ADD(8, p0 - l0);
 #endif
-    panel::panel_factor(S, nbk, nact);
+    panel::panel_factor<SUB>(S, nbk, nact);
 #ifdef IFK_TRACE
     const long long p1 = TR_NOW();
     TR_ADD(11, p1 - p0);
+    TR_ADD(15, clock64() - k0);
 #endif
     TR_ADD(12, 1);
     // Y image (bf16, K-major for GEMM3 / MN-major for GEMM1) and T hi / lo images;

@@ -10,7 +10,8 @@ namespace panel {
 #ifdef IFK_TRACE
 // Diagnostic build only: slot for per-phase panel times (filled when
 // IFK_TRACE_PANEL is also defined; the phase marks slow the Gram steps down
-// severely, so task-level traces leave them out).
+// severely, so task-level traces leave them out); slots 9 and 10 count Gram
+// runs and leaves.
 __device__ unsigned long long g_panel_phase[16];
 #endif
 #ifdef IFK_TRACE_PANEL
@@ -44,26 +45,32 @@ __device__ __forceinline__ long long ptime() {
 #endif
 
 constexpr int LDP = NB + 1;   // row stride of the small NB x NB blocks
-constexpr int SP = SUB + 4;   // column stride of the panel (column-major; 16-byte aligned columns,
-                              // column c starts at bank 4c mod 32)
-constexpr int PT2 = 256;
-constexpr int NWARP = PT2 / 32;
+// The panel has ROWS rows (256 for the wave scheduler, 128 for the persistent
+// fold) and runs on threads 0 .. ROWS-1, thread = row.
+template <int ROWS>
+struct Geo {
+  static constexpr int SP = ROWS + 4;  // column stride of the panel (column-major; 16-byte aligned
+                                       // columns, column c starts at bank 4c mod 32)
+  static constexpr int NW = ROWS / 32;
+  static_assert(ROWS == 128 || ROWS == 256, "panels of 128 or 256 rows");
+};
+constexpr int SP = Geo<SUB>::SP;  // the wave scheduler's panels (SUB rows)
+constexpr int PT2 = SUB;
 constexpr int LEAF = 16;
 constexpr int NLEAF = NB / LEAF;
 constexpr int ZST = 20;       // stride per output column of the block-product partials (bank-conflict free)
 constexpr int LDW = NB;       // row stride of W
-static_assert(SUB == PT2, "the panel maps one row to each thread");
 
 // A column's squared norm may shrink to this fraction of its value at the last
 // Gram evaluation before the Gram matrix is evaluated again from the data.
 constexpr float GRAM_KEEP = 0.5f;
 
 // ---- method --------------------------------------------------------------------
-// 256 threads; thread t owns row t of the sub-tile.  The NB = 64 panel columns
+// ROWS threads; thread t owns row t of the sub-tile.  The NB = 64 panel columns
 // are factored in 4 leaves of 16 Householder reflectors (TPQRT: reflector j acts
 // on row j of the R block and on the sub-tile rows).
 //  * Leaf: the Gram matrix M = X_leaf^T X_leaf of the leaf's current columns is
-//    formed once (block product over the 256 rows).  One warp then computes the
+//    formed once (block product over the rows).  One warp then computes the
 //    16 reflectors in sequence from M and the leaf's R rows: reflector j needs
 //    |x_j|^2 = M[j][j] and the dot products M[j][c]; applying it updates M by a
 //    rank-2 term and row j of R.  No block-wide reduction is needed per column.
@@ -76,8 +83,9 @@ constexpr float GRAM_KEEP = 0.5f;
 //    substitution with T^-T = diag(1/tau) + strict_lower(Y^T Y); then
 //    R[leaf rows, trailing] -= W and P[:, trailing] -= Y_leaf W.
 //  * T is assembled from the leaf T's by T_AB = -T_A (Y_A^T Y_B) T_B.
-struct PanelSmem {
-  float P[NB * SP];          // X_t[:, panel] -> Y, column-major: element (i, c) at P[c * SP + i]
+template <int ROWS>
+struct PanelSmemT {
+  float P[NB * Geo<ROWS>::SP];  // X_t[:, panel] -> Y, column-major: element (i, c) at P[c * SP + i]
   float Rk[NB * LDP];        // diagonal block of R
   float G[NB * LDP];         // strict upper part of Y^T Y
   float Tm[NB * LDP];        // T, row-major
@@ -88,7 +96,14 @@ struct PanelSmem {
   float tau[NB];
   int jend;
 };
+using PanelSmem = PanelSmemT<SUB>;
 static_assert(4 * NB * ZST >= NB * LDP, "T assembly scratch fits the partials block");
+
+// Barrier of the panel's threads (id 2; the panel may run on part of a CTA)
+template <int ROWS>
+__device__ __forceinline__ void psync() {
+  asm volatile("bar.sync 2, %0;" ::"n"(ROWS) : "memory");
+}
 
 // Reflector of xLARFGP form (beta >= 0) for the column (aj; x) with |x|^2 = xn2:
 // H = I - tj v v^T, v = (1; x / v0), v0 = aj - beta formed without cancellation.
@@ -125,24 +140,25 @@ __device__ __forceinline__ float dot4(const float4 a, const float4 b, float acc)
 
 // Block product partials: for the 16 panel columns a0.. and the nb (1..64)
 // columns b0.., Zp[(q * NB + c) * ZST + i] = sum over the rows of quarter q
-// of P[r][a0 + i] * P[r][b0 + c].  Warps w and w + 4 share row quarter w % 4 and
-// split the output columns; lane (i4 = lane & 3, g = lane >> 2) accumulates rows
-// i4 + 4u of A against columns g + 8e of B, so every 16-byte load of a warp
-// touches distinct banks or broadcasts.  E = output-column groups of 8 (even).
-template <int E>
-__device__ __forceinline__ void block_product(PanelSmem& S, int a0, int b0, int nb) {
-  constexpr int EH = E / 2;
+// of P[r][a0 + i] * P[r][b0 + c].  Warp w takes row quarter w % 4; with 8 warps,
+// warps w and w + 4 split the output columns.  Lane (i4 = lane & 3, g = lane >> 2)
+// accumulates rows i4 + 4u of A against columns g + 8e of B, so every 16-byte
+// load of a warp touches distinct banks or broadcasts.  E = output-column groups of 8 (even).
+template <int ROWS, int E>
+__device__ __forceinline__ void block_product(PanelSmemT<ROWS>& S, int a0, int b0, int nb) {
+  constexpr int SP = Geo<ROWS>::SP;
+  constexpr int EH = E * 4 / Geo<ROWS>::NW;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int i4 = lane & 3, g = lane >> 2;
   const int rq = warp & 3, oh = warp >> 2;
   const float* pa[4];
   const float* pb[EH];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) pa[u] = S.P + (a0 + i4 + 4 * u) * SP + rq * (SUB / 4);
+  for (int u = 0; u < 4; ++u) pa[u] = S.P + (a0 + i4 + 4 * u) * SP + rq * (ROWS / 4);
 #pragma unroll
   for (int e = 0; e < EH; ++e) {
     const int c = g + 8 * (oh * EH + e);
-    pb[e] = S.P + (b0 + (c < nb ? c : nb - 1)) * SP + rq * (SUB / 4);
+    pb[e] = S.P + (b0 + (c < nb ? c : nb - 1)) * SP + rq * (ROWS / 4);
   }
   float acc[4][EH];
 #pragma unroll
@@ -150,7 +166,7 @@ __device__ __forceinline__ void block_product(PanelSmem& S, int a0, int b0, int 
 #pragma unroll
     for (int e = 0; e < EH; ++e) acc[u][e] = 0.f;
 #pragma unroll 4
-  for (int i = 0; i < SUB / 4; i += 4) {
+  for (int i = 0; i < ROWS / 4; i += 4) {
     float4 ya[4], pv[EH];
 #pragma unroll
     for (int u = 0; u < 4; ++u) ya[u] = *reinterpret_cast<const float4*>(pa[u] + i);
@@ -172,18 +188,19 @@ __device__ __forceinline__ void block_product(PanelSmem& S, int a0, int b0, int 
 }
 
 // Sum of the four row-quarter partials of output (i, c)
-__device__ __forceinline__ float zsum(const PanelSmem& S, int i, int c) {
+template <int ROWS>
+__device__ __forceinline__ float zsum(const PanelSmemT<ROWS>& S, int i, int c) {
   const float* z = S.Zp + c * ZST + i;
   return (z[0] + z[NB * ZST]) + (z[2 * NB * ZST] + z[3 * NB * ZST]);
 }
 
 // dst block (M x N at dr, dc) = (NEG ? -1 : 1) * A (M x K at ar, ac) * B (K x N at br, bc),
-// row-major LDP-stride blocks in shared memory; all PT2 threads.  Used for T assembly.
-template <int M, int K, int N, bool NEG>
+// row-major LDP-stride blocks in shared memory; all PT threads.  Used for T assembly.
+template <int PT, int M, int K, int N, bool NEG>
 __device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* A, int ar, int ac, const float* B,
                                        int br, int bc, int tid) {
 #pragma unroll
-  for (int o = tid; o < M * N; o += PT2) {
+  for (int o = tid; o < M * N; o += PT) {
     const int i = o / N, j = o % N;
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -199,13 +216,20 @@ __device__ __forceinline__ void matmul(float* dst, int dr, int dc, const float* 
 // L0..L0+15 against themselves) and the leaf's R rows in Rk, up to nl or until a
 // column's norm has shrunk past GRAM_KEEP.  Writes the R rows, tau, 1/v0 and
 // tau_j w_jc, and the end of the run to S.jend.
-__device__ __forceinline__ void gram_steps(PanelSmem& S, int L0, int jl, int nl, int nbk) {
+// Lanes c and c + 16 own column c of the leaf and split its row of M by the
+// parity of the column index (lane c + 16h keeps M[c][d] for d = h mod 2), so a
+// step costs each lane half the shuffles and updates of a whole row.  The
+// diagonal M[c][c] follows its own recurrence in both lanes, and the next pivot
+// |x_j|^2 is read from it, off the shuffles of the row update.
+template <int ROWS>
+__device__ __forceinline__ void gram_steps(PanelSmemT<ROWS>& S, int L0, int jl, int nl, int nbk) {
   const unsigned F = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const int c = lane & 15;  // lanes 16..31 repeat lanes 0..15
-  float Mc[LEAF], Rc[LEAF];
+  const int c = lane & 15, h = lane >> 4;
+  constexpr int HALF = LEAF / 2;
+  float Mh[HALF], Rc[LEAF];
 #pragma unroll
-  for (int d = 0; d < LEAF; ++d) Mc[d] = zsum(S, c, d);
+  for (int k = 0; k < HALF; ++k) Mh[k] = zsum(S, c, 2 * k + h);
 #pragma unroll
   for (int j = 0; j < LEAF; ++j) Rc[j] = S.Rk[(L0 + j) * LDP + L0 + c];
   float dc = zsum(S, c, c);  // M[c][c], kept by its own recurrence
@@ -213,30 +237,41 @@ __device__ __forceinline__ void gram_steps(PanelSmem& S, int L0, int jl, int nl,
   // Steps run to nl; a step whose update shrank a norm past GRAM_KEEP ends the
   // run after it (steps computed beyond that point are discarded).
   unsigned badmask = 0u;
+  // software pipelined: each step ends its critical chain (reflector, w, own
+  // diagonal) by fetching the next pivot, then does its row update
+  float xn2_next = __shfl_sync(F, dc, jl & 15);
 #pragma unroll
   for (int j = 0; j < LEAF; ++j) {
     if (j >= jl && j < nl) {
-      const float xn2 = __shfl_sync(F, Mc[j], j);
+      const float xn2 = xn2_next;
       const float al = __shfl_sync(F, Rc[j], j);
-      float Mj[LEAF];
-#pragma unroll
-      for (int d = j + 1; d < LEAF; ++d) Mj[d] = __shfl_sync(F, Mc[d], j);
+      // M[c][j]: in this lane when j has its parity, else in the partner lane
+      const float other = __shfl_xor_sync(F, Mh[j >> 1], 16);
+      const float mcj = (h == (j & 1)) ? Mh[j >> 1] : other;
       float tj, beta, iv;
       reflector(al, xn2, tj, beta, iv);
-      const float w = fmaf(Mc[j], iv, Rc[j]);
-      float wd[LEAF];
-#pragma unroll
-      for (int d = j + 1; d < LEAF; ++d) wd[d] = __shfl_sync(F, w, d);
+      const float w = fmaf(mcj, iv, Rc[j]);
       const float p = tj * iv;
       const float qw = p * p * xn2 * w;
-      const float mcj = Mc[j];
+      // own diagonal M[c][c] (c > j): -2 p w M[c][j] + p^2 xn2 w^2; next pivot
+      dc = fmaf(qw, w, fmaf(-2.f * p * w, mcj, dc));
+      if (j + 1 < LEAF) xn2_next = __shfl_sync(F, dc, j + 1);
+      // row j of M, this lane's parity: lane j + 16h holds it
+      float Mj[HALF];
+#pragma unroll
+      for (int k = 0; k < HALF; ++k)
+        if (2 * k + 1 > j) Mj[k] = __shfl_sync(F, Mh[k], j + 16 * h);
       // rows of finished columns (c <= j) are dead: update every lane's row
 #pragma unroll
-      for (int d = j + 1; d < LEAF; ++d) Mc[d] = fmaf(qw, wd[d], fmaf(-p, fmaf(w, Mj[d], wd[d] * mcj), Mc[d]));
-      // own diagonal M[c][c] (c > j): -2 p w M[c][j] + p^2 xn2 w^2
-      dc = fmaf(qw, w, fmaf(-2.f * p * w, mcj, dc));
+      for (int k = 0; k < HALF; ++k) {
+        if (2 * k + 1 > j) {
+          const float wd = __shfl_sync(F, w, 2 * k + h);  // w of column d = 2k + h
+          const float upd = fmaf(qw, wd, fmaf(-p, fmaf(w, Mj[k], wd * mcj), Mh[k]));
+          Mh[k] = (2 * k + h > j) ? upd : Mh[k];
+        }
+      }
       Rc[j] = (c == j) ? beta : fmaf(-tj, w, Rc[j]);
-      if (c > j && lane < LEAF) S.Wr[j * LEAF + c] = tj * w;
+      if (c > j && h == 0) S.Wr[j * LEAF + c] = tj * w;
       if (lane == j) {
         S.ivv[j] = iv;
         S.tau[L0 + j] = tj;
@@ -255,24 +290,27 @@ __device__ __forceinline__ void gram_steps(PanelSmem& S, int L0, int jl, int nl,
   if (lane == 0) S.jend = jend;
 }
 
-// Factor the panel in S.P (SUB x NB fp32, column-major; rows beyond the
+// Factor the panel in S.P (ROWS x NB fp32, column-major; rows beyond the
 // sub-tile are zero) under the R diagonal block S.Rk.  nbk panel columns exist,
 // the first nact carry reflectors (the rest lie beyond the rank bound and get
 // identity reflectors).  On return S.P holds Y, S.Rk the new R block
 // (non-negative diagonal), S.Tm the compact-WY T (row-major) and S.tau the
-// tau's.  All PT2 threads call it; it begins and ends with a __syncthreads.
-static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, const int nact) {
+// tau's.  Threads 0 .. ROWS-1 call it; it begins and ends with a barrier of them.
+template <int ROWS>
+static __device__ __noinline__ void panel_factor(PanelSmemT<ROWS>& S, const int nbk, const int nact) {
+  constexpr int SP = Geo<ROWS>::SP;
+  constexpr int PT = ROWS;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   PH_DECL
-  for (int idx = tid; idx < NB * LDP; idx += PT2) {
+  for (int idx = tid; idx < NB * LDP; idx += PT) {
     S.G[idx] = 0.f;
     S.Tm[idx] = 0.f;
   }
   if (tid < NB) S.tau[tid] = 0.f;
   const int r = tid;
   for (int c = nbk; c < NB; ++c) S.P[c * SP + r] = 0.f;  // columns past the block: zero
-  __syncthreads();
+  psync<ROWS>();
 #pragma unroll 1
   for (int s = 0; s < NLEAF; ++s) {
     const int L0 = s * LEAF;
@@ -284,12 +322,18 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
     // ---- leaf: Gram runs ----
     int jl = 0;
 #pragma unroll 1
+#ifdef IFK_TRACE
+    if (tid == 0 && nl > 0) atomicAdd(&g_panel_phase[10], 1ull);
+#endif
     while (jl < nl) {
-      block_product<2>(S, L0, L0, LEAF);
-      __syncthreads();
+#ifdef IFK_TRACE
+      if (tid == 0) atomicAdd(&g_panel_phase[9], 1ull);
+#endif
+      block_product<ROWS, 2>(S, L0, L0, LEAF);
+      psync<ROWS>();
       PH_MARK(0);
-      if (warp == 0) gram_steps(S, L0, jl, nl, nbk);
-      __syncthreads();
+      if (warp == 0) gram_steps<ROWS>(S, L0, jl, nl, nbk);
+      psync<ROWS>();
       PH_MARK(1);
       const int jend = S.jend;
       // apply reflectors jl .. jend-1 to this thread's row
@@ -315,7 +359,7 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
 #pragma unroll
         for (int c = 0; c < LEAF; ++c) S.P[(L0 + c) * SP + r] = a[c];
       }
-      __syncthreads();  // Wr / ivv / jend are rewritten by the next run
+      psync<ROWS>();  // Wr / ivv / jend are rewritten by the next run
       PH_MARK(2);
     }
     // columns beyond the rank bound carry no reflector
@@ -324,22 +368,22 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
       if (L0 + c >= nact) a[c] = 0.f;
       S.P[(L0 + c) * SP + r] = a[c];
     }
-    __syncthreads();
+    psync<ROWS>();
     if (L0 >= nact) continue;  // no reflectors: R rows, T and trailing columns unchanged
     // ---- Y_leaf^T P[:, 0:nbk]: leaf blocks of Y^T Y and Z ----
-    block_product<8>(S, L0, 0, nbk);
-    __syncthreads();
+    block_product<ROWS, 8>(S, L0, 0, nbk);
+    psync<ROWS>();
     PH_MARK(3);
     const int C0 = L0 + LEAF;
     const int wcI = nbk - C0;
-    for (int o = tid; o < LEAF * nbk; o += PT2) {
+    for (int o = tid; o < LEAF * nbk; o += PT) {
       const int i = o & 15, c = o >> 4;
       const float v = zsum(S, i, c);
       if (c < L0) S.G[c * LDP + L0 + i] = v;                    // (Y_c-leaf)^T Y_leaf
       else if (c < C0) { if (c > L0 + i) S.G[(L0 + i) * LDP + c] = v; }  // strict upper of the leaf block
       else S.Wb[i * LDW + (c - C0)] = v + S.Rk[(L0 + i) * LDP + c];     // Z + R rows
     }
-    __syncthreads();
+    psync<ROWS>();
     PH_MARK(4);
     // W = T_leaf^T Z by forward substitution; leaf T by the column recursion (warp 7)
     if (tid < wcI) {
@@ -364,7 +408,7 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
 #pragma unroll
       for (int j = 0; j < LEAF; ++j) S.Wb[j * LDW + tid] = 0.f;
     }
-    if (warp == NWARP - 1 && (tid & 31) < LEAF) {
+    if (warp == Geo<ROWS>::NW - 1 && (tid & 31) < LEAF) {
       const int i = tid & 31;
       float Tr[LEAF];
 #pragma unroll
@@ -382,10 +426,10 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
       for (int jj = 0; jj < LEAF; ++jj) S.Tm[(L0 + i) * LDP + L0 + jj] = Tr[jj];
     }
     if (wcI <= 0) {
-      __syncthreads();
+      psync<ROWS>();
       continue;
     }
-    __syncthreads();
+    psync<ROWS>();
     PH_MARK(5);
     // P[:, C] -= Y_leaf W; this thread's Y_leaf row is still in a[]
     const int nq = (wcI + 3) / 4;
@@ -406,21 +450,21 @@ static __device__ __noinline__ void panel_factor(PanelSmem& S, const int nbk, co
         if (c < nbk) S.P[c * SP + r] -= d[e];
       }
     }
-    __syncthreads();
+    psync<ROWS>();
     PH_MARK(6);
   }
   // T assembly: T_{01} = -T_0 G_{01} T_1, T_{23} likewise, then the 32 x 32 coupling
   float* Tmp = S.Zp;
-  matmul<16, 16, 16, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, tid);     // T0 G01
-  matmul<16, 16, 16, false>(Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, tid); // T2 G23
-  __syncthreads();
-  matmul<16, 16, 16, true>(S.Tm, 0, 16, Tmp, 0, 0, S.Tm, 16, 16, tid);    // T01
-  matmul<16, 16, 16, true>(S.Tm, 32, 48, Tmp, 16, 32, S.Tm, 48, 48, tid); // T23
-  __syncthreads();
-  matmul<32, 32, 32, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, tid);      // T_A G_AB (32 x 32)
-  __syncthreads();
-  matmul<32, 32, 32, true>(S.Tm, 0, 32, Tmp, 0, 0, S.Tm, 32, 32, tid);    // T_AB
-  __syncthreads();
+  matmul<PT, 16, 16, 16, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 16, tid);     // T0 G01
+  matmul<PT, 16, 16, 16, false>(Tmp, 16, 32, S.Tm, 32, 32, S.G, 32, 48, tid); // T2 G23
+  psync<ROWS>();
+  matmul<PT, 16, 16, 16, true>(S.Tm, 0, 16, Tmp, 0, 0, S.Tm, 16, 16, tid);    // T01
+  matmul<PT, 16, 16, 16, true>(S.Tm, 32, 48, Tmp, 16, 32, S.Tm, 48, 48, tid); // T23
+  psync<ROWS>();
+  matmul<PT, 32, 32, 32, false>(Tmp, 0, 0, S.Tm, 0, 0, S.G, 0, 32, tid);      // T_A G_AB (32 x 32)
+  psync<ROWS>();
+  matmul<PT, 32, 32, 32, true>(S.Tm, 0, 32, Tmp, 0, 0, S.Tm, 32, 32, tid);    // T_AB
+  psync<ROWS>();
   PH_MARK(7);
   PH_FLUSH()
 }

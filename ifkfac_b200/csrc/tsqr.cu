@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
     }
   }
 
-  panel::panel_factor(S, nbk, nact);
+  panel::panel_factor<SUB>(S, nbk, nact);
 
   // T stored column-major (Tb[j*NB + i] = T[i][j]) for the trailing update
   float* Tb = a.Tb + (size_t)t * NB * NB;
