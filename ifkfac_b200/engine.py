@@ -11,7 +11,7 @@ reference's hooks (``_n_rows_X`` / ``_n_rows_G``, ifkfac/activation_hooks.py:205
 from __future__ import annotations
 
 import ctypes
-from typing import Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 
@@ -107,12 +107,37 @@ def fold_batched(factors: Sequence[Factor], chunks: Sequence[torch.Tensor], ws: 
     return ws
 
 
+def _rows_view(chunks: Sequence[torch.Tensor]) -> torch.Tensor:
+    """The chunks stacked by rows: a view when they are consecutive row slices of
+    one tensor (no copy), else a concatenation."""
+    c0 = chunks[0]
+    if len(chunks) == 1:
+        return c0
+    es, rs = c0.element_size(), c0.stride(0)
+    adjacent = all(c.dtype == c0.dtype and c.shape[1] == c0.shape[1] and c.stride() == c0.stride()
+                   and c.stride(1) == 1 and c.untyped_storage().data_ptr() == c0.untyped_storage().data_ptr()
+                   for c in chunks)
+    for a, b in zip(chunks, chunks[1:]):
+        adjacent = adjacent and b.data_ptr() == a.data_ptr() + a.shape[0] * rs * es
+    if adjacent:
+        return torch.as_strided(c0, (sum(c.shape[0] for c in chunks), c0.shape[1]), c0.stride())
+    return torch.cat(list(chunks), 0)
+
+
 class LayerCurvature:
-    """Device state of one layer's curvature path (factors, natgrad, momentum)."""
+    """Device state of one layer's curvature path (factors, natgrad, momentum).
+
+    ``window`` > 1 defers folding like the reference's deferred hook mode
+    (``ifkfac/activation_hooks.py:347-364``): chunks are kept (by reference; the
+    caller keeps them alive) until ``window`` of them are pending or the factors
+    are refreshed, then folded as one chunk of all their rows, so one persistent
+    launch covers several tiles."""
 
     def __init__(self, n_in: int, n_out: int, device, prec: int = _lib.PREC_AUTO,
-                 factor_dtype: torch.dtype = torch.float32, chunk_rows: int = 0):
+                 factor_dtype: torch.dtype = torch.float32, chunk_rows: int = 0, window: int = 1):
         L = _lib.lib()
+        self.window = max(int(window), 1)
+        self._pending: List[Tuple[torch.Tensor, torch.Tensor]] = []
         self.n_in, self.n_out = n_in, n_out
         self.device = torch.device(device)
         self.prec = prec
@@ -131,18 +156,34 @@ class LayerCurvature:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.fx.status = self.status
         self.fg.status = self.status
-        rows = max(chunk_rows, 1)
+        rows = max(chunk_rows, 1) * self.window
         self.ws_pair = _ws(L.ifk_tsqr_fold_batched_workspace(
             2, _arr(ctypes.c_int64, [rows, rows]), _arr(ctypes.c_int64, [n_in, n_out])), self.device)
 
     def fold(self, x_chunk: torch.Tensor, g_chunk: torch.Tensor) -> None:
-        """Fold an activation chunk into R_X and a gradient chunk into R_G together."""
-        self.ws_pair = fold_batched((self.fx, self.fg), (x_chunk, g_chunk), self.ws_pair)
+        """Fold an activation chunk into R_X and a gradient chunk into R_G together
+        (or keep them for a deferred fold when window > 1)."""
+        if self.window <= 1:
+            self.ws_pair = fold_batched((self.fx, self.fg), (x_chunk, g_chunk), self.ws_pair)
+            return
+        self._pending.append((x_chunk, g_chunk))
+        if len(self._pending) >= self.window:
+            self.flush()
+
+    def flush(self) -> None:
+        """Fold the pending chunks (deferred mode) as one chunk per factor."""
+        if not self._pending:
+            return
+        x = _rows_view([x for x, _ in self._pending])
+        g = _rows_view([g for _, g in self._pending])
+        self._pending = []
+        self.ws_pair = fold_batched((self.fx, self.fg), (x, g), self.ws_pair)
 
     # ---- factor refresh: get_factors + _update_factors (finite check, dtype) ----
     def refresh(self, damping: float, solve_prec: Optional[int] = None) -> bool:
         """Damped factors from the running R's; False (nothing queued) while either is
         still trapezoidal, the reference's per-layer skip (ifkfac/activation_hooks.py:287-300)."""
+        self.flush()
         if self.fx.rows_R < self.n_in or self.fg.rows_R < self.n_out:
             return False
         L = _lib.lib()
@@ -198,5 +239,6 @@ class LayerCurvature:
             "ifk_update")
 
     def clear(self) -> None:
+        self._pending = []
         self.fx.clear()
         self.fg.clear()
