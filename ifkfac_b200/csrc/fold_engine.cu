@@ -147,6 +147,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Bulk copy of a panel's images from shared to global memory by the TMA engine
+// (one thread; completion through the bulk-group counter).
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait for this thread's bulk stores, then release *flag to other CTAs.
+__device__ __forceinline__ void bulk_publish(int* flag) {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __threadfence();
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
+}
+
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -439,17 +454,19 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 #ifdef IFK_TRACE
     const long long w0 = TR_NOW();
 #endif
-    if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
-    if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
-    TR_ADD(9, TR_NOW() - w0);
-    TR_ADD(10, 1);
-    copy_images_in(c, F.img + ((size_t)t * F.K + k) * PIMG);
+    // the operand image of X depends on the previous apply only: refresh it before waiting
     if (!a1_valid) {
       tc::fence_before();
       __syncthreads();
       tc::fence_after();
       refresh_a1(c);
+      a1_valid = true;
     }
+    if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
+    if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
+    TR_ADD(9, TR_NOW() - w0);
+    TR_ADD(10, 1);
+    copy_images_in(c, F.img + ((size_t)t * F.K + k) * PIMG);
     sync_for_mma();
     apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false);
     a1_valid = false;
@@ -467,6 +484,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   //   every earlier sub-tile too, or by every later one, so its stage passes at once.
   TR_SET(6, TR_NOW());
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
+  int* pending_img = nullptr;  // flag of panel images whose bulk store is in flight
 #pragma unroll 1
   for (int q = 0; q < 2; ++q) {
     const int kk = 2 * cb + q;
@@ -514,6 +532,11 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     TR_ADD(15, clock64() - k0);
 #endif
     TR_ADD(12, 1);
+    if (pending_img) {  // the first panel's bulk store must be done before its images are overwritten
+      if (tid == 0) bulk_publish(pending_img);
+      pending_img = nullptr;
+      __syncthreads();
+    }
     // Y image (bf16, K-major for GEMM3 / MN-major for GEMM1) and T hi / lo images;
     // lanes take consecutive rows, so the column reads of P are conflict-free
     for (int it = tid; it < SUB * (NB / 8); it += TPB) {
@@ -536,25 +559,30 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       const int i = idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) F.R[(c0 + i) * F.ldR + c0 + j] = S.Rk[i * LDP + j];
     }
+    // The R diagonal block (stage K + 1 + 2q) goes out at once; the images go
+    // by a bulk store.  The first panel's images are released only before the
+    // second panel's overwrite them (the copy runs under the apply to the
+    // block's second half and the second panel); the second panel's at once.
+    tc::fence_async_smem();
     __syncthreads();
-    {
-      uint4* dst = reinterpret_cast<uint4*>(F.img + ((size_t)t * F.K + kk) * PIMG);
-      const uint4* srcs = reinterpret_cast<const uint4*>(c.sm + OFF_Y);
-      for (int i = tid; i < (int)(PIMG / 16); i += TPB) dst[i] = srcs[i];
-    }
-    // one fence publishes both the R diagonal block (stage) and the panel images
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      st_release(prog, F.K + 1 + 2 * q);
-      st_release(F.pflag + (size_t)t * F.K + kk, 1);
+    if (tid == 0) bulk_store(F.img + ((size_t)t * F.K + kk) * PIMG, c.sb + OFF_Y, PIMG);
+    const bool half = q == 0 && wc > NB;
+    if (half) {
+      cta_publish_value(prog, F.K + 1 + 2 * q);
+      pending_img = F.pflag + (size_t)t * F.K + kk;
+    } else {
+      __syncthreads();
+      if (tid == 0) {
+        bulk_publish(F.pflag + (size_t)t * F.K + kk);
+        st_release(prog, F.K + 1 + 2 * q);
+      }
     }
     TR_ADD(13, TR_NOW() - p1);
     if (q == 0) {
 #ifdef IFK_TRACE
       const long long h0 = TR_NOW();
 #endif
-      if (wc > NB) {
+      if (half) {
         // the first panel also acts on the block's second half
         if (t > 0 && !cta_wait_ge(prev_prog, F.K + 2, b, s_ok)) return;
         refresh_a1(c);
@@ -564,6 +592,10 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       cta_publish_value(prog, F.K + 2);
       TR_ADD(14, TR_NOW() - h0);
     }
+  }
+  if (pending_img) {
+    if (tid == 0) bulk_publish(pending_img);
+    __syncthreads();
   }
   tc::fence_before();
   cta_publish_value(prog, F.K + 3);
@@ -634,6 +666,8 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
       break;
     }
   }
+  // a task that gave up may leave a bulk store of panel images in flight
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {
