@@ -317,15 +317,41 @@ def run_ours(args, rank, world, local_rank):
         bi = hX.numel() * 2 + hD.numel() * 2 + hG.numel() * 4
         bo = hW.numel() * 4
         k2 = max(1, min(args.steps, 5))
+        # Each step copies its inputs tile by tile on a copy stream; the fold of a
+        # tile waits for that tile only, so the transfers run under the folds.
+        # The step starts its copies after the previous step's reads of X, D, gW.
+        cs = torch.cuda.Stream()
+        s0 = torch.cuda.current_stream()
+
+        def e2e_step():
+            cs.wait_stream(s0)
+            evs = []
+            with torch.cuda.stream(cs):
+                for lo, hi in tiles:
+                    X[lo:hi].copy_(hX[lo:hi], non_blocking=True)
+                    D[lo:hi].copy_(hD[lo:hi], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(cs)
+                    evs.append(e)
+                gW.copy_(hG, non_blocking=True)
+                eg = torch.cuda.Event()
+                eg.record(cs)
+            lc.clear()
+            for (lo, hi), e in zip(tiles, evs):
+                s0.wait_event(e)
+                lc.fold(X[lo:hi], D[lo:hi])
+            lc.refresh(DAMPING)
+            s0.wait_event(eg)
+            lc.update(W, lc.natgrad(gW), LR, MOM, 0.0, None)
+            hW.copy_(W, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(k2):
-            X.copy_(hX, non_blocking=True)
-            D.copy_(hD, non_blocking=True)
-            gW.copy_(hG, non_blocking=True)
-            run_steps(1)
-            hW.copy_(W, non_blocking=True)
+            e2e_step()
         b.record()
         b.synchronize()
         e2e_ms = a.elapsed_time(b) / k2
@@ -334,7 +360,8 @@ def run_ours(args, rank, world, local_rank):
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(t.item())
         e2e = {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": bi,
-               "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms}
+               "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms,
+               "note": "pinned host inputs copied per tile on a copy stream under the folds; W read back each step"}
 
     if rank != 0:
         return
