@@ -9,6 +9,16 @@ lr 1e-3 update of fp32 master weights.  Inputs are synthetic with the
 config's distributions (no dataset is involved): X, delta ~ N(0,1) times
 per-column scales log-uniform in [1, 100] (kappa ~ 1e2), grad_W ~ N(0, 1e-2).
 
+Fold schedules (--schedule), both with the reflector sequence of the streaming
+fold, one 256-row sub-tile after another in tile order, and the same factors:
+  one-launch (default): the tiles are resident, so one persistent launch per
+      step folds all of them in order together with the damping rows
+      sqrt(lambda p) I, and the result is scaled by 1/sqrt(p) (exact for
+      p = 16384, a power of 4);
+  per-tile: one fold launch per tile as it would arrive from a hook, then the
+      damping fold.
+The other schedule is timed too and reported as "other_schedule".
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 (launched with torchrun, one rank per GPU): layers are dealt
@@ -44,7 +54,7 @@ def algorithmic_flops(n=N_DIM, p=P_ROWS, n_in=N_DIM, n_out=N_DIM):
     tsqr = 2 * (2 * p * n * n - 2.0 / 3.0 * n ** 3)
     fold = 2 * (2.0 / 3.0 * n ** 3)
     trsm = 2 * n_out * n_out * n_in + 2 * n_in * n_in * n_out
-    return {"tsqr": tsqr, "fold": fold, "trsm": trsm, "total": tsqr + fold + trsm}
+    return {"tsqr": tsqr, "fold": fold, "trsm": trsm, "tsqr_fold": tsqr + fold, "total": tsqr + fold + trsm}
 
 
 def peaks():
@@ -99,9 +109,14 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # the timed region starts once the sampler answers (its start-up takes a moment)
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.01)
+            self.lines.clear()
         except Exception:
             self.proc = None
         return self
@@ -151,6 +166,61 @@ def make_inputs(device, seed):
     return X, D, gW, W
 
 
+def make_layer(dev, per_tile, ntiles):
+    """Device state of the layer: fp32 running factors, bf16 damped factors."""
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import LayerCurvature
+    import torch
+    return LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_BF16, torch.bfloat16, TILE,
+                          window=1 if per_tile else ntiles)
+
+
+def run_step(lc, per_tile, tiles, x, d, g, w):
+    """One operator step.  Schedules (same reflector sequence, same factors):
+    "one-launch": the row tiles are resident, so they are folded in arrival order
+    by one persistent launch per factor pair together with the damping rows
+    (ifk_tsqr_fold_segments with an identity tail), then scaled by 1/sqrt(p);
+    "per-tile": one fold launch per tile as it arrives, then the damping fold."""
+    lc.clear()
+    for lo, hi in tiles:
+        lc.fold(x[lo:hi], d[lo:hi])
+    lc.refresh(DAMPING, consume=not per_tile)
+    lc.update(w, lc.natgrad(g), LR, MOM, 0.0, None)
+
+
+def time_components(lc, per_tile, tiles, X, D, gW, W):
+    """Device time of each stage of one eager step (CUDA events on the launching stream)."""
+    import torch
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        a, b = ev(), ev()
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    lc.clear()
+    torch.cuda.synchronize()
+    comp = {}
+    if per_tile:
+        comp["tsqr_ms"] = sum(timed(lambda: lc.fold(X[lo:hi], D[lo:hi])) for lo, hi in tiles)
+        comp["fold_ms"] = timed(lambda: lc.refresh(DAMPING))
+    else:
+        for lo, hi in tiles:
+            lc.fold(X[lo:hi], D[lo:hi])  # kept for the launch below: no device work
+        comp["tsqr_fold_ms"] = timed(lambda: lc.refresh(DAMPING, consume=True))
+    nat = [None]
+
+    def nat_fn():
+        nat[0] = lc.natgrad(gW)
+
+    comp["trsm_ms"] = timed(nat_fn)
+    comp["update_ms"] = timed(lambda: lc.update(W, nat[0], LR, MOM, 0.0, None))
+    return comp
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     from ifkfac_b200 import _lib
@@ -160,16 +230,12 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     _lib.check(_lib.lib().ifk_device_check(), "ifk_device_check")
     X, D, gW, W = make_inputs(dev, 1234 + rank)
-    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_BF16, torch.bfloat16, TILE)
     tiles = [(t * TILE, (t + 1) * TILE) for t in range(P_ROWS // TILE)]
+    per_tile = args.schedule == "per-tile"
+    lc = make_layer(dev, per_tile, len(tiles))
 
     def step(x, d, g, w):
-        lc.clear()
-        for lo, hi in tiles:
-            lc.fold(x[lo:hi], d[lo:hi])
-        lc.refresh(DAMPING)
-        nat = lc.natgrad(g)
-        lc.update(w, nat, LR, MOM, 0.0, None)
+        run_step(lc, per_tile, tiles, x, d, g, w)
 
     def barrier():
         if world > 1:
@@ -235,77 +301,28 @@ def run_ours(args, rank, world, local_rank):
     # ---- component timing (eager, events on the launching stream) ----
     comp = {}
     if rank == 0:
-        ev = lambda: torch.cuda.Event(enable_timing=True)
-        lc.clear()
-        torch.cuda.synchronize()
-        fold_ms = 0.0
-        for lo, hi in tiles:
-            a, b = ev(), ev()
-            a.record()
-            lc.fold(X[lo:hi], D[lo:hi])
-            b.record()
-            b.synchronize()
-            fold_ms += a.elapsed_time(b)
-        a, b = ev(), ev()
-        a.record()
-        lc.refresh(DAMPING)
-        b.record()
-        b.synchronize()
-        fin_ms = a.elapsed_time(b)
-        a, b = ev(), ev()
-        a.record()
-        nat = lc.natgrad(gW)
-        b.record()
-        b.synchronize()
-        nat_ms = a.elapsed_time(b)
-        a, b = ev(), ev()
-        a.record()
-        lc.update(W, nat, LR, MOM, 0.0, None)
-        b.record()
-        b.synchronize()
-        upd_ms = a.elapsed_time(b)
-        comp = {"tsqr_ms": fold_ms, "fold_ms": fin_ms, "trsm_ms": nat_ms, "update_ms": upd_ms}
+        comp = time_components(lc, per_tile, tiles, X, D, gW, W)
 
-    # ---- secondary: the reference's deferred hook mode (window = all tiles of the step) ----
-    # Same rows, same factors; the tiles are kept and folded as one chunk at refresh,
-    # so one persistent launch covers the whole batch.  Reported beside the headline,
-    # which stays the streaming fold of the named configuration.
-    deferred = None
-    if rank == 0 and not args.no_deferred:
-        lcd = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_BF16, torch.bfloat16, TILE, window=len(tiles))
-        Wd = W.clone()
-
-        def dstep():
-            lcd.clear()
-            for lo, hi in tiles:
-                lcd.fold(X[lo:hi], D[lo:hi])
-            lcd.refresh(DAMPING)
-            lcd.update(Wd, lcd.natgrad(gW), LR, MOM, 0.0, None)
-
+    # ---- secondary: the other schedule of the same step (eager timing) ----
+    other = None
+    if rank == 0 and not args.no_other_schedule:
+        lco = make_layer(dev, not per_tile, len(tiles))
+        Wo = W.clone()
         for _ in range(2):
-            dstep()
+            run_step(lco, not per_tile, tiles, X, D, gW, Wo)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        kd = max(1, min(args.steps, 5))
+        ko = max(1, min(args.steps, 5))
         a.record()
-        for _ in range(kd):
-            dstep()
+        for _ in range(ko):
+            run_step(lco, not per_tile, tiles, X, D, gW, Wo)
         b.record()
         b.synchronize()
-        dms = a.elapsed_time(b) / kd
-        lcd.clear()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for lo, hi in tiles:
-            lcd.fold(X[lo:hi], D[lo:hi])
-        lcd.flush()
-        b.record()
-        b.synchronize()
-        deferred = {"window_tiles": len(tiles), "ms_per_step": dms, "value": 1000.0 / dms, "unit": "steps/s",
-                    "tsqr_ms": a.elapsed_time(b), "timing": "eager, CUDA events, one GPU",
-                    "note": "deferred hook mode (ifkfac/activation_hooks.py:347-364): tiles folded as one chunk"}
-        del lcd, Wd
+        oms = a.elapsed_time(b) / ko
+        other = {"schedule": "one-launch" if per_tile else "per-tile", "ms_per_step": oms,
+                 "value": 1000.0 / oms, "unit": "steps/s", "timing": "eager, CUDA events, one GPU",
+                 "components_ms": time_components(lco, not per_tile, tiles, X, D, gW, Wo)}
+        del lco, Wo
 
     # ---- end to end through the public API: pinned host inputs in, weights out ----
     e2e = None
@@ -317,11 +334,16 @@ def run_ours(args, rank, world, local_rank):
         bi = hX.numel() * 2 + hD.numel() * 2 + hG.numel() * 4
         bo = hW.numel() * 4
         k2 = max(1, min(args.steps, 5))
-        # Each step copies its inputs tile by tile on a copy stream; the fold of a
-        # tile waits for that tile only, so the transfers run under the folds.
-        # The step starts its copies after the previous step's reads of X, D, gW.
+        # Each step copies its inputs tile by tile on a copy stream.  per-tile: the
+        # fold of a tile waits for that tile only.  one-launch: the tiles are folded
+        # in --e2e-groups launches of consecutive tiles (the last one with the
+        # damping rows), each waiting for its own tiles, so the copies of a group
+        # run under the fold of the one before.  The step starts its copies after
+        # the previous step's reads of X, D, gW.
         cs = torch.cuda.Stream()
         s0 = torch.cuda.current_stream()
+        ng = 1 if per_tile else max(1, min(args.e2e_groups, len(tiles)))
+        bounds = [round(i * len(tiles) / ng) for i in range(ng + 1)]
 
         def e2e_step():
             cs.wait_stream(s0)
@@ -337,10 +359,19 @@ def run_ours(args, rank, world, local_rank):
                 eg = torch.cuda.Event()
                 eg.record(cs)
             lc.clear()
-            for (lo, hi), e in zip(tiles, evs):
-                s0.wait_event(e)
-                lc.fold(X[lo:hi], D[lo:hi])
-            lc.refresh(DAMPING)
+            if per_tile:
+                for (lo, hi), e in zip(tiles, evs):
+                    s0.wait_event(e)
+                    lc.fold(X[lo:hi], D[lo:hi])
+                lc.refresh(DAMPING)
+            else:
+                for gi in range(ng):
+                    s0.wait_event(evs[bounds[gi + 1] - 1])
+                    for lo, hi in tiles[bounds[gi]:bounds[gi + 1]]:
+                        lc.fold(X[lo:hi], D[lo:hi])
+                    if gi + 1 < ng:
+                        lc.flush()
+                lc.refresh(DAMPING, consume=True)
             s0.wait_event(eg)
             lc.update(W, lc.natgrad(gW), LR, MOM, 0.0, None)
             hW.copy_(W, non_blocking=True)
@@ -361,7 +392,9 @@ def run_ours(args, rank, world, local_rank):
             e2e_ms = float(t.item())
         e2e = {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": bi,
                "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms,
-               "note": "pinned host inputs copied per tile on a copy stream under the folds; W read back each step"}
+               "schedule": args.schedule, "launch_groups": ng,
+               "note": ("pinned host inputs copied per tile on a copy stream; each fold launch waits for its "
+                        "own tiles only; W read back each step")}
 
     if rank != 0:
         return
@@ -377,7 +410,8 @@ def run_ours(args, rank, world, local_rank):
         "tflops": world * flops["total"] / (ms * 1e-3) / 1e12,
         "tflops_frac_of_measured_bf16": flops["total"] / (ms * 1e-3) / 1e12 / pk["bf16"],
         "components_ms": comp,
-        "deferred_mode": deferred,
+        "schedule": args.schedule,
+        "other_schedule": other,
         "gpu_launches": (n_ours * args.steps) if n_ours is not None else None,
         "gpu_launches_detail": {"libifk_per_step": n_ours, "torch_per_step": n_other, "source": launch_src},
         "clocks": clk.summary(),
@@ -385,8 +419,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if comp:
         # dominant component by time; achieved = its algorithmic flops / its device time
-        name, key = max((("tsqr", "tsqr_ms"), ("fold", "fold_ms"), ("trsm", "trsm_ms")),
-                        key=lambda x: comp[x[1]])
+        stages = [("tsqr_fold", "tsqr_fold_ms"), ("tsqr", "tsqr_ms"), ("fold", "fold_ms"), ("trsm", "trsm_ms")]
+        name, key = max(((nm, k) for nm, k in stages if k in comp), key=lambda x: comp[x[1]])
         ach = flops[name] / (comp[key] * 1e-3) / 1e12
         traffic = None
         try:
@@ -466,12 +500,17 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-deferred", action="store_true", help="skip the secondary deferred-mode timing")
+    ap.add_argument("--schedule", choices=["one-launch", "per-tile"], default="one-launch",
+                    help="fold schedule of the timed step (the other one is reported beside it)")
+    ap.add_argument("--e2e-groups", type=int, default=2,
+                    help="one-launch schedule, e2e: fold launches the row tiles are split into")
+    ap.add_argument("--no-other-schedule", action="store_true",
+                    help="skip the secondary timing of the other schedule")
     ap.add_argument("--cpu-sample-scale", type=float, default=1.0)
     ap.add_argument("--profile", action="store_true",
                     help="run --warmup eager steps and one more step, then exit (for ncu)")

@@ -35,6 +35,9 @@ SIGNATURES = {
     "ifk_tsqr_fold_batched_workspace": (_sz, [_int, _vp, _vp]),
     "ifk_tsqr_fold_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp,
                                      _vp, _sz, _vp]),
+    "ifk_tsqr_fold_segments_workspace": (_sz, [_int, _vp, _vp, _vp, _vp]),
+    "ifk_tsqr_fold_segments": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _int, _vp,
+                                      _vp, _sz, _vp]),
     "ifk_finalize_workspace": (_sz, [_i64]),
     "ifk_finalize_batched_workspace": (_sz, [_int, _vp]),
     "ifk_finalize_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp,

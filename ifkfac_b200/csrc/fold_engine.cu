@@ -94,18 +94,27 @@ __device__ __forceinline__ long long gtime() {
 #define TR_FLUSH()
 #endif
 
+// A segment of a fold's rows: sub-tiles t0 .. of the fold, row_off rows of the
+// fold before it.
+struct PSeg {
+  const void* X;
+  int64_t ldX;
+  int64_t rows, row_off;
+  int t0;
+  int xkind;
+  int tri;      // row i of the segment is zero left of column i
+  float ident;  // diagonal value when xkind == XK_IDENT
+};
+
 struct PFold {
   float* R;
   int64_t ldR;
-  const void* X;
-  int64_t ldX;
-  int xkind;
-  float ident;  // diagonal value when xkind == XK_IDENT
-  int64_t n, rows, rows_R;
-  int T, K, CB, tri;
+  int64_t n, rows_R;
+  int T, K, CB, nseg;
   int* prog;     // [T][CB]: k < K: panels < k applied to the block's R rows; K + s: own-panel stage s
   int* pflag;    // [T][K]
   uint8_t* img;  // [T][K][PIMG]
+  PSeg seg[MAX_SEGS];
 };
 
 struct PFBatch {
@@ -209,8 +218,8 @@ __device__ __forceinline__ void cta_publish_value(int* flag, int v) {
 }
 __device__ __forceinline__ void cta_publish(int* flag) { cta_publish_value(flag, 1); }
 
-// fp32 value of chunk element (i, j) (rows/cols already bounds-checked)
-__device__ __forceinline__ void load_row32(const PFold& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
+// fp32 values of segment row gi, columns gj .. gj + 31 (rows/cols already bounds-checked)
+__device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
   if (F.xkind == XK_IDENT) {
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = (e < valid && gi == gj + e) ? F.ident : 0.f;
@@ -403,16 +412,20 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(2, cb);
   TR_SET(3, TR_NOW());
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t row0 = (int64_t)t * SUB;
-  const int h = (int)mn<int64_t>(SUB, F.rows - row0);
+  int si = 0;  // segment of sub-tile t
+  while (si + 1 < F.nseg && F.seg[si + 1].t0 <= t) ++si;
+  const PSeg& G = F.seg[si];
+  const int64_t row0 = (int64_t)(t - G.t0) * SUB;  // first row of the sub-tile within its segment
+  const int h = (int)mn<int64_t>(SUB, G.rows - row0);
   const int64_t cs = (int64_t)cb * WB;
   const int wc = (int)mn<int64_t>(WB, F.n - cs);
-  const int64_t lim = mn<int64_t>(F.n, F.rows_R + row0 + h);
-  const int kfirst = F.tri ? (int)(row0 / NB) : 0;
+  // rank bound: the rows folded so far, this sub-tile's included
+  const int64_t lim = mn<int64_t>(F.n, F.rows_R + G.row_off + row0 + h);
+  const int kfirst = G.tri ? (int)(row0 / NB) : 0;
   int* prog = F.prog + (size_t)t * F.CB + cb;
   const int* prev_prog = t > 0 ? F.prog + (size_t)(t - 1) * F.CB + cb : nullptr;
 
-  if (F.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
+  if (G.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
     cta_publish_value(prog, F.K + 3);
     return;
   }
@@ -428,7 +441,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     for (int q = 0; q < WB / 32; ++q) {
       float v[32];
       if (r < h) {
-        load_row32(F, row0 + r, cs + q * 32, wc - q * 32, v);
+        load_row32(G, row0 + r, cs + q * 32, wc - q * 32, v);
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0.f;
@@ -713,84 +726,95 @@ extern "C" __attribute__((visibility("default"))) int ifk_trace_panel_phases(uns
 }
 #endif
 
-size_t pfold_workspace(int nf, const PFoldDesc* d) {
+int64_t pfold_subtiles(const PFoldDesc& d) {
+  int64_t t = 0;
+  for (int s = 0; s < d.nseg; ++s) t += cdiv(d.seg[s].rows, SUB);
+  return t;
+}
+
+int64_t pfold_max_subtiles(int64_t n) { return (int64_t)MAXW - cdiv(n, WB) + 1; }
+
+size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n) {
   size_t b = 256;
   for (int f = 0; f < nf; ++f) {
-    if (d[f].rows <= 0) continue;
-    const int64_t T = cdiv(d[f].rows, SUB), K = cdiv(d[f].n, NB), CB = cdiv(d[f].n, WB);
+    if (subtiles[f] <= 0) continue;
+    const int64_t T = subtiles[f], K = cdiv(n[f], NB), CB = cdiv(n[f], WB);
     b += align256((size_t)T * CB * 4) + align256((size_t)T * K * 4) + (size_t)T * K * PIMG;
   }
   return b;
 }
 
-int64_t pfold_max_rows(int64_t n) { return (int64_t)(MAXW - cdiv(n, WB) + 1) * SUB; }
-
 int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s) {
   const int sms = num_sms();
   if (sms <= 0) return IFK_ERR_CUDA;
-  int first = 0;
-  while (first < nf) {
-    // a group of up to MAX_FOLDS folds shares one launch; groups run one after another
-    // and reuse the workspace from its start
-    PFBatch b;
-    b.nf = 0;
-    b.status = status;
-    b.ctr = (int*)ws;
-    b.abort_ = (int*)ws + 1;
-    int idx[MAX_FOLDS];
-    int q = first;
-    for (; q < nf && b.nf < MAX_FOLDS; ++q)
-      if (d[q].rows > 0) idx[b.nf++] = q;
-    char* w = (char*)ws + 256;
-    int maxw = 0;
-    for (int g = 0; g < b.nf; ++g) {  // flags first, so one memset clears them all
-      const PFoldDesc& D = d[idx[g]];
-      PFold& F = b.f[g];
-      F.R = D.R;
-      F.ldR = D.ldR;
-      F.X = D.X;
-      F.ldX = D.ldX;
-      F.xkind = D.xkind;
-      F.ident = D.ident;
-      F.n = D.n;
-      F.rows = D.rows;
-      F.rows_R = D.rows_R;
-      F.T = (int)cdiv(F.rows, SUB);
-      F.K = (int)cdiv(F.n, NB);
-      F.CB = (int)cdiv(F.n, WB);
-      F.tri = D.tri;
-      if (F.T + F.CB - 1 > MAXW) return IFK_ERR_SHAPE;  // callers split chunks (pfold_max_rows)
-      F.prog = (int*)w;
-      w += align256((size_t)F.T * F.CB * 4);
-      F.pflag = (int*)w;
-      w += align256((size_t)F.T * F.K * 4);
-      maxw = maxw > F.T + F.CB - 1 ? maxw : F.T + F.CB - 1;
+  if (nf > MAX_FOLDS) return IFK_ERR_SHAPE;
+  PFBatch b;
+  b.nf = 0;
+  b.status = status;
+  b.ctr = (int*)ws;
+  b.abort_ = (int*)ws + 1;
+  char* w = (char*)ws + 256;
+  int maxw = 0;
+  for (int q = 0; q < nf; ++q) {  // flags first, so one memset clears them all
+    const PFoldDesc& D = d[q];
+    const int64_t T = pfold_subtiles(D);
+    if (T <= 0) continue;
+    if (D.nseg > MAX_SEGS || T > pfold_max_subtiles(D.n)) return IFK_ERR_SHAPE;  // callers split
+    PFold& F = b.f[b.nf++];
+    F.R = D.R;
+    F.ldR = D.ldR;
+    F.n = D.n;
+    F.rows_R = D.rows_R;
+    F.T = (int)T;
+    F.K = (int)cdiv(F.n, NB);
+    F.CB = (int)cdiv(F.n, WB);
+    F.nseg = 0;
+    int t0 = 0;
+    int64_t off = 0;
+    for (int g = 0; g < D.nseg; ++g) {
+      const PFoldSeg& E = D.seg[g];
+      if (E.rows <= 0) continue;
+      if (E.tri && g + 1 < D.nseg) return IFK_ERR_SHAPE;  // only the last segment may be trapezoidal
+      PSeg& P = F.seg[F.nseg++];
+      P.X = E.X;
+      P.ldX = E.ldX;
+      P.rows = E.rows;
+      P.row_off = off;
+      P.t0 = t0;
+      P.xkind = E.xkind;
+      P.tri = E.tri;
+      P.ident = E.ident;
+      t0 += (int)cdiv(E.rows, SUB);
+      off += E.rows;
     }
-    const size_t flag_bytes = (size_t)(w - (char*)ws);
-    for (int g = 0; g < b.nf; ++g) {
-      b.f[g].img = (uint8_t*)w;
-      w += (size_t)b.f[g].T * b.f[g].K * PIMG;
-    }
-    if (b.nf > 0) {
-      b.nwaves = maxw;
-      int acc = 0;
-      for (int dd = 0; dd < maxw; ++dd) {
-        b.wave_off[dd] = acc;
-        for (int g = 0; g < b.nf; ++g) {
-          const int tlo = dd - b.f[g].CB + 1 > 0 ? dd - b.f[g].CB + 1 : 0;
-          const int thi = dd < b.f[g].T - 1 ? dd : b.f[g].T - 1;
-          if (thi >= tlo) acc += thi - tlo + 1;
-        }
-      }
-      b.wave_off[maxw] = acc;
-      b.ntasks = acc;
-      IFK_CUDA_TRY(cudaMemsetAsync(ws, 0, flag_bytes, s));
-      const int grid = acc < sms ? acc : sms;
-      fold_persistent_kernel<<<grid, TPB, SMEM, s>>>(b);
-      IFK_CUDA_TRY(cudaGetLastError());
-    }
-    first = q;
+    F.prog = (int*)w;
+    w += align256((size_t)F.T * F.CB * 4);
+    F.pflag = (int*)w;
+    w += align256((size_t)F.T * F.K * 4);
+    maxw = maxw > F.T + F.CB - 1 ? maxw : F.T + F.CB - 1;
   }
+  if (b.nf == 0) return IFK_OK;
+  const size_t flag_bytes = (size_t)(w - (char*)ws);
+  for (int g = 0; g < b.nf; ++g) {
+    b.f[g].img = (uint8_t*)w;
+    w += (size_t)b.f[g].T * b.f[g].K * PIMG;
+  }
+  b.nwaves = maxw;
+  int acc = 0;
+  for (int dd = 0; dd < maxw; ++dd) {
+    b.wave_off[dd] = acc;
+    for (int g = 0; g < b.nf; ++g) {
+      const int tlo = dd - b.f[g].CB + 1 > 0 ? dd - b.f[g].CB + 1 : 0;
+      const int thi = dd < b.f[g].T - 1 ? dd : b.f[g].T - 1;
+      if (thi >= tlo) acc += thi - tlo + 1;
+    }
+  }
+  b.wave_off[maxw] = acc;
+  b.ntasks = acc;
+  IFK_CUDA_TRY(cudaMemsetAsync(ws, 0, flag_bytes, s));
+  const int grid = acc < sms ? acc : sms;
+  fold_persistent_kernel<<<grid, TPB, SMEM, s>>>(b);
+  IFK_CUDA_TRY(cudaGetLastError());
   return IFK_OK;
 }
 

@@ -2,6 +2,7 @@
 // Host-side validation happens before anything is queued on the stream.
 #include <algorithm>
 #include <cmath>
+#include <vector>
 
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
@@ -18,45 +19,82 @@ bool prec_ok(int p) { return p == IFK_PREC_AUTO || p == IFK_PREC_FP32 || p == IF
 cudaStream_t S(ifk_stream_t s) { return (cudaStream_t)s; }
 
 size_t wave_ws(int64_t rows, int64_t n) { return align_up(xw_bytes(rows, n)) + align_up(fold_tbuf_bytes(rows)); }
-size_t pers_ws(int64_t rows, int64_t n) {
-  PFoldDesc d{};
-  d.n = n;
-  d.rows = std::min<int64_t>(rows, pfold_max_rows(n));
-  return align_up(pfold_workspace(1, &d));
+// persistent-fold workspace of one fold of `subtiles` sub-tiles (one launch takes at most
+// pfold_max_subtiles of them; longer folds run as several launches over one workspace)
+size_t pers_ws_subtiles(int64_t subtiles, int64_t n) {
+  const int64_t t = std::min<int64_t>(subtiles, pfold_max_subtiles(n));
+  return align_up(pfold_workspace(1, &t, &n));
 }
+size_t pers_ws(int64_t rows, int64_t n) { return pers_ws_subtiles(cdiv(rows, SUB), n); }
 // per-fold workspace: enough for either schedule (fp32 waves or the persistent tensor-core fold)
 size_t fold_ws(int64_t rows, int64_t n) { return std::max(wave_ws(rows, n), pers_ws(rows, n)); }
 
-// Persistent tensor-core folds, splitting chunks taller than one launch allows.
-int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStream_t s) {
-  PFoldDesc d[MAX_FOLDS];
-  int64_t done_rows[MAX_FOLDS] = {};
+size_t elem_bytes(int xkind) { return xkind == 1 ? 2 : 4; }
+
+// Cut a fold into launch pieces of at most pfold_max_subtiles sub-tiles and
+// MAX_SEGS segments; piece i starts from the rows of the pieces before it.
+int plan_pieces(const PFoldDesc& D, const PFoldSeg* segs, int nseg, std::vector<PFoldDesc>& out) {
+  out.clear();
+  const int64_t max_sub = pfold_max_subtiles(D.n);
+  if (max_sub <= 0) return IFK_ERR_SHAPE;
+  PFoldDesc cur = pfold_desc(D.R, D.ldR, D.n, D.rows_R);
+  int64_t cur_sub = 0, done = 0;
+  for (int g = 0; g < nseg; ++g) {
+    const PFoldSeg& E = segs[g];
+    if (E.rows <= 0) continue;
+    if (E.tri && g + 1 < nseg) return IFK_ERR_SHAPE;  // only the last segment may be trapezoidal
+    if (E.tri && cur.nseg > 0 && cdiv(E.rows, SUB) > max_sub - cur_sub) {
+      // a trapezoidal chunk is not split: it starts the next launch
+      out.push_back(cur);
+      cur = pfold_desc(D.R, D.ldR, D.n, std::min<int64_t>(D.n, D.rows_R + done));
+      cur_sub = 0;
+    }
+    int64_t off = 0;
+    while (off < E.rows) {
+      if (cur_sub == max_sub || cur.nseg == MAX_SEGS) {
+        out.push_back(cur);
+        cur = pfold_desc(D.R, D.ldR, D.n, std::min<int64_t>(D.n, D.rows_R + done));
+        cur_sub = 0;
+      }
+      const int64_t take_sub = std::min<int64_t>(max_sub - cur_sub, cdiv(E.rows - off, SUB));
+      const int64_t take = std::min<int64_t>(take_sub * SUB, E.rows - off);
+      if (E.tri && take < E.rows) return IFK_ERR_SHAPE;  // trapezoidal chunks come in one piece
+      const void* X = E.xkind == 2 ? E.X : (const void*)((const char*)E.X + off * E.ldX * elem_bytes(E.xkind));
+      pfold_add(cur, X, E.ldX, take, E.xkind, E.ident, E.tri);
+      cur_sub += take_sub;
+      off += take;
+      done += take;
+    }
+  }
+  if (cur.nseg > 0) out.push_back(cur);
+  return IFK_OK;
+}
+
+// Persistent tensor-core folds: groups of MAX_FOLDS folds share launches; a fold
+// longer than one launch allows continues in the group's next launch.  Fold f
+// takes its segments from segs[f] (nsegs[f] of them) when segs is given, else
+// from in[f].seg.
+int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStream_t s,
+                   const PFoldSeg* const* segs = nullptr, const int* nsegs = nullptr) {
+  std::vector<PFoldDesc> pieces[MAX_FOLDS];
   for (int base = 0; base < nf; base += MAX_FOLDS) {
     const int cnt = std::min(MAX_FOLDS, nf - base);
-    for (;;) {
-      bool any = false;
-      for (int q = 0; q < cnt; ++q) {
-        const PFoldDesc& D = in[base + q];
-        d[q] = D;
-        const int64_t left = D.rows - done_rows[q];
-        const int64_t take = std::min<int64_t>(left, pfold_max_rows(D.n));
-        d[q].rows = take > 0 ? take : 0;
-        if (take > 0) {
-          any = true;
-          d[q].rows_R = std::min<int64_t>(D.n, D.rows_R + done_rows[q]);
-          if (D.xkind == 1)
-            d[q].X = (const char*)D.X + done_rows[q] * D.ldX * 2;
-          else if (D.xkind == 0)
-            d[q].X = (const char*)D.X + done_rows[q] * D.ldX * 4;
-          if (D.tri && done_rows[q] > 0) return IFK_ERR_SHAPE;  // trapezoidal chunks come in one piece
-          done_rows[q] += take;
-        }
-      }
-      if (!any) break;
-      const int rc = pfold_run(cnt, d, ws, status, s);
+    size_t most = 0;
+    for (int q = 0; q < cnt; ++q) {
+      const PFoldDesc& D = in[base + q];
+      const int rc = segs ? plan_pieces(D, segs[base + q], nsegs[base + q], pieces[q])
+                          : plan_pieces(D, D.seg, D.nseg, pieces[q]);
+      if (rc != IFK_OK) return rc;
+      most = std::max(most, pieces[q].size());
+    }
+    for (size_t i = 0; i < most; ++i) {
+      PFoldDesc d[MAX_FOLDS];
+      int m = 0;
+      for (int q = 0; q < cnt; ++q)
+        if (i < pieces[q].size()) d[m++] = pieces[q][i];
+      const int rc = pfold_run(m, d, ws, status, s);
       if (rc != IFK_OK) return rc;
     }
-    for (int q = 0; q < cnt; ++q) done_rows[q] = 0;
   }
   return IFK_OK;
 }
@@ -112,8 +150,9 @@ int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int6
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   if (prec == IFK_PREC_BF16) {
-    PFoldDesc d{R, ldR, chunk, ld_chunk, chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, n, rows, rows_R,
-                (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0};
+    PFoldDesc d = pfold_desc(R, ldR, n, rows_R);
+    pfold_add(d, chunk, ld_chunk, rows, chunk_dtype == IFK_BF16 ? 1 : 0, 0.f,
+              (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0);
     return run_persistent(1, &d, workspace, d_status, S(stream));
   }
   FoldArgs a;
@@ -167,8 +206,9 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
     int cnt = 0;
     for (int f = 0; f < nfolds; ++f) {
       if (rows[f] == 0) continue;
-      d[cnt++] = PFoldDesc{R[f], ldR[f], chunk[f], ld_chunk[f], chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, n[f],
-                           rows[f], rows_R[f], (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0};
+      d[cnt] = pfold_desc(R[f], ldR[f], n[f], rows_R[f]);
+      pfold_add(d[cnt++], chunk[f], ld_chunk[f], rows[f], chunk_dtype == IFK_BF16 ? 1 : 0, 0.f,
+                (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0);
       if (cnt == MAX_FOLDS) {
         const int rc = run_persistent(cnt, d, workspace, d_status, s);
         if (rc != IFK_OK) return rc;
@@ -207,6 +247,127 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
   return fold_run_batch(b, prec, s);
 }
 
+// fp32 wave fold of one chunk (copied into the workspace) or of ident * I when chunk is null
+static int fold_fp32(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int64_t ld_chunk,
+                     int64_t rows, int64_t n, int chunk_dtype, int tri, float ident, int prec,
+                     int* d_status, void* workspace, cudaStream_t s) {
+  FoldArgs a;
+  a.R = R;
+  a.ldR = ldR;
+  a.X = (float*)workspace;
+  a.ldX = xw_ld(n);
+  a.Tb = (float*)((char*)workspace + align_up(xw_bytes(rows, n)));
+  a.n = n;
+  a.rows = rows;
+  a.rows_R = rows_R;
+  a.tiles = (int)cdiv(rows, SUB);
+  a.K = (int)cdiv(n, NB);
+  a.tri = tri;
+  a.err = d_status;
+  const int rc = chunk ? copy_chunk(a.X, a.ldX, chunk, ld_chunk, rows, n, chunk_dtype, s)
+                       : fill_scaled_identity(a.X, a.ldX, n, ident, s);
+  if (rc != IFK_OK) return rc;
+  return fold_run(a, prec, s);
+}
+
+static int64_t seg_base(int f, const int* nseg) {
+  int64_t b = 0;
+  for (int g = 0; g < f; ++g) b += nseg[g];
+  return b;
+}
+
+size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
+                                        const int64_t* seg_rows, const double* ident_tail) {
+  if (nfolds <= 0 || !n || !nseg || !seg_rows) return 0;
+  size_t b = 0;
+  for (int f = 0; f < nfolds; ++f) {
+    if (n[f] <= 0 || nseg[f] < 0) return 0;
+    const int64_t base = seg_base(f, nseg);
+    int64_t sub = 0, most = 0;
+    for (int g = 0; g < nseg[f]; ++g) {
+      sub += cdiv(std::max<int64_t>(seg_rows[base + g], 0), SUB);
+      most = std::max(most, seg_rows[base + g]);
+    }
+    if (ident_tail && ident_tail[f] > 0) {
+      sub += cdiv(n[f], SUB);
+      most = std::max(most, n[f]);
+    }
+    if (sub > 0) b += std::max(pers_ws_subtiles(sub, n[f]), wave_ws(std::max<int64_t>(most, 1), n[f]));
+  }
+  return b;
+}
+
+int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, const int64_t* rows_R,
+                           const int64_t* n, const int* nseg, const void* const* seg_chunk,
+                           const int64_t* seg_ld, const int64_t* seg_rows, int chunk_dtype,
+                           const double* ident_tail, int prec, int* d_status, void* workspace,
+                           size_t workspace_bytes, ifk_stream_t stream) {
+  if (nfolds < 0 || (nfolds > 0 && (!R || !ldR || !rows_R || !n || !nseg || !seg_chunk || !seg_ld ||
+                                    !seg_rows)))
+    return IFK_ERR_ARG;
+  if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec)) return IFK_ERR_ARG;
+  bool any = false;
+  for (int f = 0; f < nfolds; ++f) {
+    if (!R[f] || nseg[f] < 0) return IFK_ERR_ARG;
+    if (n[f] <= 0 || rows_R[f] < 0 || rows_R[f] > n[f] || ldR[f] < n[f]) return IFK_ERR_SHAPE;
+    if (ident_tail && !(ident_tail[f] >= 0)) return IFK_ERR_ARG;
+    const int64_t base = seg_base(f, nseg);
+    for (int g = 0; g < nseg[f]; ++g) {
+      const int64_t r = seg_rows[base + g];
+      if (r < 0 || (r > 0 && seg_ld[base + g] < n[f])) return IFK_ERR_SHAPE;
+      if (r > 0 && !seg_chunk[base + g]) return IFK_ERR_ARG;
+      any = any || r > 0;
+    }
+    any = any || (ident_tail && ident_tail[f] > 0);
+  }
+  if (!any) return IFK_OK;
+  if (!workspace || !aligned(workspace) ||
+      workspace_bytes < ifk_tsqr_fold_segments_workspace(nfolds, n, nseg, seg_rows, ident_tail))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  if (prec == IFK_PREC_BF16) {
+    std::vector<PFoldDesc> d((size_t)nfolds);
+    std::vector<std::vector<PFoldSeg>> segs((size_t)nfolds);
+    std::vector<const PFoldSeg*> sp((size_t)nfolds);
+    std::vector<int> ns((size_t)nfolds);
+    for (int f = 0; f < nfolds; ++f) {
+      d[f] = pfold_desc(R[f], ldR[f], n[f], rows_R[f]);
+      const int64_t base = seg_base(f, nseg);
+      for (int g = 0; g < nseg[f]; ++g)
+        if (seg_rows[base + g] > 0)
+          segs[f].push_back(PFoldSeg{seg_chunk[base + g], seg_ld[base + g], seg_rows[base + g],
+                                     chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, 0});
+      if (ident_tail && ident_tail[f] > 0)
+        segs[f].push_back(PFoldSeg{nullptr, 0, n[f], 2, (float)ident_tail[f], 1});
+      sp[f] = segs[f].data();
+      ns[f] = (int)segs[f].size();
+    }
+    // folds without rows are dropped by the launcher
+    return run_persistent(nfolds, d.data(), workspace, d_status, s, sp.data(), ns.data());
+  }
+  // fp32 mode: the segments of each fold one after another through the wave schedule
+  for (int f = 0; f < nfolds; ++f) {
+    int64_t rr = rows_R[f];
+    const int64_t base = seg_base(f, nseg);
+    for (int g = 0; g < nseg[f]; ++g) {
+      const int64_t r = seg_rows[base + g];
+      if (r == 0) continue;
+      const int rc = fold_fp32(R[f], ldR[f], rr, seg_chunk[base + g], seg_ld[base + g], r, n[f], chunk_dtype,
+                               0, 0.f, prec, d_status, workspace, s);
+      if (rc != IFK_OK) return rc;
+      rr = std::min<int64_t>(n[f], rr + r);
+    }
+    if (ident_tail && ident_tail[f] > 0) {
+      const int rc = fold_fp32(R[f], ldR[f], rr, nullptr, 0, n[f], n[f], IFK_F32, 1, (float)ident_tail[f], prec,
+                               d_status, workspace, s);
+      if (rc != IFK_OK) return rc;
+    }
+  }
+  return IFK_OK;
+}
+
 size_t ifk_finalize_workspace(int64_t n) {
   if (n <= 0) return 0;
   return align_up((size_t)n * xw_ld(n) * sizeof(float)) + fold_ws(n, n);
@@ -230,7 +391,8 @@ int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, doub
   int rc = scale_upper(Rf, ldF, R_in, ldR, n, (float)std::sqrt(rows_total), s);
   if (rc != IFK_OK) return rc;
   if (damping > 0 && prec == IFK_PREC_BF16) {
-    PFoldDesc d{Rf, ldF, nullptr, 0, 2, (float)std::sqrt(damping), n, n, n, 1};
+    PFoldDesc d = pfold_desc(Rf, ldF, n, n);
+    pfold_add(d, nullptr, 0, n, 2, (float)std::sqrt(damping), 1);
     rc = run_persistent(1, &d, fws, d_status, s);
     if (rc != IFK_OK) return rc;
   } else if (damping > 0) {
@@ -301,7 +463,8 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
         PFoldDesc pd[MAX_FOLDS];
         for (int q = 0; q < cnt; ++q) {
           const int f = base + q;
-          pd[q] = PFoldDesc{Rf[q], xw_ld(n[f]), nullptr, 0, 2, (float)std::sqrt(damping), n[f], n[f], n[f], 1};
+          pd[q] = pfold_desc(Rf[q], xw_ld(n[f]), n[f], n[f]);
+          pfold_add(pd[q], nullptr, 0, n[f], 2, (float)std::sqrt(damping), 1);
         }
         rc = run_persistent(cnt, pd, ws, d_status, s);
       } else {

@@ -35,20 +35,45 @@ size_t fold_tbuf_bytes(int64_t rows);
 size_t xw_bytes(int64_t rows, int64_t n);
 int64_t xw_ld(int64_t n);
 
-// One fold of the persistent tensor-core path (fold_engine.cu): the chunk is
-// read in place (fp32, bf16, or generated as ident * I for the damping fold).
+// One fold of the persistent tensor-core path (fold_engine.cu).  Its rows come
+// in up to MAX_SEGS segments that are folded in order, with the result of
+// folding them one after another: a chunk read in place (fp32 or bf16), or
+// ident * I (n rows, the damping rows).  Only the last segment may be
+// trapezoidal (row i zero left of column i).
+constexpr int MAX_SEGS = 12;
+struct PFoldSeg {
+  const void* X;
+  int64_t ldX;
+  int64_t rows;
+  int xkind;     // 0 fp32, 1 bf16, 2 ident * I (X unused)
+  float ident;
+  int tri;
+};
 struct PFoldDesc {
   float* R;
   int64_t ldR;
-  const void* X;
-  int64_t ldX;
-  int xkind;     // 0 fp32, 1 bf16, 2 ident * I (X unused)
-  float ident;
-  int64_t n, rows, rows_R;
-  int tri;
+  int64_t n, rows_R;
+  int nseg;
+  PFoldSeg seg[MAX_SEGS];
 };
-size_t pfold_workspace(int nf, const PFoldDesc* d);
-int64_t pfold_max_rows(int64_t n);
+inline PFoldDesc pfold_desc(float* R, int64_t ldR, int64_t n, int64_t rows_R) {
+  PFoldDesc d{};
+  d.R = R;
+  d.ldR = ldR;
+  d.n = n;
+  d.rows_R = rows_R;
+  return d;
+}
+inline void pfold_add(PFoldDesc& d, const void* X, int64_t ldX, int64_t rows, int xkind, float ident, int tri) {
+  d.seg[d.nseg++] = PFoldSeg{X, ldX, rows, xkind, ident, tri};
+}
+// sub-tiles of a fold (sum over its segments)
+int64_t pfold_subtiles(const PFoldDesc& d);
+// most sub-tiles one launch takes for a fold of n columns
+int64_t pfold_max_subtiles(int64_t n);
+// workspace of one launch over folds of the given sub-tile counts and widths
+size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n);
+// one launch; every fold must have at most pfold_max_subtiles sub-tiles
 int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s);
 
 // chunk (bf16 or fp32, rows x n) -> X fp32

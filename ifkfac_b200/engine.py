@@ -11,6 +11,7 @@ reference's hooks (``_n_rows_X`` / ``_n_rows_G``, ifkfac/activation_hooks.py:205
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -39,6 +40,7 @@ class Factor:
         self.R = torch.zeros(n, n, dtype=torch.float32, device=self.device)
         self.rows_R = 0
         self.rows_seen = 0
+        self.consumed = False  # R holds a damped factor (fused refresh) until clear()
         self.ws = _ws(_lib.lib().ifk_tsqr_fold_workspace(max(chunk_rows, 1), n), self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -51,6 +53,8 @@ class Factor:
         """R <- R of [R; chunk] (streaming_tsqr_update, ifkfac/triangular.py:246-307)."""
         if chunk.dim() != 2 or chunk.shape[1] != self.n:
             raise ValueError(f"chunk of shape {tuple(chunk.shape)} for a factor of width {self.n}")
+        if self.consumed:
+            raise RuntimeError("factor was consumed by a fused refresh; clear() it first")
         if chunk.stride(1) != 1:
             chunk = chunk.contiguous()
         p = chunk.shape[0]
@@ -69,6 +73,7 @@ class Factor:
         self.R.zero_()
         self.rows_R = 0
         self.rows_seen = 0
+        self.consumed = False
 
 
 def _arr(ctype, vals):
@@ -85,6 +90,8 @@ def fold_batched(factors: Sequence[Factor], chunks: Sequence[torch.Tensor], ws: 
     for f, c in zip(factors, chunks):
         if c.dim() != 2 or c.shape[1] != f.n:
             raise ValueError(f"chunk of shape {tuple(c.shape)} for a factor of width {f.n}")
+        if f.consumed:
+            raise RuntimeError("factor was consumed by a fused refresh; clear() it first")
         cs.append(c if c.stride(1) == 1 else c.contiguous())
     dts = {c.dtype for c in cs}
     if len(dts) != 1:
@@ -107,31 +114,68 @@ def fold_batched(factors: Sequence[Factor], chunks: Sequence[torch.Tensor], ws: 
     return ws
 
 
-def _rows_view(chunks: Sequence[torch.Tensor]) -> torch.Tensor:
-    """The chunks stacked by rows: a view when they are consecutive row slices of
-    one tensor (no copy), else a concatenation."""
-    c0 = chunks[0]
-    if len(chunks) == 1:
-        return c0
-    es, rs = c0.element_size(), c0.stride(0)
-    adjacent = all(c.dtype == c0.dtype and c.shape[1] == c0.shape[1] and c.stride() == c0.stride()
-                   and c.stride(1) == 1 and c.untyped_storage().data_ptr() == c0.untyped_storage().data_ptr()
-                   for c in chunks)
-    for a, b in zip(chunks, chunks[1:]):
-        adjacent = adjacent and b.data_ptr() == a.data_ptr() + a.shape[0] * rs * es
-    if adjacent:
-        return torch.as_strided(c0, (sum(c.shape[0] for c in chunks), c0.shape[1]), c0.stride())
-    return torch.cat(list(chunks), 0)
+def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence[torch.Tensor]], ws: torch.Tensor,
+                  ident_tail: Optional[Sequence[float]] = None) -> torch.Tensor:
+    """Fold the chunks segments[i] into factors[i] in order, without concatenating
+    them: one persistent launch where they fit (ifk_tsqr_fold_segments), with the
+    result of folding them one after another.  ident_tail[i] > 0 appends the rows
+    ident_tail[i] * I (damping rows at the caller's scale); the factor then holds a
+    damped factor and is marked consumed until clear().
+
+    Returns the workspace actually used (grown if ``ws`` was too small)."""
+    L = _lib.lib()
+    segs, dts = [], set()
+    for f, chunks in zip(factors, segments):
+        if f.consumed:
+            raise RuntimeError("factor was consumed by a fused refresh; clear() it first")
+        cs = []
+        for c in chunks:
+            if c.dim() != 2 or c.shape[1] != f.n:
+                raise ValueError(f"chunk of shape {tuple(c.shape)} for a factor of width {f.n}")
+            if c.shape[0] == 0:
+                continue
+            cs.append(c if c.stride(1) == 1 else c.contiguous())
+            dts.add(cs[-1].dtype)
+        segs.append(cs)
+    if len(dts) > 1:
+        raise TypeError("all chunks of a segmented fold must share one dtype")
+    dt = _DT[dts.pop()] if dts else _lib.BF16
+    nf = len(factors)
+    flat = [c for cs in segs for c in cs]
+    ns = _arr(ctypes.c_int64, [f.n for f in factors])
+    nseg = _arr(ctypes.c_int, [len(cs) for cs in segs])
+    rows = _arr(ctypes.c_int64, [c.shape[0] for c in flat] or [0])
+    tail = _arr(ctypes.c_double, [float(v) for v in ident_tail]) if ident_tail is not None else None
+    need = L.ifk_tsqr_fold_segments_workspace(nf, ns, nseg, rows, tail)
+    if need == 0 and (flat or ident_tail):
+        raise ValueError("ifk_tsqr_fold_segments_workspace rejected the shapes")
+    if ws is None or ws.numel() < need:
+        ws = _ws(need, factors[0].device)
+    check(L.ifk_tsqr_fold_segments(
+        nf, _arr(ctypes.c_void_p, [f.R.data_ptr() for f in factors]), ns,
+        _arr(ctypes.c_int64, [f.rows_R for f in factors]), ns, nseg,
+        _arr(ctypes.c_void_p, [c.data_ptr() for c in flat] or [None]),
+        _arr(ctypes.c_int64, [c.stride(0) for c in flat] or [0]), rows, dt, tail, factors[0].prec,
+        factors[0].status.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "ifk_tsqr_fold_segments")
+    for i, (f, cs) in enumerate(zip(factors, segs)):
+        p = sum(c.shape[0] for c in cs)
+        f.rows_R = min(f.n, f.rows_R + p)
+        f.rows_seen += p
+        if ident_tail is not None and ident_tail[i] > 0:
+            f.consumed = True
+    return ws
 
 
 class LayerCurvature:
     """Device state of one layer's curvature path (factors, natgrad, momentum).
 
     ``window`` > 1 defers folding like the reference's deferred hook mode
-    (``ifkfac/activation_hooks.py:347-364``): chunks are kept (by reference; the
-    caller keeps them alive) until ``window`` of them are pending or the factors
-    are refreshed, then folded as one chunk of all their rows, so one persistent
-    launch covers several tiles."""
+    (``ifkfac/activation_hooks.py:347-364, 560-570``): chunks are kept (by
+    reference; the caller keeps them alive) and folded ``window`` at a time in
+    one persistent launch, in arrival order.  A full window is folded when the
+    next chunk arrives or at the refresh, so the last one can share its launch
+    with the damping rows (``refresh(consume=True)``); the factors are those of
+    folding each chunk as it arrives."""
 
     def __init__(self, n_in: int, n_out: int, device, prec: int = _lib.PREC_AUTO,
                  factor_dtype: torch.dtype = torch.float32, chunk_rows: int = 0, window: int = 1):
@@ -156,9 +200,11 @@ class LayerCurvature:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.fx.status = self.status
         self.fg.status = self.status
-        rows = max(chunk_rows, 1) * self.window
-        self.ws_pair = _ws(L.ifk_tsqr_fold_batched_workspace(
-            2, _arr(ctypes.c_int64, [rows, rows]), _arr(ctypes.c_int64, [n_in, n_out])), self.device)
+        # fold workspace of a full window (with the damping rows of a fused refresh)
+        rows = [max(chunk_rows, 1)] * self.window
+        self.ws_pair = _ws(L.ifk_tsqr_fold_segments_workspace(
+            2, _arr(ctypes.c_int64, [n_in, n_out]), _arr(ctypes.c_int, [self.window] * 2),
+            _arr(ctypes.c_int64, rows * 2), _arr(ctypes.c_double, [1.0, 1.0])), self.device)
 
     def fold(self, x_chunk: torch.Tensor, g_chunk: torch.Tensor) -> None:
         """Fold an activation chunk into R_X and a gradient chunk into R_G together
@@ -166,33 +212,51 @@ class LayerCurvature:
         if self.window <= 1:
             self.ws_pair = fold_batched((self.fx, self.fg), (x_chunk, g_chunk), self.ws_pair)
             return
-        self._pending.append((x_chunk, g_chunk))
+        if self.fx.consumed:
+            raise RuntimeError("factor was consumed by a fused refresh; clear() it first")
         if len(self._pending) >= self.window:
             self.flush()
+        self._pending.append((x_chunk, g_chunk))
 
     def flush(self) -> None:
-        """Fold the pending chunks (deferred mode) as one chunk per factor."""
+        """Fold the pending chunks (deferred mode): all of them in one launch per
+        factor pair, in arrival order, without concatenating them."""
         if not self._pending:
             return
-        x = _rows_view([x for x, _ in self._pending])
-        g = _rows_view([g for _, g in self._pending])
+        segs = ([x for x, _ in self._pending], [g for _, g in self._pending])
         self._pending = []
-        self.ws_pair = fold_batched((self.fx, self.fg), (x, g), self.ws_pair)
+        self.ws_pair = fold_segments((self.fx, self.fg), segs, self.ws_pair)
 
     # ---- factor refresh: get_factors + _update_factors (finite check, dtype) ----
-    def refresh(self, damping: float, solve_prec: Optional[int] = None) -> bool:
+    def refresh(self, damping: float, solve_prec: Optional[int] = None, consume: bool = False) -> bool:
         """Damped factors from the running R's; False (nothing queued) while either is
-        still trapezoidal, the reference's per-layer skip (ifkfac/activation_hooks.py:287-300)."""
-        self.flush()
+        still trapezoidal, the reference's per-layer skip (ifkfac/activation_hooks.py:287-300).
+
+        consume=True is for a caller that clears the running factors after the
+        refresh (the optimizer does after a successful get_factors,
+        ifkfac/ifkfac.py:224-227): the
+        pending chunks and the damping rows sqrt(damping * p) I are folded in the
+        same launch into the running factors, which are then only good for clear();
+        the damped factor is the result scaled by 1 / sqrt(p)."""
+        fs, outs = (self.fx, self.fg), (self.RX, self.RG)
+        pend = [sum(c.shape[0] for c in cs) for cs in zip(*self._pending)] if self._pending else [0, 0]
+        square = all(min(f.n, f.rows_R + p) >= f.n for f, p in zip(fs, pend))
+        fused = consume and damping > 0 and square
+        if fused:
+            segs = ([x for x, _ in self._pending], [g for _, g in self._pending])
+            self._pending = []
+            tails = [math.sqrt(damping * float(f.rows_seen + p)) for f, p in zip(fs, pend)]
+            self.ws_pair = fold_segments(fs, segs, self.ws_pair, ident_tail=tails)
+        else:
+            self.flush()
         if self.fx.rows_R < self.n_in or self.fg.rows_R < self.n_out:
             return False
         L = _lib.lib()
         prec = self.prec if solve_prec is None else solve_prec
-        fs, outs = (self.fx, self.fg), (self.RX, self.RG)
         check(L.ifk_finalize_batched(
             2, _arr(ctypes.c_void_p, [f.R.data_ptr() for f in fs]), _arr(ctypes.c_int64, [f.n for f in fs]),
             _arr(ctypes.c_int64, [f.rows_R for f in fs]), _arr(ctypes.c_int64, [f.n for f in fs]),
-            _arr(ctypes.c_double, [float(f.rows_seen) for f in fs]), float(damping),
+            _arr(ctypes.c_double, [float(f.rows_seen) for f in fs]), 0.0 if fused else float(damping),
             _arr(ctypes.c_void_p, [o.data_ptr() for o in outs]), _arr(ctypes.c_int64, [f.n for f in fs]),
             _DT[self.factor_dtype], prec, self.status.data_ptr(), self.ws_fin.data_ptr(),
             self.ws_fin.numel(), _stream()), "ifk_finalize_batched")

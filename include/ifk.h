@@ -128,6 +128,38 @@ IFK_API int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ld
                           int chunk_dtype, int prec, int flags, int* d_status,
                           void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
+/* Workspace bytes for ifk_tsqr_fold_segments (same arguments). */
+IFK_API size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
+                                                const int64_t* seg_rows, const double* ident_tail);
+
+/*
+ * Fold a sequence of chunks ("segments") into each of nfolds factors, in
+ * order, in one persistent launch where they fit (IFK_PREC_BF16): the result
+ * is that of one ifk_tsqr_fold per segment in turn, with the same reflector
+ * sequence (one sub-tile of rows after another), while the fold of segment
+ * s + 1 overlaps that of segment s.  Fold f has nseg[f] segments; segment
+ * arrays are flat, fold after fold.  Segment g is seg_rows[g] rows of
+ * seg_chunk[g] (n[f] columns, leading dimension seg_ld[g], element type
+ * chunk_dtype); the segments need not be adjacent in memory.  When
+ * ident_tail is not NULL and ident_tail[f] > 0, n[f] more rows
+ * ident_tail[f] * I follow the segments (the damping rows of ifk_finalize at
+ * the caller's scale: a caller that then runs ifk_finalize with damping 0
+ * and rows_total p gets the damped factor of lambda = ident_tail^2 / p).
+ * R[f], ldR[f], rows_R[f] are as in ifk_tsqr_fold.
+ *
+ * Replaces the deferred drain of the hooks, which concatenates the buffered
+ * chunks and folds them with one streaming_tsqr_update
+ * (ifkfac/activation_hooks.py:347-364, 560-570, 627-635), without the
+ * concatenation; and a run of streaming_tsqr_update calls over row tiles that
+ * are all resident (ifkfac/triangular.py:246-307).
+ */
+IFK_API int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR,
+                                   const int64_t* rows_R, const int64_t* n, const int* nseg,
+                                   const void* const* seg_chunk, const int64_t* seg_ld,
+                                   const int64_t* seg_rows, int chunk_dtype,
+                                   const double* ident_tail, int prec, int* d_status,
+                                   void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
 /* ---- damping fold ------------------------------------------------------ */
 
 /* Workspace bytes for ifk_finalize on an n x n factor. */

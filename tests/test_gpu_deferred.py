@@ -1,5 +1,6 @@
 """Deferred folding (window > 1, the reference's deferred hook mode): tiles kept
-and folded as one chunk give the factors of the streaming folds.  Both are held
+and folded in one launch (ifk_tsqr_fold_segments) give the factors of the
+streaming folds.  Both are held
 to the fp64 damped factor of all rows; the deferred schedule must be as
 accurate as the streaming one (fp32 mode to 2e-5, bf16 mode within the bf16
 mode's own error)."""
@@ -11,17 +12,9 @@ import torch
 
 from oracle import ifk_oracle as ora
 from ifkfac_b200 import _lib
-from ifkfac_b200.engine import LayerCurvature, _rows_view
+from ifkfac_b200.engine import LayerCurvature
 
 pytestmark = pytest.mark.gpu
-
-
-def test_rows_view_is_a_view_for_adjacent_slices():
-    X = torch.randn(10, 4, device="cuda")
-    v = _rows_view([X[0:3], X[3:7], X[7:10]])
-    assert v.data_ptr() == X.data_ptr() and v.shape == (10, 4)
-    c = _rows_view([X[0:3], X[5:7]])  # not adjacent: a copy
-    assert c.shape == (5, 4) and torch.equal(c, torch.cat([X[0:3], X[5:7]]))
 
 
 @pytest.mark.parametrize("prec,tol", [(_lib.PREC_FP32, 2e-5), (_lib.PREC_BF16, 2e-2)])
