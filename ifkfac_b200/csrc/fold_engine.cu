@@ -36,6 +36,26 @@ constexpr int WB = 128;   // columns of a task
 constexpr int TPB = 256;  // 8 warps; warps w and w + 4 share TMEM lanes 32(w%4)..+31
 static_assert(TPB == panel::PT2, "the persistent fold runs the panel with all its threads");
 constexpr int MAXW = 384; // waves per launch
+// Ticket order: wave d = t + CBW * cb (then by fold and t).  Any positive
+// weights give a topological order of the dependencies; weighting the column
+// block more hands out the tasks that have many panels to apply (right-hand
+// blocks) before the tasks of later sub-tiles that could only wait.
+#ifndef IFK_FOLD_CBW
+#define IFK_FOLD_CBW 2
+#endif
+constexpr int CBW = IFK_FOLD_CBW;
+
+// The sub-tiles t of wave d for a fold of T sub-tiles and CB column blocks:
+// t = tlo, tlo + CBW, ... (cnt of them), column block (d - t) / CBW.
+__host__ __device__ __forceinline__ void wave_range(int d, int T, int CB, int* tlo, int* cnt) {
+  int lo = d - CBW * (CB - 1);
+  if (lo < 0) lo = 0;
+  lo += (d - lo) % CBW;
+  const int hi = d < T - 1 ? d : T - 1;
+  *tlo = lo;
+  *cnt = hi >= lo ? (hi - lo) / CBW + 1 : 0;
+}
+__host__ __device__ __forceinline__ int num_waves(int T, int CB) { return T + CBW * (CB - 1); }
 using panel::LDP;
 using panel::PanelSmem;
 
@@ -44,20 +64,29 @@ constexpr uint32_t YIMG = SUB * NB * 2;
 constexpr uint32_t TIMG = NB * NB * 2;
 constexpr uint32_t PIMG = YIMG + 2 * TIMG;
 
-// shared memory: a union of the apply operands and the panel workspace, then the images
+// Shared memory: a union of the apply operands and the panel workspace, then
+// image buffer 0.  The apply phase uses two image buffers (panel k's images in
+// one while panel k + 1's arrive in the other by a bulk copy) and a staging
+// area for the next panel's R rows; the panel phase builds its own images in
+// buffer 0.
 constexpr uint32_t SZ_A1 = WB * SUB * 2;     // X^T bf16, MN-major (mn = column c, k = row i)
 constexpr uint32_t SZ_A2 = WB * NB * 2;      // W^T hi / lo, K-major (mn = c, k = j)
 constexpr uint32_t OFF_A1 = 0;
 constexpr uint32_t OFF_A2H = OFF_A1 + SZ_A1;
 constexpr uint32_t OFF_A2L = OFF_A2H + SZ_A2;
-constexpr uint32_t OFF_B3 = OFF_A2L + SZ_A2;  // W2 bf16, K-major (mn = c, k = j)
-constexpr uint32_t APPLY_END = OFF_B3 + SZ_A2;
+constexpr uint32_t OFF_B3 = OFF_A2H;          // W2 bf16, K-major: over W^T hi once GEMM2 has completed
+constexpr uint32_t OFF_IMG1 = OFF_A2L + SZ_A2;                 // image buffer 1 (apply phase)
+constexpr uint32_t OFF_RN = OFF_IMG1 + PIMG;                   // next panel's R rows, fp32 [j][column]
+constexpr uint32_t SZ_RN = NB * WB * 4;
+constexpr uint32_t APPLY_END = OFF_RN + SZ_RN;
 constexpr uint32_t UNION = ((sizeof(PanelSmem) > APPLY_END ? sizeof(PanelSmem) : APPLY_END) + 1023) / 1024 * 1024;
-constexpr uint32_t OFF_Y = UNION;             // Y image: B of GEMM1 (MN-major), A of GEMM3 (K-major)
-constexpr uint32_t OFF_TH = OFF_Y + YIMG;     // T hi / lo images, K-major (mn = j, k = l)
-constexpr uint32_t OFF_TL = OFF_TH + TIMG;
-constexpr uint32_t OFF_BAR = OFF_TL + TIMG;
+constexpr uint32_t OFF_IMG0 = UNION;          // image buffer 0: Y (B of GEMM1, MN-major; A of GEMM3, K-major),
+constexpr uint32_t IMG_TH = YIMG;             //   then T hi / lo, K-major (mn = j, k = l)
+constexpr uint32_t IMG_TL = YIMG + TIMG;
+constexpr uint32_t OFF_BAR = OFF_IMG0 + PIMG;
 constexpr uint32_t SMEM = OFF_BAR + 64;
+static_assert(SMEM <= 227 * 1024, "shared memory of one CTA");
+static_assert(OFF_IMG1 % 1024 == 0 && OFF_IMG0 % 1024 == 0 && PIMG % 16 == 0, "bulk copy alignment");
 
 constexpr uint32_t A1_MN = 128, A1_K = (WB / 8) * 128;  // 128, 2048
 constexpr uint32_t Y_I = 1024, Y_J = 128;
@@ -68,15 +97,16 @@ constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
 enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2 };
 
 #ifdef IFK_TRACE
-// Diagnostic build only: per-task timestamps (globaltimer, ns), 16 int64 per task.
-__device__ long long g_trace[1 << 18];
+// Diagnostic build only: per-task timestamps (globaltimer, ns), 24 int64 per task.
+constexpr int TRN = 24;
+__device__ long long g_trace[(1 << 14) * TRN];
 __device__ int g_trace_n;
 __device__ __forceinline__ long long gtime() {
   long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-#define TR_DECL long long tr[16] = {};
+#define TR_DECL long long tr[TRN] = {};
 #define TR_SET(i, v) tr[i] = (v)
 #define TR_ADD(i, v) tr[i] += (v)
 #define TR_NOW() gtime()
@@ -84,7 +114,7 @@ __device__ __forceinline__ long long gtime() {
   if (threadIdx.x == 0) {                                              \
     const int slot = atomicAdd(&g_trace_n, 1);                         \
     if (slot < (1 << 14))                                              \
-      for (int q_ = 0; q_ < 16; ++q_) g_trace[slot * 16 + q_] = tr[q_]; \
+      for (int q_ = 0; q_ < TRN; ++q_) g_trace[slot * TRN + q_] = tr[q_]; \
   }
 #else
 #define TR_DECL
@@ -92,6 +122,24 @@ __device__ __forceinline__ long long gtime() {
 #define TR_ADD(i, v)
 #define TR_NOW() 0
 #define TR_FLUSH()
+#endif
+
+#ifdef IFK_TRACE
+// Diagnostic build only: time (ns) of the phases of the applies, summed over all
+// applies by thread 0 of each CTA; slot 8 counts applies.
+__device__ unsigned long long g_apply_phase[16];
+#define AP_DECL long long ap_last = gtime();
+#define AP_MARK(i)                                                      \
+  do {                                                                  \
+    if (threadIdx.x == 0) {                                             \
+      const long long t_ = gtime();                                     \
+      atomicAdd(&g_apply_phase[i], (unsigned long long)(t_ - ap_last)); \
+      ap_last = t_;                                                     \
+    }                                                                   \
+  } while (0)
+#else
+#define AP_DECL
+#define AP_MARK(i) do { } while (0)
 #endif
 
 // A segment of a fold's rows: sub-tiles t0 .. of the fold, row_off rows of the
@@ -216,7 +264,6 @@ __device__ __forceinline__ void cta_publish_value(int* flag, int v) {
     st_release(flag, v);
   }
 }
-__device__ __forceinline__ void cta_publish(int* flag) { cta_publish_value(flag, 1); }
 
 // fp32 values of segment row gi, columns gj .. gj + 31 (rows/cols already bounds-checked)
 __device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
@@ -267,10 +314,15 @@ struct Ctx {
   uint8_t* sm;
   uint32_t sb;
   uint32_t tm;
-  uint64_t* bar;
+  uint64_t* bar;     // MMA completion
+  uint64_t* ibar;    // [2] image buffer loads
+  int* s_next;       // shared flag: the next panel's R rows may be staged
   uint32_t phase;
+  uint32_t ipar;     // bit b: parity of the next load phase of image buffer b
+  int ipend;         // thread 0: bit b set while a load into buffer b is in flight
   bool ok;
 };
+__device__ __forceinline__ uint32_t img_off(int b) { return b ? OFF_IMG1 : OFF_IMG0; }
 
 __device__ __forceinline__ void mma_wait(Ctx& c) {
   c.ok = tc::mbar_wait(c.bar, c.phase) && c.ok;
@@ -307,32 +359,99 @@ __device__ void refresh_a1(Ctx& c) {
   }
 }
 
-// Apply panel k (Y / T images in smem, A1 current) to the task's block; when
-// skip_half0 the first 64 columns are the panel itself and are left alone in R.
-__device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t cs, int wc, bool skip_half0) {
+// Thread 0: start the bulk copy of a published panel's images (Y, T hi, T lo,
+// contiguous as in global memory) into image buffer b.  The panel's flag was
+// acquired by this thread; the proxy fence orders that acquire before the
+// copy engine's reads.
+__device__ __forceinline__ void img_issue(Ctx& c, int b, const uint8_t* src) {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  tc::mbar_expect_tx(c.ibar + b, PIMG);
+  tc::bulk_g2s(c.sb + img_off(b), src, PIMG, c.ibar + b);
+  c.ipend |= 1 << b;
+}
+// All threads: wait (bounded) for the load into image buffer b.
+__device__ __forceinline__ void img_wait(Ctx& c, int b) {
+  c.ok = tc::mbar_wait(c.ibar + b, (c.ipar >> b) & 1u) && c.ok;
+  c.ipar ^= 1u << b;
+  c.ipend &= ~(1 << b);
+}
+
+// Where apply_panel takes its images and R rows, and its lookahead to the next panel.
+struct ApplyOpts {
+  int buf = 0;                      // image buffer holding the panel's Y / T images
+  bool rpre = false;                // the panel's R rows were staged in OFF_RN by this thread
+  // Lookahead to the next panel (none when next_flag is null), checked by
+  // thread 0 while GEMM1 runs: its images are loaded into the other buffer if
+  // it is published, and its R rows (k0_next, nbk_next) are staged while
+  // GEMM2 runs if prev_prog shows them final (prev_prog null: always final).
+  const int* next_flag = nullptr;
+  const uint8_t* next_img = nullptr;
+  const int* prev_prog = nullptr;
+  int prev_need = 0;
+  int64_t k0_next = 0;
+  int nbk_next = 0;
+};
+
+// Stage this thread's 32 R entries of panel rows k0 .. k0 + nbk - 1 in OFF_RN
+// (element (j, col) at j * WB + col) by asynchronous 4-byte copies; entries
+// outside the panel or the block are zero-filled.
+__device__ __forceinline__ void stage_r_rows(const Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t cs,
+                                             int wc, int col, int jh) {
+  const uint32_t dst = c.sb + OFF_RN + (uint32_t)((jh * 32) * WB + col) * 4u;
+  const float* src = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const bool v = jh * 32 + e < nbk && col < wc;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst + (uint32_t)(e * WB * 4)),
+                 "l"(v ? src + (int64_t)e * F.ldR : F.R), "r"(v ? 4 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Apply panel k (Y / T images in image buffer o.buf, A1 current) to the task's
+// block; when skip_half0 the first 64 columns are the panel itself and are left
+// alone in R.
+__device__ __forceinline__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t cs, int wc,
+                                            bool skip_half0, const ApplyOpts& o) {
   const int tid = threadIdx.x, warp = tid >> 5;
   const int col = tid & 127;   // trailing column of this thread == TMEM lane
   const int jh = tid >> 7;     // which 32 of the 64 panel columns this thread handles
   const uint32_t lane_base = c.tm + ((uint32_t)((warp & 3) * 32) << 16);
+  const uint32_t img = c.sb + img_off(o.buf);
+  AP_DECL
   if (tid == 0) {
     constexpr uint32_t id1 = tc::idesc_bf16(128, NB, true, true);
 #pragma unroll 1
     for (int s = 0; s < SUB / 16; ++s) {
       const uint64_t ad = tc::sdesc(c.sb + OFF_A1 + s * 2 * A1_K, A1_K, A1_MN);
-      const uint64_t bd = tc::sdesc(c.sb + OFF_Y + s * 2 * Y_I, Y_I, Y_J);
+      const uint64_t bd = tc::sdesc(img + s * 2 * Y_I, Y_I, Y_J);
       tc::mma_bf16(c.tm + TM_D1, ad, bd, id1, s > 0);
     }
     tc::commit(c.bar);
+    if (o.next_flag) {
+      if (ld_acquire(o.next_flag) >= 1) img_issue(c, o.buf ^ 1, o.next_img);
+      *c.s_next = !o.prev_prog || ld_acquire(o.prev_prog) >= o.prev_need;
+    } else {
+      *c.s_next = 0;
+    }
   }
-  // this thread's 32 R entries, read once while GEMM1 runs
+  // this thread's 32 R entries, read once while GEMM1 runs (staged by this thread
+  // during the previous apply, or from global memory)
   const bool rcol = col < wc && !(skip_half0 && col < NB);
   float rr[32];
-  {
+  if (o.rpre) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    const float* rs = reinterpret_cast<const float*>(c.sm + OFF_RN) + (jh * 32) * WB + col;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) rr[e] = rs[e * WB];
+  } else {
     const float* rp = F.R + (k0 + jh * 32) * F.ldR + cs + col;
 #pragma unroll
     for (int e = 0; e < 32; ++e) rr[e] = (jh * 32 + e < nbk && col < wc) ? rp[(int64_t)e * F.ldR] : 0.f;
   }
   mma_wait(c);
+  AP_MARK(1);
   {
     float w[32];
     tc::tmem_ld32(lane_base + TM_D1 + jh * 32, w);
@@ -347,21 +466,25 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
     }
   }
   sync_for_mma();
+  AP_MARK(2);
   if (tid == 0) {
     constexpr uint32_t id2 = tc::idesc_bf16(128, NB, false, false);
 #pragma unroll 1
     for (int s = 0; s < NB / 16; ++s) {
       const uint64_t ah = tc::sdesc(c.sb + OFF_A2H + s * 2 * A2_K, A2_K, A2_MN);
       const uint64_t al = tc::sdesc(c.sb + OFF_A2L + s * 2 * A2_K, A2_K, A2_MN);
-      const uint64_t bh = tc::sdesc(c.sb + OFF_TH + s * 2 * B2_K, B2_K, B2_MN);
-      const uint64_t bl = tc::sdesc(c.sb + OFF_TL + s * 2 * B2_K, B2_K, B2_MN);
+      const uint64_t bh = tc::sdesc(img + IMG_TH + s * 2 * B2_K, B2_K, B2_MN);
+      const uint64_t bl = tc::sdesc(img + IMG_TL + s * 2 * B2_K, B2_K, B2_MN);
       tc::mma_bf16(c.tm + TM_D2, ah, bh, id2, s > 0);
       tc::mma_bf16(c.tm + TM_D2, ah, bl, id2, 1);
       tc::mma_bf16(c.tm + TM_D2, al, bh, id2, 1);
     }
     tc::commit(c.bar);
   }
+  // rr[] is in registers: the staging area takes the next panel's rows while GEMM2 runs
+  if (*(volatile int*)c.s_next) stage_r_rows(c, F, o.k0_next, o.nbk_next, cs, wc, col, jh);
   mma_wait(c);
+  AP_MARK(3);
   {
     float w[32];
     tc::tmem_ld32(lane_base + TM_D2 + jh * 32, w);
@@ -375,10 +498,12 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
         v[e] = w[j];
         if (jh * 32 + j < nbk && rcol) rp[(int64_t)j * F.ldR] = rr[j] - v[e];
       }
+      // GEMM2 has completed: W2 goes over W^T hi
       store8(c.sb + OFF_B3 + tc::cm_off<true>(col, jh * 32 + g * 8, A2_MN, A2_K), v);
     }
   }
   sync_for_mma();
+  AP_MARK(4);
   if (tid == 0) {
     // D3 += (-Y) W2: negate-A bit of the instruction descriptor
     constexpr uint32_t id3 = tc::idesc_bf16(128, WB, false, false) | (1u << 13);
@@ -386,7 +511,7 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
     for (int mh = 0; mh < 2; ++mh) {
 #pragma unroll 1
       for (int s = 0; s < NB / 16; ++s) {
-        const uint64_t ad = tc::sdesc(c.sb + OFF_Y + mh * 16 * Y_I + s * 2 * Y_J, Y_J, Y_I);
+        const uint64_t ad = tc::sdesc(img + mh * 16 * Y_I + s * 2 * Y_J, Y_J, Y_I);
         const uint64_t bd = tc::sdesc(c.sb + OFF_B3 + s * 2 * A2_K, A2_K, A2_MN);
         tc::mma_bf16(c.tm + TM_D3 + mh * WB, ad, bd, id3, 1);
       }
@@ -394,14 +519,7 @@ __device__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t
     tc::commit(c.bar);
   }
   mma_wait(c);
-}
-
-// Y, T hi and T lo images (contiguous in smem as in global): 16-byte cp.async, all in flight.
-__device__ void copy_images_in(Ctx& c, const uint8_t* src) {
-  for (int i = threadIdx.x; i < (int)(PIMG / 16); i += TPB)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(c.sb + OFF_Y + i * 16), "l"(src + i * 16)
-                 : "memory");
-  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+  AP_MARK(5);
 }
 
 __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_ok) {
@@ -461,12 +579,19 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(5, TR_NOW());
 
   // ---- apply the panels of sub-tile t left of this block ----
+  // Panel k's images are in image buffer buf: loaded by a bulk copy started
+  // during the previous apply when panel k was already published, else now.
+  // The R rows of panel k + 1 are staged during apply k when sub-tile t - 1
+  // has finished them by then.
   const int kend = (int)mn<int64_t>(2 * cb, cdiv(lim, NB));
+  int buf = 0;
+  bool rpre = false;
 #pragma unroll 1
   for (int k = kfirst; k < kend; ++k) {
 #ifdef IFK_TRACE
     const long long w0 = TR_NOW();
 #endif
+    AP_DECL
     // the operand image of X depends on the previous apply only: refresh it before waiting
     if (!a1_valid) {
       tc::fence_before();
@@ -474,16 +599,44 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       tc::fence_after();
       refresh_a1(c);
       a1_valid = true;
+      // Panel k - 1 is applied to the block's R rows (written before the
+      // previous apply's last barrier); by now those writes have mostly
+      // drained, so the fence before the release is short.
+      if (tid == 0) {
+        __threadfence();
+        st_release(prog, k);
+      }
     }
+    AP_MARK(6);
     if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
     if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
+    AP_MARK(9);
+    TR_SET(21, TR_NOW());
     TR_ADD(9, TR_NOW() - w0);
     TR_ADD(10, 1);
-    copy_images_in(c, F.img + ((size_t)t * F.K + k) * PIMG);
+    if (tid == 0 && !(c.ipend & (1 << buf))) img_issue(c, buf, F.img + ((size_t)t * F.K + k) * PIMG);
+    img_wait(c, buf);
     sync_for_mma();
-    apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false);
+    if (!c.ok) return;
+    AP_MARK(0);
+    ApplyOpts o;
+    o.buf = buf;
+    o.rpre = rpre;
+    if (k + 1 < kend) {
+      o.next_flag = F.pflag + (size_t)t * F.K + k + 1;
+      o.next_img = F.img + ((size_t)t * F.K + k + 1) * PIMG;
+      o.prev_prog = prev_prog;
+      o.prev_need = k + 2;
+      o.k0_next = (int64_t)(k + 1) * NB;
+      o.nbk_next = (int)mn<int64_t>(NB, F.n - (int64_t)(k + 1) * NB);
+    }
+    apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false, o);
+    rpre = *(volatile int*)c.s_next != 0;
+    buf ^= 1;
     a1_valid = false;
-    cta_publish_value(prog, k + 1);
+#ifdef IFK_TRACE
+    if (tid == 0) atomicAdd(&g_apply_phase[8], 1ull);
+#endif
   }
   // panels this sub-tile does not reach leave their R rows as they are
   cta_publish_value(prog, F.K);
@@ -511,6 +664,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     if (t > 0 && !cta_wait_ge(prev_prog, F.K + 1 + 2 * q, b, s_ok)) return;
 #ifdef IFK_TRACE
     const long long l0 = TR_NOW();
+    TR_SET(18 + q, l0);
 #endif
     tc::fence_before();
     __syncthreads();
@@ -557,7 +711,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       float e8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) e8[e] = S.P[(j8 * 8 + e) * panel::SP + i];
-      store8(c.sb + OFF_Y + tc::cm_off<true>(i, j8 * 8, Y_I, Y_J), e8);
+      store8(c.sb + OFF_IMG0 + tc::cm_off<true>(i, j8 * 8, Y_I, Y_J), e8);
     }
     for (int it = tid; it < NB * (NB / 8); it += TPB) {
       const int j = it >> 3, l8 = it & 7;
@@ -565,8 +719,8 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 #pragma unroll
       for (int e = 0; e < 8; ++e) tc::split_bf16(S.Tm[(l8 * 8 + e) * LDP + j], hi[e], lo[e]);
       const uint32_t off = tc::cm_off<true>(j, l8 * 8, B2_MN, B2_K);
-      store8(c.sb + OFF_TH + off, hi);
-      store8(c.sb + OFF_TL + off, lo);
+      store8(c.sb + OFF_IMG0 + IMG_TH + off, hi);
+      store8(c.sb + OFF_IMG0 + IMG_TL + off, lo);
     }
     for (int idx = tid; idx < NB * NB; idx += TPB) {
       const int i = idx / NB, j = idx % NB;
@@ -578,10 +732,11 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     // block's second half and the second panel); the second panel's at once.
     tc::fence_async_smem();
     __syncthreads();
-    if (tid == 0) bulk_store(F.img + ((size_t)t * F.K + kk) * PIMG, c.sb + OFF_Y, PIMG);
+    if (tid == 0) bulk_store(F.img + ((size_t)t * F.K + kk) * PIMG, c.sb + OFF_IMG0, PIMG);
     const bool half = q == 0 && wc > NB;
     if (half) {
       cta_publish_value(prog, F.K + 1 + 2 * q);
+      TR_SET(16, TR_NOW());
       pending_img = F.pflag + (size_t)t * F.K + kk;
     } else {
       __syncthreads();
@@ -600,9 +755,10 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
         if (t > 0 && !cta_wait_ge(prev_prog, F.K + 2, b, s_ok)) return;
         refresh_a1(c);
         sync_for_mma();
-        apply_panel(c, F, c0, nbk, cs, wc, true);
+        apply_panel(c, F, c0, nbk, cs, wc, true, ApplyOpts{});  // own images: buffer 0
       }
       cta_publish_value(prog, F.K + 2);
+      TR_SET(17, TR_NOW());
       TR_ADD(14, TR_NOW() - h0);
     }
   }
@@ -627,13 +783,12 @@ __device__ __forceinline__ void decode(const PFBatch& b, int tk, int* f, int* t,
   int r = tk - b.wave_off[d];
   for (int q = 0; q < b.nf; ++q) {
     const PFold& F = b.f[q];
-    const int tlo = d - F.CB + 1 > 0 ? d - F.CB + 1 : 0;
-    const int thi = d < F.T - 1 ? d : F.T - 1;
-    const int cnt = thi >= tlo ? thi - tlo + 1 : 0;
+    int tlo, cnt;
+    wave_range(d, F.T, F.CB, &tlo, &cnt);
     if (r < cnt) {
       *f = q;
-      *t = tlo + r;
-      *cb = d - *t;
+      *t = tlo + r * CBW;
+      *cb = (d - *t) / CBW;
       return;
     }
     r -= cnt;
@@ -647,9 +802,15 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   int* s_tk = reinterpret_cast<int*>(sm + OFF_BAR + 16);
   int* s_ok = reinterpret_cast<int*>(sm + OFF_BAR + 20);
+  uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 24);  // [2]
+  int* s_next = reinterpret_cast<int*>(sm + OFF_BAR + 40);
   const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) tc::tmem_alloc(tslot, TM_COLS);
-  if (tid == 0) tc::mbar_init(bar, 1);
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::mbar_init(ibar, 1);
+    tc::mbar_init(ibar + 1, 1);
+  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -658,7 +819,11 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
   c.sb = tc::smem_u32(sm);
   c.tm = *tslot;
   c.bar = bar;
+  c.ibar = ibar;
+  c.s_next = s_next;
   c.phase = 0;
+  c.ipar = 0;
+  c.ipend = 0;
   c.ok = true;
 #pragma unroll 1
   for (;;) {
@@ -679,8 +844,14 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
       break;
     }
   }
-  // a task that gave up may leave a bulk store of panel images in flight
-  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  // a task that gave up may leave a bulk store of panel images, a bulk load of
+  // images or staged R rows in flight: wait for them (bounded) before exiting
+  if (tid == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    for (int q = 0; q < 2; ++q)
+      if (c.ipend & (1 << q)) tc::mbar_wait(ibar + q, (c.ipar >> q) & 1u);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -713,10 +884,16 @@ extern "C" __attribute__((visibility("default"))) int ifk_trace_read(long long* 
   if (cudaMemcpyFromSymbol(&n, g_trace_n, sizeof(int)) != cudaSuccess) return -1;
   n = n < max_tasks ? n : max_tasks;
   if (n > (1 << 14)) n = 1 << 14;
-  if (cudaMemcpyFromSymbol(dst, g_trace, (size_t)n * 16 * sizeof(long long)) != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(dst, g_trace, (size_t)n * TRN * sizeof(long long)) != cudaSuccess) return -1;
   const int zero = 0;
   cudaMemcpyToSymbol(g_trace_n, &zero, sizeof(int));
   return n;
+}
+extern "C" __attribute__((visibility("default"))) int ifk_trace_apply_phases(unsigned long long* dst) {
+  if (cudaMemcpyFromSymbol(dst, g_apply_phase, 16 * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  unsigned long long z[16] = {};
+  cudaMemcpyToSymbol(g_apply_phase, z, sizeof(z));
+  return 0;
 }
 extern "C" __attribute__((visibility("default"))) int ifk_trace_panel_phases(unsigned long long* dst) {
   if (cudaMemcpyFromSymbol(dst, panel::g_panel_phase, 16 * sizeof(unsigned long long)) != cudaSuccess) return -1;
@@ -732,7 +909,7 @@ int64_t pfold_subtiles(const PFoldDesc& d) {
   return t;
 }
 
-int64_t pfold_max_subtiles(int64_t n) { return (int64_t)MAXW - cdiv(n, WB) + 1; }
+int64_t pfold_max_subtiles(int64_t n) { return (int64_t)MAXW - CBW * (cdiv(n, WB) - 1); }
 
 size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n) {
   size_t b = 256;
@@ -791,7 +968,7 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
     w += align256((size_t)F.T * F.CB * 4);
     F.pflag = (int*)w;
     w += align256((size_t)F.T * F.K * 4);
-    maxw = maxw > F.T + F.CB - 1 ? maxw : F.T + F.CB - 1;
+    maxw = maxw > num_waves(F.T, F.CB) ? maxw : num_waves(F.T, F.CB);
   }
   if (b.nf == 0) return IFK_OK;
   const size_t flag_bytes = (size_t)(w - (char*)ws);
@@ -804,9 +981,9 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
   for (int dd = 0; dd < maxw; ++dd) {
     b.wave_off[dd] = acc;
     for (int g = 0; g < b.nf; ++g) {
-      const int tlo = dd - b.f[g].CB + 1 > 0 ? dd - b.f[g].CB + 1 : 0;
-      const int thi = dd < b.f[g].T - 1 ? dd : b.f[g].T - 1;
-      if (thi >= tlo) acc += thi - tlo + 1;
+      int tlo, cnt;
+      wave_range(dd, b.f[g].T, b.f[g].CB, &tlo, &cnt);
+      acc += cnt;
     }
   }
   b.wave_off[maxw] = acc;

@@ -93,6 +93,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
   return false;
 }
 
+// Arm an mbarrier phase for `bytes` of incoming asynchronous copies (one arrival).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mbar)), "r"(bytes)
+               : "memory");
+}
+// Bulk copy global -> shared by the TMA engine, completing on an mbarrier (no multicast).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+               : "memory");
+}
+
 // TMEM allocation by one full warp; the base address is written to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
