@@ -333,56 +333,86 @@ def run_ours(args, rank, world, local_rank):
         hW = torch.empty_like(W, device="cpu").pin_memory()
         bi = hX.numel() * 2 + hD.numel() * 2 + hG.numel() * 4
         bo = hW.numel() * 4
-        k2 = max(1, min(args.steps, 5))
-        # Each step copies its inputs tile by tile on a copy stream.  per-tile: the
-        # fold of a tile waits for that tile only.  one-launch: the tiles are folded
-        # in --e2e-groups launches of consecutive tiles (the last one with the
-        # damping rows), each waiting for its own tiles, so the copies of a group
-        # run under the fold of the one before.  The step starts its copies after
-        # the previous step's reads of X, D, gW.
-        cs = torch.cuda.Stream()
+        k2 = max(2, min(args.steps, 10))
+        # Every step copies all of its inputs from pinned host memory and reads the
+        # updated W back.  The device inputs are double-buffered, so the copies of
+        # step k + 1 (on a copy stream) run under the compute of step k, and the
+        # read-back of W runs on its own stream (the next update waits for it).
+        # per-tile: the fold of a tile waits for that tile only.  one-launch: the
+        # tiles are folded in --e2e-groups launches of consecutive tiles (the last
+        # one with the damping rows), each waiting for its own tiles.
+        cs, dh = torch.cuda.Stream(), torch.cuda.Stream()
         s0 = torch.cuda.current_stream()
-        ng = 1 if per_tile else max(1, min(args.e2e_groups, len(tiles)))
-        bounds = [round(i * len(tiles) / ng) for i in range(ng + 1)]
+        if per_tile:
+            sizes = [len(tiles)]
+        else:
+            sizes = [int(x) for x in str(args.e2e_groups).split(",") if int(x) > 0]
+            if len(sizes) == 1:  # a count of equal groups
+                ng = max(1, min(sizes[0], len(tiles)))
+                sizes = [round((i + 1) * len(tiles) / ng) - round(i * len(tiles) / ng) for i in range(ng)]
+            if sum(sizes) != len(tiles):
+                raise SystemExit(f"--e2e-groups {args.e2e_groups}: group sizes must add up to {len(tiles)} tiles")
+        ng = len(sizes)
+        bounds = [sum(sizes[:i]) for i in range(ng + 1)]
+        bufs = [(X, D, gW), (torch.empty_like(X), torch.empty_like(D), torch.empty_like(gW))]
+        st = {"free": [None, None], "wdone": None, "k": 0}
 
         def e2e_step():
-            cs.wait_stream(s0)
+            xb, db, gb = bufs[st["k"] % 2]
             evs = []
             with torch.cuda.stream(cs):
+                if st["free"][st["k"] % 2] is not None:
+                    cs.wait_event(st["free"][st["k"] % 2])  # step k - 2 is done reading this buffer
                 for lo, hi in tiles:
-                    X[lo:hi].copy_(hX[lo:hi], non_blocking=True)
-                    D[lo:hi].copy_(hD[lo:hi], non_blocking=True)
+                    xb[lo:hi].copy_(hX[lo:hi], non_blocking=True)
+                    db[lo:hi].copy_(hD[lo:hi], non_blocking=True)
                     e = torch.cuda.Event()
                     e.record(cs)
                     evs.append(e)
-                gW.copy_(hG, non_blocking=True)
+                gb.copy_(hG, non_blocking=True)
                 eg = torch.cuda.Event()
                 eg.record(cs)
             lc.clear()
             if per_tile:
                 for (lo, hi), e in zip(tiles, evs):
                     s0.wait_event(e)
-                    lc.fold(X[lo:hi], D[lo:hi])
+                    lc.fold(xb[lo:hi], db[lo:hi])
                 lc.refresh(DAMPING)
             else:
                 for gi in range(ng):
                     s0.wait_event(evs[bounds[gi + 1] - 1])
                     for lo, hi in tiles[bounds[gi]:bounds[gi + 1]]:
-                        lc.fold(X[lo:hi], D[lo:hi])
+                        lc.fold(xb[lo:hi], db[lo:hi])
                     if gi + 1 < ng:
                         lc.flush()
                 lc.refresh(DAMPING, consume=True)
             s0.wait_event(eg)
-            lc.update(W, lc.natgrad(gW), LR, MOM, 0.0, None)
-            hW.copy_(W, non_blocking=True)
+            nat = lc.natgrad(gb)
+            fe = torch.cuda.Event()
+            fe.record(s0)
+            st["free"][st["k"] % 2] = fe
+            if st["wdone"] is not None:
+                s0.wait_event(st["wdone"])  # the previous read-back of W has finished
+            lc.update(W, nat, LR, MOM, 0.0, None)
+            ue = torch.cuda.Event()
+            ue.record(s0)
+            dh.wait_event(ue)
+            with torch.cuda.stream(dh):
+                hW.copy_(W, non_blocking=True)
+                wd = torch.cuda.Event()
+                wd.record(dh)
+            st["wdone"] = wd
+            st["k"] += 1
 
-        e2e_step()
+        for _ in range(2):
+            e2e_step()
         torch.cuda.synchronize()
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(k2):
             e2e_step()
+        s0.wait_event(st["wdone"])  # the last step's W is on the host
         b.record()
         b.synchronize()
         e2e_ms = a.elapsed_time(b) / k2
@@ -392,9 +422,10 @@ def run_ours(args, rank, world, local_rank):
             e2e_ms = float(t.item())
         e2e = {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": bi,
                "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms,
-               "schedule": args.schedule, "launch_groups": ng,
-               "note": ("pinned host inputs copied per tile on a copy stream; each fold launch waits for its "
-                        "own tiles only; W read back each step")}
+               "schedule": args.schedule, "launch_groups": sizes,
+               "note": ("every step copies its X, delta (per tile) and grad_W from pinned host memory and reads "
+                        "the updated W back; device inputs double-buffered, so step k+1's copies run under step "
+                        "k's compute; each fold launch waits for its own tiles only")}
 
     if rank != 0:
         return
@@ -507,8 +538,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--schedule", choices=["one-launch", "per-tile"], default="one-launch",
                     help="fold schedule of the timed step (the other one is reported beside it)")
-    ap.add_argument("--e2e-groups", type=int, default=2,
-                    help="one-launch schedule, e2e: fold launches the row tiles are split into")
+    ap.add_argument("--e2e-groups", default="1",
+                    help="one-launch schedule, e2e: fold launches the row tiles are split into: a count of "
+                         "equal groups, or comma-separated tile counts of consecutive groups (e.g. 1,7)")
     ap.add_argument("--no-other-schedule", action="store_true",
                     help="skip the secondary timing of the other schedule")
     ap.add_argument("--cpu-sample-scale", type=float, default=1.0)
