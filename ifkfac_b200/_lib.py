@@ -36,8 +36,7 @@ SIGNATURES = {
     "ifk_tsqr_fold_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp,
                                      _vp, _sz, _vp]),
     "ifk_tsqr_fold_segments_workspace": (_sz, [_int, _vp, _vp, _vp, _vp]),
-    "ifk_tsqr_fold_segments": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _int, _vp,
-                                      _vp, _sz, _vp]),
+    "ifk_tsqr_fold_segments": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _int, _vp, _vp, _sz, _vp]),
     "ifk_finalize_workspace": (_sz, [_i64]),
     "ifk_finalize_batched_workspace": (_sz, [_int, _vp]),
     "ifk_finalize_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp,
@@ -54,6 +53,12 @@ SIGNATURES = {
     "ifk_update": (_int, [_vp, _vp, _vp, _i64, _dbl, _dbl, _dbl, _dbl, _int, _vp, _sz, _vp]),
     "ifk_update_bias": (_int, [_vp, _vp, _i64, _dbl, _dbl, _vp]),
 }
+
+
+class Segment(ctypes.Structure):
+    """``ifk_segment`` of include/ifk.h: rows of a chunk for ifk_tsqr_fold_segments."""
+    _fields_ = [("chunk", ctypes.c_void_p), ("ld", ctypes.c_int64), ("rows", ctypes.c_int64),
+                ("row_index", ctypes.c_void_p), ("src_rows", ctypes.c_int64), ("cols", ctypes.c_int64)]
 
 
 class IFKError(RuntimeError):

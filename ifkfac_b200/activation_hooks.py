@@ -25,7 +25,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .engine import Factor, fold_batched
+from .engine import Factor, Rows, as_rows, fold_segments
 
 logger = logging.getLogger(__name__)
 
@@ -51,40 +51,47 @@ def reshape_conv_grad(delta: torch.Tensor) -> torch.Tensor:
 
 
 def prepare_x(x: torch.Tensor, module: nn.Module, max_conv_rows: int, max_seq_rows: int,
-              augment_bias: bool, transform=None) -> torch.Tensor:
-    """Activation chunk of one forward call (ifkfac/activation_hooks.py:519-548)."""
+              augment_bias: bool, transform=None):
+    """Activation rows of one forward call (ifkfac/activation_hooks.py:519-548).
+
+    The rows are returned as :class:`Rows`: the 3-D reshape is a view, and the
+    random row subsample and the bias column are read in place by the fold
+    kernels instead of being copied.  With a chunk transform the rows are
+    materialised and the transform's output (a tensor) is returned."""
+    idx = None
     if isinstance(module, nn.Conv2d):
         x = unfold_conv_input(x, module)
         if max_conv_rows > 0 and x.shape[0] > max_conv_rows:
-            x = x[torch.randperm(x.shape[0], device=x.device)[:max_conv_rows]]
+            idx = torch.randperm(x.shape[0], device=x.device)[:max_conv_rows]
     elif x.ndim > 2:
         x = x.reshape(-1, x.shape[-1])
         if max_seq_rows > 0 and x.shape[0] > max_seq_rows:
-            x = x[torch.randperm(x.shape[0], device=x.device)[:max_seq_rows]]
-    if augment_bias and isinstance(module, nn.Linear) and module.bias is not None:
-        x = torch.cat([x, torch.ones(x.shape[0], 1, device=x.device, dtype=x.dtype)], dim=1)
+            idx = torch.randperm(x.shape[0], device=x.device)[:max_seq_rows]
+    ones = augment_bias and isinstance(module, nn.Linear) and module.bias is not None
+    rows = Rows(x, idx, ones)
     if transform is not None:
-        x = transform(x)
-    return x
+        return transform(rows.materialize())
+    return rows
 
 
-def prepare_g(delta: torch.Tensor, module: nn.Module, max_seq_rows: int, transform=None) -> torch.Tensor:
-    """Gradient chunk of one backward call (ifkfac/activation_hooks.py:601-615)."""
+def prepare_g(delta: torch.Tensor, module: nn.Module, max_seq_rows: int, transform=None):
+    """Gradient rows of one backward call (ifkfac/activation_hooks.py:601-615), as
+    :class:`Rows` (or the transform's output)."""
+    idx = None
     if isinstance(module, nn.Conv2d):
         delta = reshape_conv_grad(delta)
     elif delta.ndim > 2:
         delta = delta.reshape(-1, delta.shape[-1])
         if max_seq_rows > 0 and delta.shape[0] > max_seq_rows:
-            delta = delta[torch.randperm(delta.shape[0], device=delta.device)[:max_seq_rows]]
+            idx = torch.randperm(delta.shape[0], device=delta.device)[:max_seq_rows]
+    rows = Rows(delta, idx)
     if transform is not None:
-        delta = transform(delta)
-    return delta
+        return transform(rows.materialize())
+    return rows
 
 
-def _chunk_for_fold(c: torch.Tensor) -> torch.Tensor:
-    if c.dtype not in (torch.float32, torch.bfloat16):
-        c = c.float()
-    return c if c.stride(-1) == 1 else c.contiguous()
+def _rows_count(c) -> int:
+    return c.rows if isinstance(c, Rows) else int(c.shape[0])
 
 
 class RawActivationHooks:
@@ -203,27 +210,27 @@ class RawActivationHooks:
             self._ws[key] = ws
         return ws
 
-    def _fold_now(self, table, module, chunk: torch.Tensor) -> None:
-        if not chunk.is_cuda:
-            raise ValueError("ifkfac_b200 hooks need CUDA activations (no CPU path)")
-        chunk = _chunk_for_fold(chunk)
-        f = self._factor(table, module, chunk.shape[1], chunk.device)
-        key = ("fold", chunk.device)
-        self._ws[key] = fold_batched([f], [chunk], self._ws.get(key))
-
-    def _fold_many(self, table, items) -> None:
-        """Fold (module, chunk) pairs in batched wave schedules of up to 8 folds
-        (the bucketed flush of ifkfac/activation_hooks.py:370-457)."""
+    def _fold_lists(self, table, items) -> None:
+        """Fold (module, [chunks]) pairs: every module's chunks in arrival order,
+        the modules of one dtype and device together, by ifk_tsqr_fold_segments
+        (no concatenation; the bucketed flush of ifkfac/activation_hooks.py:370-457
+        and the deferred drain of :347-364)."""
         by_dt: Dict[Tuple, List] = {}
-        for module, chunk in items:
-            chunk = _chunk_for_fold(chunk)
-            by_dt.setdefault((chunk.dtype, chunk.device), []).append((module, chunk))
+        for module, chunks in items:
+            rs = [as_rows(c) for c in chunks]
+            rs = [r for r in rs if r.rows > 0]
+            if not rs:
+                continue
+            if not rs[0].x.is_cuda:
+                raise ValueError("ifkfac_b200 hooks need CUDA activations (no CPU path)")
+            by_dt.setdefault((rs[0].dtype, rs[0].device), []).append((module, rs))
         for (dt, dev), lst in by_dt.items():
-            for i in range(0, len(lst), 8):
-                grp = lst[i:i + 8]
-                fs = [self._factor(table, m, c.shape[1], c.device) for m, c in grp]
-                key = ("fold", dev)
-                self._ws[key] = fold_batched(fs, [c for _, c in grp], self._ws.get(key))
+            fs = [self._factor(table, m, rs[0].cols, dev) for m, rs in lst]
+            key = ("fold", dev)
+            self._ws[key] = fold_segments(fs, [rs for _, rs in lst], self._ws.get(key))
+
+    def _fold_now(self, table, module, chunk) -> None:
+        self._fold_lists(table, [(module, [chunk])])
 
     # ---- hooks ----
     def _forward_hook(self, module, inp, out):
@@ -240,43 +247,39 @@ class RawActivationHooks:
         self._accumulate(module, d, self._fg, self._n_rows_G, self._pending_G, self._raw_G)
 
     def _accumulate(self, module, chunk, table, nrows, pending, raw):
+        n = _rows_count(chunk)
         if self.deferred:
             raw[module].append(chunk)
-            nrows[module] += chunk.shape[0]
+            nrows[module] += n
             if len(raw[module]) >= self.deferred_window:
-                c = raw[module][0] if len(raw[module]) == 1 else torch.cat(raw[module], 0)
-                self._fold_now(table, module, c)
+                self._fold_lists(table, [(module, raw[module])])
                 raw[module] = []
             return
         if self.batched:
             pending[module].append(chunk)
-            nrows[module] += chunk.shape[0]
+            nrows[module] += n
             return
         self._fold_now(table, module, chunk)
-        nrows[module] += chunk.shape[0]
+        nrows[module] += n
 
     def flush(self) -> None:
         """Batched mode: fold every pending chunk (no-op otherwise)."""
         if not self.batched:
             return
         for pending, table in ((self._pending_X, self._fx), (self._pending_G, self._fg)):
-            items = []
-            for m, chunks in pending.items():
-                if chunks:
-                    items.append((m, chunks[0] if len(chunks) == 1 else torch.cat(chunks, 0)))
-                    pending[m] = []
+            items = [(m, chunks) for m, chunks in pending.items() if chunks]
+            for m, _ in items:
+                pending[m] = []
             if items:
-                self._fold_many(table, items)
+                self._fold_lists(table, items)
 
     def _drain_deferred(self) -> None:
         for raw, table in ((self._raw_X, self._fx), (self._raw_G, self._fg)):
-            items = []
-            for m, chunks in raw.items():
-                if chunks:
-                    items.append((m, chunks[0] if len(chunks) == 1 else torch.cat(chunks, 0)))
-                    raw[m] = []
+            items = [(m, chunks) for m, chunks in raw.items() if chunks]
+            for m, _ in items:
+                raw[m] = []
             if items:
-                self._fold_many(table, items)
+                self._fold_lists(table, items)
 
     # ---- factors ----
     def get_factors(self, out_dtype: torch.dtype = torch.float32,

@@ -148,6 +148,9 @@ struct PSeg {
   const void* X;
   int64_t ldX;
   int64_t rows, row_off;
+  const int64_t* ridx;  // row i of the segment is row ridx[i] of X (null: row i)
+  int64_t src_rows;     // rows of X (bound for ridx)
+  int64_t cols;         // columns read from X; column cols (when < n) is ones
   int t0;
   int xkind;
   int tri;      // row i of the segment is zero left of column i
@@ -265,14 +268,32 @@ __device__ __forceinline__ void cta_publish_value(int* flag, int v) {
   }
 }
 
-// fp32 values of segment row gi, columns gj .. gj + 31 (rows/cols already bounds-checked)
-__device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj, int valid, float (&v)[32]) {
+// fp32 values of segment row gi, columns gj .. gj + 31 of the fold (gi < rows and
+// the valid count already bounded by the fold's width).  Gathered rows come from
+// row ridx[gi] of X; an index outside X gives a zero row and IFK_ERR_ARG.
+// Columns past X's own (cols) read 1 (the bias column) then 0.
+__device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj, int valid, float (&v)[32],
+                                           int* status) {
   if (F.xkind == XK_IDENT) {
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = (e < valid && gi == gj + e) ? F.ident : 0.f;
-  } else if (F.xkind == XK_BF16) {
-    const __nv_bfloat16* p = (const __nv_bfloat16*)F.X + gi * F.ldX + gj;
-    const bool vec = valid >= 32 && ((((uintptr_t)p) & 15) == 0);
+    return;
+  }
+  int64_t si = gi;
+  if (F.ridx) {
+    si = F.ridx[gi];
+    if (si < 0 || si >= F.src_rows) {
+      if (status) atomicExch(status, IFK_ERR_ARG);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = 0.f;
+      return;
+    }
+  }
+  const int64_t vm64 = F.cols - gj;  // columns of this group held by X
+  const int vm = vm64 < valid ? (vm64 > 0 ? (int)vm64 : 0) : valid;
+  if (F.xkind == XK_BF16) {
+    const __nv_bfloat16* p = (const __nv_bfloat16*)F.X + si * F.ldX + gj;
+    const bool vec = vm >= 32 && ((((uintptr_t)p) & 15) == 0);
     if (vec) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -286,27 +307,32 @@ __device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] = e < valid ? __bfloat162float(p[e]) : 0.f;
+      for (int e = 0; e < 32; ++e) v[e] = e < vm ? __bfloat162float(p[e]) : 0.f;
     }
   } else {
-    const float* p = (const float*)F.X + gi * F.ldX + gj;
+    const float* p = (const float*)F.X + si * F.ldX + gj;
     const bool vec = ((((uintptr_t)p) & 15) == 0);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       float4 x;
       if (vec) {
-        x = ld4(p + 4 * q, valid - 4 * q);
+        x = ld4(p + 4 * q, vm - 4 * q);
       } else {
-        x.x = 4 * q < valid ? p[4 * q] : 0.f;
-        x.y = 4 * q + 1 < valid ? p[4 * q + 1] : 0.f;
-        x.z = 4 * q + 2 < valid ? p[4 * q + 2] : 0.f;
-        x.w = 4 * q + 3 < valid ? p[4 * q + 3] : 0.f;
+        x.x = 4 * q < vm ? p[4 * q] : 0.f;
+        x.y = 4 * q + 1 < vm ? p[4 * q + 1] : 0.f;
+        x.z = 4 * q + 2 < vm ? p[4 * q + 2] : 0.f;
+        x.w = 4 * q + 3 < vm ? p[4 * q + 3] : 0.f;
       }
       v[4 * q] = x.x;
       v[4 * q + 1] = x.y;
       v[4 * q + 2] = x.z;
       v[4 * q + 3] = x.w;
     }
+  }
+  const int64_t oc = F.cols - gj;  // the column of ones, when inside this group
+  if (oc >= 0 && oc < valid) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = (e == oc) ? 1.f : v[e];  // constant indices: v stays in registers
   }
 }
 
@@ -559,7 +585,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     for (int q = 0; q < WB / 32; ++q) {
       float v[32];
       if (r < h) {
-        load_row32(G, row0 + r, cs + q * 32, wc - q * 32, v);
+        load_row32(G, row0 + r, cs + q * 32, wc - q * 32, v, b.status);
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0.f;
@@ -957,6 +983,9 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
       P.ldX = E.ldX;
       P.rows = E.rows;
       P.row_off = off;
+      P.ridx = E.ridx;
+      P.src_rows = E.src_rows;
+      P.cols = E.cols < 0 ? D.n : E.cols;
       P.t0 = t0;
       P.xkind = E.xkind;
       P.tri = E.tri;

@@ -59,8 +59,11 @@ int plan_pieces(const PFoldDesc& D, const PFoldSeg* segs, int nseg, std::vector<
       const int64_t take_sub = std::min<int64_t>(max_sub - cur_sub, cdiv(E.rows - off, SUB));
       const int64_t take = std::min<int64_t>(take_sub * SUB, E.rows - off);
       if (E.tri && take < E.rows) return IFK_ERR_SHAPE;  // trapezoidal chunks come in one piece
-      const void* X = E.xkind == 2 ? E.X : (const void*)((const char*)E.X + off * E.ldX * elem_bytes(E.xkind));
-      pfold_add(cur, X, E.ldX, take, E.xkind, E.ident, E.tri);
+      PFoldSeg piece = E;
+      piece.rows = take;
+      if (E.ridx) piece.ridx = E.ridx + off;  // gathered rows: the index array advances
+      else if (E.xkind != 2) piece.X = (const char*)E.X + off * E.ldX * elem_bytes(E.xkind);
+      cur.seg[cur.nseg++] = piece;
       cur_sub += take_sub;
       off += take;
       done += take;
@@ -250,7 +253,8 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
 // fp32 wave fold of one chunk (copied into the workspace) or of ident * I when chunk is null
 static int fold_fp32(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int64_t ld_chunk,
                      int64_t rows, int64_t n, int chunk_dtype, int tri, float ident, int prec,
-                     int* d_status, void* workspace, cudaStream_t s) {
+                     int* d_status, void* workspace, cudaStream_t s, const int64_t* ridx = nullptr,
+                     int64_t src_rows = 0, int64_t cols = -1) {
   FoldArgs a;
   a.R = R;
   a.ldR = ldR;
@@ -264,7 +268,8 @@ static int fold_fp32(float* R, int64_t ldR, int64_t rows_R, const void* chunk, i
   a.K = (int)cdiv(n, NB);
   a.tri = tri;
   a.err = d_status;
-  const int rc = chunk ? copy_chunk(a.X, a.ldX, chunk, ld_chunk, rows, n, chunk_dtype, s)
+  const int rc = chunk ? copy_chunk(a.X, a.ldX, chunk, ld_chunk, rows, n, chunk_dtype, s, ridx, src_rows, cols,
+                                    d_status)
                        : fill_scaled_identity(a.X, a.ldX, n, ident, s);
   if (rc != IFK_OK) return rc;
   return fold_run(a, prec, s);
@@ -277,16 +282,17 @@ static int64_t seg_base(int f, const int* nseg) {
 }
 
 size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
-                                        const int64_t* seg_rows, const double* ident_tail) {
-  if (nfolds <= 0 || !n || !nseg || !seg_rows) return 0;
+                                        const ifk_segment* segs, const double* ident_tail) {
+  if (nfolds <= 0 || !n || !nseg) return 0;
   size_t b = 0;
   for (int f = 0; f < nfolds; ++f) {
-    if (n[f] <= 0 || nseg[f] < 0) return 0;
+    if (n[f] <= 0 || nseg[f] < 0 || (nseg[f] > 0 && !segs)) return 0;
     const int64_t base = seg_base(f, nseg);
     int64_t sub = 0, most = 0;
     for (int g = 0; g < nseg[f]; ++g) {
-      sub += cdiv(std::max<int64_t>(seg_rows[base + g], 0), SUB);
-      most = std::max(most, seg_rows[base + g]);
+      const int64_t r = std::max<int64_t>(segs[base + g].rows, 0);
+      sub += cdiv(r, SUB);
+      most = std::max(most, r);
     }
     if (ident_tail && ident_tail[f] > 0) {
       sub += cdiv(n[f], SUB);
@@ -298,51 +304,71 @@ size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int*
 }
 
 int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, const int64_t* rows_R,
-                           const int64_t* n, const int* nseg, const void* const* seg_chunk,
-                           const int64_t* seg_ld, const int64_t* seg_rows, int chunk_dtype,
+                           const int64_t* n, const int* nseg, const ifk_segment* segs, int chunk_dtype,
                            const double* ident_tail, int prec, int* d_status, void* workspace,
                            size_t workspace_bytes, ifk_stream_t stream) {
-  if (nfolds < 0 || (nfolds > 0 && (!R || !ldR || !rows_R || !n || !nseg || !seg_chunk || !seg_ld ||
-                                    !seg_rows)))
-    return IFK_ERR_ARG;
+  if (nfolds < 0 || (nfolds > 0 && (!R || !ldR || !rows_R || !n || !nseg))) return IFK_ERR_ARG;
   if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
   if (!prec_ok(prec)) return IFK_ERR_ARG;
   bool any = false;
   for (int f = 0; f < nfolds; ++f) {
-    if (!R[f] || nseg[f] < 0) return IFK_ERR_ARG;
+    if (!R[f] || nseg[f] < 0 || (nseg[f] > 0 && !segs)) return IFK_ERR_ARG;
     if (n[f] <= 0 || rows_R[f] < 0 || rows_R[f] > n[f] || ldR[f] < n[f]) return IFK_ERR_SHAPE;
     if (ident_tail && !(ident_tail[f] >= 0)) return IFK_ERR_ARG;
     const int64_t base = seg_base(f, nseg);
     for (int g = 0; g < nseg[f]; ++g) {
-      const int64_t r = seg_rows[base + g];
-      if (r < 0 || (r > 0 && seg_ld[base + g] < n[f])) return IFK_ERR_SHAPE;
-      if (r > 0 && !seg_chunk[base + g]) return IFK_ERR_ARG;
-      any = any || r > 0;
+      const ifk_segment& E = segs[base + g];
+      if (E.rows < 0) return IFK_ERR_SHAPE;
+      if (E.rows == 0) continue;
+      if (!E.chunk) return IFK_ERR_ARG;
+      if (E.cols != n[f] && E.cols != n[f] - 1) return IFK_ERR_SHAPE;
+      if (E.cols < 1 || E.ld < E.cols) return IFK_ERR_SHAPE;
+      if (E.row_index && E.src_rows <= 0) return IFK_ERR_SHAPE;
+      any = true;
     }
     any = any || (ident_tail && ident_tail[f] > 0);
   }
   if (!any) return IFK_OK;
   if (!workspace || !aligned(workspace) ||
-      workspace_bytes < ifk_tsqr_fold_segments_workspace(nfolds, n, nseg, seg_rows, ident_tail))
+      workspace_bytes < ifk_tsqr_fold_segments_workspace(nfolds, n, nseg, segs, ident_tail))
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   cudaStream_t s = S(stream);
   if (prec == IFK_PREC_BF16) {
     std::vector<PFoldDesc> d((size_t)nfolds);
-    std::vector<std::vector<PFoldSeg>> segs((size_t)nfolds);
+    std::vector<std::vector<PFoldSeg>> sg((size_t)nfolds);
     std::vector<const PFoldSeg*> sp((size_t)nfolds);
     std::vector<int> ns((size_t)nfolds);
     for (int f = 0; f < nfolds; ++f) {
       d[f] = pfold_desc(R[f], ldR[f], n[f], rows_R[f]);
       const int64_t base = seg_base(f, nseg);
-      for (int g = 0; g < nseg[f]; ++g)
-        if (seg_rows[base + g] > 0)
-          segs[f].push_back(PFoldSeg{seg_chunk[base + g], seg_ld[base + g], seg_rows[base + g],
-                                     chunk_dtype == IFK_BF16 ? 1 : 0, 0.f, 0});
-      if (ident_tail && ident_tail[f] > 0)
-        segs[f].push_back(PFoldSeg{nullptr, 0, n[f], 2, (float)ident_tail[f], 1});
-      sp[f] = segs[f].data();
-      ns[f] = (int)segs[f].size();
+      for (int g = 0; g < nseg[f]; ++g) {
+        const ifk_segment& E = segs[base + g];
+        if (E.rows <= 0) continue;
+        PFoldSeg P;
+        P.X = E.chunk;
+        P.ldX = E.ld;
+        P.rows = E.rows;
+        P.xkind = chunk_dtype == IFK_BF16 ? 1 : 0;
+        P.ident = 0.f;
+        P.tri = 0;
+        P.ridx = E.row_index;
+        P.src_rows = E.src_rows;
+        P.cols = E.cols;
+        sg[f].push_back(P);
+      }
+      if (ident_tail && ident_tail[f] > 0) {
+        PFoldSeg P;
+        P.X = nullptr;
+        P.ldX = 0;
+        P.rows = n[f];
+        P.xkind = 2;
+        P.ident = (float)ident_tail[f];
+        P.tri = 1;
+        sg[f].push_back(P);
+      }
+      sp[f] = sg[f].data();
+      ns[f] = (int)sg[f].size();
     }
     // folds without rows are dropped by the launcher
     return run_persistent(nfolds, d.data(), workspace, d_status, s, sp.data(), ns.data());
@@ -352,12 +378,12 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
     int64_t rr = rows_R[f];
     const int64_t base = seg_base(f, nseg);
     for (int g = 0; g < nseg[f]; ++g) {
-      const int64_t r = seg_rows[base + g];
-      if (r == 0) continue;
-      const int rc = fold_fp32(R[f], ldR[f], rr, seg_chunk[base + g], seg_ld[base + g], r, n[f], chunk_dtype,
-                               0, 0.f, prec, d_status, workspace, s);
+      const ifk_segment& E = segs[base + g];
+      if (E.rows == 0) continue;
+      const int rc = fold_fp32(R[f], ldR[f], rr, E.chunk, E.ld, E.rows, n[f], chunk_dtype, 0, 0.f, prec, d_status,
+                               workspace, s, E.row_index, E.src_rows, E.cols);
       if (rc != IFK_OK) return rc;
-      rr = std::min<int64_t>(n[f], rr + r);
+      rr = std::min<int64_t>(n[f], rr + E.rows);
     }
     if (ident_tail && ident_tail[f] > 0) {
       const int rc = fold_fp32(R[f], ldR[f], rr, nullptr, 0, n[f], n[f], IFK_F32, 1, (float)ident_tail[f], prec,

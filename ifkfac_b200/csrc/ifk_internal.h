@@ -48,6 +48,9 @@ struct PFoldSeg {
   int xkind;     // 0 fp32, 1 bf16, 2 ident * I (X unused)
   float ident;
   int tri;
+  const int64_t* ridx = nullptr;  // device row indices into X (rows of them), or null: rows 0 .. rows-1
+  int64_t src_rows = 0;           // rows of X (bound for ridx)
+  int64_t cols = -1;              // columns of X read (n, or n - 1 with a column of ones after them); < 0: n
 };
 struct PFoldDesc {
   float* R;
@@ -65,7 +68,14 @@ inline PFoldDesc pfold_desc(float* R, int64_t ldR, int64_t n, int64_t rows_R) {
   return d;
 }
 inline void pfold_add(PFoldDesc& d, const void* X, int64_t ldX, int64_t rows, int xkind, float ident, int tri) {
-  d.seg[d.nseg++] = PFoldSeg{X, ldX, rows, xkind, ident, tri};
+  PFoldSeg g;
+  g.X = X;
+  g.ldX = ldX;
+  g.rows = rows;
+  g.xkind = xkind;
+  g.ident = ident;
+  g.tri = tri;
+  d.seg[d.nseg++] = g;
 }
 // sub-tiles of a fold (sum over its segments)
 int64_t pfold_subtiles(const PFoldDesc& d);
@@ -76,9 +86,12 @@ size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n);
 // one launch; every fold must have at most pfold_max_subtiles sub-tiles
 int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s);
 
-// chunk (bf16 or fp32, rows x n) -> X fp32
+// chunk (bf16 or fp32, rows x n) -> X fp32.  With ridx, row i is chunk row ridx[i]
+// (an index outside [0, src_rows) gives a zero row and IFK_ERR_ARG in *status);
+// with cols = n - 1, column n - 1 is ones.
 int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows,
-               int64_t n, int dtype, cudaStream_t s);
+               int64_t n, int dtype, cudaStream_t s, const int64_t* ridx = nullptr, int64_t src_rows = 0,
+               int64_t cols = -1, int* status = nullptr);
 // X = sqrt(damping) I (n x n)
 int fill_scaled_identity(float* X, int64_t ldX, int64_t n, float v, cudaStream_t s);
 // Rout = upper(Rin) * scale (n x n fp32)

@@ -238,12 +238,22 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
 
 template <typename Tin>
 __global__ void copy_chunk_kernel(float* X, int64_t ldX, const Tin* src, int64_t lds, int64_t rows,
-                                  int64_t n) {
+                                  int64_t n, const int64_t* ridx, int64_t src_rows, int64_t cols,
+                                  int* status) {
   const int64_t total = rows * n;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = idx / n, j = idx % n;
-    X[i * ldX + j] = ld_elem(src, i * lds + j);
+    int64_t si = i;
+    if (ridx) {
+      si = ridx[i];
+      if (si < 0 || si >= src_rows) {
+        if (status && j == 0) atomicExch(status, IFK_ERR_ARG);
+        X[i * ldX + j] = 0.f;
+        continue;
+      }
+    }
+    X[i * ldX + j] = j < cols ? ld_elem(src, si * lds + j) : 1.f;
   }
 }
 
@@ -316,14 +326,15 @@ size_t xw_bytes(int64_t rows, int64_t n) { return (size_t)rows * xw_ld(n) * size
 size_t fold_tbuf_bytes(int64_t rows) { return (size_t)cdiv(rows, SUB) * NB * NB * sizeof(float); }
 
 int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows, int64_t n,
-               int dtype, cudaStream_t s) {
+               int dtype, cudaStream_t s, const int64_t* ridx, int64_t src_rows, int64_t cols, int* status) {
   if (rows == 0) return IFK_OK;
+  if (cols < 0) cols = n;
   if (dtype == IFK_BF16)
     copy_chunk_kernel<<<grid_for(rows * n), 256, 0, s>>>(
-        X, ldX, (const __nv_bfloat16*)chunk, ld_chunk, rows, n);
+        X, ldX, (const __nv_bfloat16*)chunk, ld_chunk, rows, n, ridx, src_rows, cols, status);
   else
     copy_chunk_kernel<<<grid_for(rows * n), 256, 0, s>>>(X, ldX, (const float*)chunk, ld_chunk,
-                                                         rows, n);
+                                                         rows, n, ridx, src_rows, cols, status);
   IFK_CUDA_TRY(cudaGetLastError());
   return IFK_OK;
 }

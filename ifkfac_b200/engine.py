@@ -114,13 +114,61 @@ def fold_batched(factors: Sequence[Factor], chunks: Sequence[torch.Tensor], ws: 
     return ws
 
 
-def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence[torch.Tensor]], ws: torch.Tensor,
+class Rows:
+    """Rows of a 2-D device tensor for a fold, read in place by the fold kernels:
+    ``x[index]`` (``index`` an int64 device tensor, or None for every row), with a
+    column of ones appended when ``ones`` (the augmented-bias column).  The
+    reference's hooks copy both (``ifkfac/activation_hooks.py:531-543``)."""
+
+    def __init__(self, x: torch.Tensor, index: Optional[torch.Tensor] = None, ones: bool = False):
+        if x.dim() != 2:
+            raise ValueError(f"Rows needs a 2-D tensor, got shape {tuple(x.shape)}")
+        if x.dtype not in _DT:
+            x = x.float()
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        if index is not None:
+            index = index.to(device=x.device, dtype=torch.int64).contiguous()
+            if index.dim() != 1:
+                raise ValueError("Rows index must be 1-D")
+        self.x, self.index, self.ones = x, index, bool(ones)
+
+    @property
+    def rows(self) -> int:
+        return int(self.index.numel()) if self.index is not None else int(self.x.shape[0])
+
+    @property
+    def cols(self) -> int:
+        return int(self.x.shape[1]) + (1 if self.ones else 0)
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.x.dtype
+
+    @property
+    def device(self) -> torch.device:
+        return self.x.device
+
+    def materialize(self) -> torch.Tensor:
+        """The rows as a tensor of their own (what the reference's hooks build)."""
+        y = self.x[self.index] if self.index is not None else self.x
+        if self.ones:
+            y = torch.cat([y, torch.ones(y.shape[0], 1, device=y.device, dtype=y.dtype)], dim=1)
+        return y
+
+
+def as_rows(c) -> Rows:
+    return c if isinstance(c, Rows) else Rows(c)
+
+
+def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence], ws: torch.Tensor,
                   ident_tail: Optional[Sequence[float]] = None) -> torch.Tensor:
-    """Fold the chunks segments[i] into factors[i] in order, without concatenating
-    them: one persistent launch where they fit (ifk_tsqr_fold_segments), with the
-    result of folding them one after another.  ident_tail[i] > 0 appends the rows
-    ident_tail[i] * I (damping rows at the caller's scale); the factor then holds a
-    damped factor and is marked consumed until clear().
+    """Fold the chunks segments[i] (tensors or :class:`Rows`) into factors[i] in
+    order, without concatenating or gathering them: one persistent launch where
+    they fit (ifk_tsqr_fold_segments), with the result of folding them one after
+    another.  ident_tail[i] > 0 appends the rows ident_tail[i] * I (damping rows at
+    the caller's scale); the factor then holds a damped factor and is marked
+    consumed until clear().
 
     Returns the workspace actually used (grown if ``ws`` was too small)."""
     L = _lib.lib()
@@ -130,35 +178,37 @@ def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence[torch.T
             raise RuntimeError("factor was consumed by a fused refresh; clear() it first")
         cs = []
         for c in chunks:
-            if c.dim() != 2 or c.shape[1] != f.n:
-                raise ValueError(f"chunk of shape {tuple(c.shape)} for a factor of width {f.n}")
-            if c.shape[0] == 0:
+            r = as_rows(c)
+            if r.cols != f.n:
+                raise ValueError(f"rows of width {r.cols} for a factor of width {f.n}")
+            if r.rows == 0:
                 continue
-            cs.append(c if c.stride(1) == 1 else c.contiguous())
-            dts.add(cs[-1].dtype)
+            cs.append(r)
+            dts.add(r.dtype)
         segs.append(cs)
     if len(dts) > 1:
         raise TypeError("all chunks of a segmented fold must share one dtype")
     dt = _DT[dts.pop()] if dts else _lib.BF16
     nf = len(factors)
-    flat = [c for cs in segs for c in cs]
+    flat = [r for cs in segs for r in cs]
+    arr = (_lib.Segment * max(len(flat), 1))()
+    for i, r in enumerate(flat):
+        arr[i] = _lib.Segment(r.x.data_ptr(), r.x.stride(0), r.rows,
+                              r.index.data_ptr() if r.index is not None else None, r.x.shape[0], r.x.shape[1])
     ns = _arr(ctypes.c_int64, [f.n for f in factors])
     nseg = _arr(ctypes.c_int, [len(cs) for cs in segs])
-    rows = _arr(ctypes.c_int64, [c.shape[0] for c in flat] or [0])
     tail = _arr(ctypes.c_double, [float(v) for v in ident_tail]) if ident_tail is not None else None
-    need = L.ifk_tsqr_fold_segments_workspace(nf, ns, nseg, rows, tail)
+    need = L.ifk_tsqr_fold_segments_workspace(nf, ns, nseg, arr, tail)
     if need == 0 and (flat or ident_tail):
         raise ValueError("ifk_tsqr_fold_segments_workspace rejected the shapes")
     if ws is None or ws.numel() < need:
         ws = _ws(need, factors[0].device)
     check(L.ifk_tsqr_fold_segments(
         nf, _arr(ctypes.c_void_p, [f.R.data_ptr() for f in factors]), ns,
-        _arr(ctypes.c_int64, [f.rows_R for f in factors]), ns, nseg,
-        _arr(ctypes.c_void_p, [c.data_ptr() for c in flat] or [None]),
-        _arr(ctypes.c_int64, [c.stride(0) for c in flat] or [0]), rows, dt, tail, factors[0].prec,
+        _arr(ctypes.c_int64, [f.rows_R for f in factors]), ns, nseg, arr, dt, tail, factors[0].prec,
         factors[0].status.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "ifk_tsqr_fold_segments")
     for i, (f, cs) in enumerate(zip(factors, segs)):
-        p = sum(c.shape[0] for c in cs)
+        p = sum(r.rows for r in cs)
         f.rows_R = min(f.n, f.rows_R + p)
         f.rows_seen += p
         if ident_tail is not None and ident_tail[i] > 0:
@@ -201,10 +251,12 @@ class LayerCurvature:
         self.fx.status = self.status
         self.fg.status = self.status
         # fold workspace of a full window (with the damping rows of a fused refresh)
-        rows = [max(chunk_rows, 1)] * self.window
+        segs = (_lib.Segment * (2 * self.window))()
+        for i in range(2 * self.window):
+            segs[i] = _lib.Segment(None, 0, max(chunk_rows, 1), None, 0, 0)
         self.ws_pair = _ws(L.ifk_tsqr_fold_segments_workspace(
-            2, _arr(ctypes.c_int64, [n_in, n_out]), _arr(ctypes.c_int, [self.window] * 2),
-            _arr(ctypes.c_int64, rows * 2), _arr(ctypes.c_double, [1.0, 1.0])), self.device)
+            2, _arr(ctypes.c_int64, [n_in, n_out]), _arr(ctypes.c_int, [self.window] * 2), segs,
+            _arr(ctypes.c_double, [1.0, 1.0])), self.device)
 
     def fold(self, x_chunk: torch.Tensor, g_chunk: torch.Tensor) -> None:
         """Fold an activation chunk into R_X and a gradient chunk into R_G together
@@ -239,7 +291,7 @@ class LayerCurvature:
         same launch into the running factors, which are then only good for clear();
         the damped factor is the result scaled by 1 / sqrt(p)."""
         fs, outs = (self.fx, self.fg), (self.RX, self.RG)
-        pend = [sum(c.shape[0] for c in cs) for cs in zip(*self._pending)] if self._pending else [0, 0]
+        pend = [sum(as_rows(c).rows for c in cs) for cs in zip(*self._pending)] if self._pending else [0, 0]
         square = all(min(f.n, f.rows_R + p) >= f.n for f, p in zip(fs, pend))
         fused = consume and damping > 0 and square
         if fused:

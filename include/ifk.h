@@ -128,35 +128,55 @@ IFK_API int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ld
                           int chunk_dtype, int prec, int flags, int* d_status,
                           void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
+/*
+ * One segment of rows for ifk_tsqr_fold_segments.  Row i of the segment
+ * (i < rows) is row row_index[i] of `chunk` when row_index (a device array of
+ * `rows` int64) is given, else row i: the reference's random row subsample
+ * (x[randperm(rows)[:k]], ifkfac/activation_hooks.py:531-538) is read in
+ * place instead of copied.  The chunk holds `cols` columns with leading
+ * dimension `ld` (elements); cols is the factor's n, or n - 1, in which case a
+ * column of ones is appended (the augmented-bias column of
+ * ifkfac/activation_hooks.py:541-543).  src_rows is the chunk's row count: an
+ * index outside [0, src_rows) reads as a zero row and sets IFK_ERR_ARG in the
+ * status word.
+ */
+typedef struct ifk_segment {
+  const void* chunk;
+  int64_t ld;
+  int64_t rows;
+  const int64_t* row_index;
+  int64_t src_rows;
+  int64_t cols;
+} ifk_segment;
+
 /* Workspace bytes for ifk_tsqr_fold_segments (same arguments). */
 IFK_API size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
-                                                const int64_t* seg_rows, const double* ident_tail);
+                                                const ifk_segment* segs, const double* ident_tail);
 
 /*
- * Fold a sequence of chunks ("segments") into each of nfolds factors, in
- * order, in one persistent launch where they fit (IFK_PREC_BF16): the result
- * is that of one ifk_tsqr_fold per segment in turn, with the same reflector
- * sequence (one sub-tile of rows after another), while the fold of segment
- * s + 1 overlaps that of segment s.  Fold f has nseg[f] segments; segment
- * arrays are flat, fold after fold.  Segment g is seg_rows[g] rows of
- * seg_chunk[g] (n[f] columns, leading dimension seg_ld[g], element type
- * chunk_dtype); the segments need not be adjacent in memory.  When
- * ident_tail is not NULL and ident_tail[f] > 0, n[f] more rows
- * ident_tail[f] * I follow the segments (the damping rows of ifk_finalize at
- * the caller's scale: a caller that then runs ifk_finalize with damping 0
- * and rows_total p gets the damped factor of lambda = ident_tail^2 / p).
- * R[f], ldR[f], rows_R[f] are as in ifk_tsqr_fold.
+ * Fold a sequence of segments of rows into each of nfolds factors, in order,
+ * in one persistent launch where they fit (IFK_PREC_BF16): the result is that
+ * of one ifk_tsqr_fold per segment in turn, with the same reflector sequence
+ * (one sub-tile of rows after another), while the fold of segment s + 1
+ * overlaps that of segment s.  Fold f has nseg[f] segments; `segs` is flat,
+ * fold after fold.  The segments need not be adjacent in memory; all have
+ * element type chunk_dtype.  When ident_tail is not NULL and
+ * ident_tail[f] > 0, n[f] more rows ident_tail[f] * I follow the segments
+ * (the damping rows of ifk_finalize at the caller's scale: a caller that then
+ * runs ifk_finalize with damping 0 and rows_total p gets the damped factor of
+ * lambda = ident_tail^2 / p).  R[f], ldR[f], rows_R[f] are as in
+ * ifk_tsqr_fold.
  *
  * Replaces the deferred drain of the hooks, which concatenates the buffered
  * chunks and folds them with one streaming_tsqr_update
  * (ifkfac/activation_hooks.py:347-364, 560-570, 627-635), without the
- * concatenation; and a run of streaming_tsqr_update calls over row tiles that
- * are all resident (ifkfac/triangular.py:246-307).
+ * concatenation; a run of streaming_tsqr_update calls over row tiles that are
+ * all resident (ifkfac/triangular.py:246-307); and the hooks' row subsample
+ * and bias column (ifkfac/activation_hooks.py:519-548) without the copies.
  */
 IFK_API int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR,
                                    const int64_t* rows_R, const int64_t* n, const int* nseg,
-                                   const void* const* seg_chunk, const int64_t* seg_ld,
-                                   const int64_t* seg_rows, int chunk_dtype,
+                                   const ifk_segment* segs, int chunk_dtype,
                                    const double* ident_tail, int prec, int* d_status,
                                    void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 

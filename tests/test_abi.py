@@ -48,3 +48,38 @@ def test_argument_errors_before_any_gpu_work():
     assert L.ifk_tsqr_fold(fake, 64, 0, fake, 64, 10, 64, _lib.F32, 0, 0, None, fake, 16, None) == _lib.ERR_WORKSPACE
     assert L.ifk_natgrad(fake, 8, fake, 8, fake, 4, 9, fake, 8, 4, 8, 0, None, fake, 256, None) == _lib.ERR_DTYPE
     assert L.ifk_update(None, None, fake, 4, 0.1, 0.0, 0.0, 0.0, 0, None, 0, None) == _lib.ERR_ARG
+
+
+def test_segment_struct_matches_header():
+    """ctypes mirror of ifk_segment: the field order and offsets of include/ifk.h."""
+    import re
+    body = re.search(r"typedef struct ifk_segment \{(.*?)\} ifk_segment;", open(_lib.HEADER).read(), re.S).group(1)
+    fields = re.findall(r"(\w+);", body)
+    assert fields == [f for f, _ in _lib.Segment._fields_]
+    assert ctypes.sizeof(_lib.Segment) == 48
+    assert _lib.Segment.cols.offset == 40
+
+
+def test_segment_fold_argument_errors_before_any_gpu_work():
+    L = _lib.lib()
+    a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
+    n = 64
+    seg = lambda rows=100, ld=64, cols=64, chunk=0x1000, idx=None, src=0: (_lib.Segment * 1)(
+        _lib.Segment(chunk, ld, rows, idx, src, cols))
+    call = lambda segs, ntail=None, rows_R=0: L.ifk_tsqr_fold_segments(
+        1, (ctypes.c_void_p * 1)(0x2000), a64(n), a64(rows_R), a64(n), (ctypes.c_int * 1)(1), segs, _lib.BF16,
+        (ctypes.c_double * 1)(ntail) if ntail is not None else None, _lib.PREC_BF16, None, None, 0, None)
+    assert call(seg(cols=62)) == _lib.ERR_SHAPE            # neither n nor n - 1 columns
+    assert call(seg(cols=63, ld=62)) == _lib.ERR_SHAPE     # leading dimension below the columns
+    assert call(seg(rows=-1)) == _lib.ERR_SHAPE
+    assert call(seg(chunk=None)) == _lib.ERR_ARG
+    assert call(seg(idx=0x3000, src=0)) == _lib.ERR_SHAPE  # gathered rows need the source's row count
+    assert call(seg(), ntail=float("nan")) == _lib.ERR_ARG
+    assert call(seg(), rows_R=n + 1) == _lib.ERR_SHAPE
+    assert call(seg(rows=0)) == _lib.OK                    # nothing to fold
+    assert call(seg(cols=63)) == _lib.ERR_WORKSPACE        # valid (bias column), but no workspace
+    ws = L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(1), seg(rows=1000), None)
+    assert ws >= L.ifk_tsqr_fold_workspace(1000, n) // 2 and ws > 0
+    wt = L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(1), seg(rows=1000),
+                                            (ctypes.c_double * 1)(1.0))
+    assert wt >= ws                                       # the damping rows add sub-tiles

@@ -146,16 +146,19 @@ def test_segments_argument_errors():
     ws = torch.empty(1 << 26, dtype=torch.uint8, device="cuda")
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
-    call = lambda rows, ld, ptr, tail=None, rows_R=0: L.ifk_tsqr_fold_segments(
-        1, (ctypes.c_void_p * 1)(R.data_ptr()), a64(n), a64(rows_R), a64(n), (ctypes.c_int * 1)(1),
-        (ctypes.c_void_p * 1)(ptr), a64(ld), a64(rows), _lib.BF16,
-        (ctypes.c_double * 1)(tail) if tail is not None else None, _lib.PREC_BF16, st.data_ptr(),
-        ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+
+    def call(rows, ld, ptr, tail=None, rows_R=0, cols=n):
+        seg = (_lib.Segment * 1)(_lib.Segment(ptr, ld, rows, None, 0, cols))
+        return L.ifk_tsqr_fold_segments(
+            1, (ctypes.c_void_p * 1)(R.data_ptr()), a64(n), a64(rows_R), a64(n), (ctypes.c_int * 1)(1), seg,
+            _lib.BF16, (ctypes.c_double * 1)(tail) if tail is not None else None, _lib.PREC_BF16,
+            st.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
     assert call(-1, n, x.data_ptr()) == _lib.ERR_SHAPE
     assert call(300, n - 1, x.data_ptr()) == _lib.ERR_SHAPE
     assert call(300, n, None) == _lib.ERR_ARG
     assert call(300, n, x.data_ptr(), tail=float("nan")) == _lib.ERR_ARG
     assert call(300, n, x.data_ptr(), rows_R=n + 1) == _lib.ERR_SHAPE
+    assert call(300, n, x.data_ptr(), cols=n - 2) == _lib.ERR_SHAPE
     assert call(0, n, None) == _lib.OK  # nothing to fold
     assert call(300, n, x.data_ptr()) == _lib.OK
     torch.cuda.synchronize()

@@ -20,26 +20,34 @@ def test_refresh_schedule_matches_oracle():
 def test_prepare_x_sequence_flatten_bias_and_subsample():
     lin = nn.Linear(6, 4)
     x = torch.randn(2, 5, 6)
-    c = AH.prepare_x(x, lin, 512, 0, True)
+    r = AH.prepare_x(x, lin, 512, 0, True)
+    assert (r.rows, r.cols, r.ones, r.index) == (10, 7, True, None)
+    assert r.x.data_ptr() == x.data_ptr()             # the 3-D reshape is a view: nothing copied
+    c = r.materialize()
     assert c.shape == (10, 7) and torch.all(c[:, -1] == 1)
     assert torch.equal(c[:, :6], x.reshape(-1, 6))
     torch.manual_seed(0)
-    c2 = AH.prepare_x(x, lin, 512, 4, False)          # randperm row subsample to max_seq_rows
-    assert c2.shape == (4, 6)
-    rows = {tuple(r.tolist()) for r in x.reshape(-1, 6)}
-    assert all(tuple(r.tolist()) in rows for r in c2)
-    assert AH.prepare_x(torch.randn(3, 6), nn.Linear(6, 4, bias=False), 512, 0, True).shape == (3, 6)
+    r2 = AH.prepare_x(x, lin, 512, 4, False)          # randperm row subsample to max_seq_rows
+    assert r2.rows == 4 and r2.cols == 6 and r2.x.data_ptr() == x.data_ptr()
+    torch.manual_seed(0)
+    assert torch.equal(r2.index, torch.randperm(10)[:4])   # the reference's draw, kept as indices
+    rows = {tuple(t.tolist()) for t in x.reshape(-1, 6)}
+    assert all(tuple(t.tolist()) in rows for t in r2.materialize())
+    assert AH.prepare_x(torch.randn(3, 6), nn.Linear(6, 4, bias=False), 512, 0, True).cols == 6
+    # a chunk transform sees the materialised rows and its output is folded
+    t = AH.prepare_x(x, lin, 512, 0, True, transform=lambda m: m * 2)
+    assert torch.is_tensor(t) and torch.equal(t, 2 * c)
 
 
 def test_prepare_conv_im2col_and_grad_layout():
     conv = nn.Conv2d(3, 5, kernel_size=3, padding=1)
     x = torch.randn(2, 3, 4, 4)
-    c = AH.prepare_x(x, conv, 0, 0, False)
+    c = AH.prepare_x(x, conv, 0, 0, False).materialize()
     assert c.shape == (2 * 16, 3 * 9)
     d = torch.randn(2, 5, 4, 4)
-    g = AH.prepare_g(d, conv, 0)
+    g = AH.prepare_g(d, conv, 0).materialize()
     assert g.shape == (32, 5) and torch.equal(g[0], d[0, :, 0, 0])
-    assert AH.prepare_x(x, conv, 8, 0, False).shape == (8, 27)    # max_conv_rows cap
+    assert AH.prepare_x(x, conv, 8, 0, False).rows == 8                  # max_conv_rows cap
 
 
 def test_layer_selection_and_constructor_contract():
