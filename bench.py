@@ -468,6 +468,95 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(out), flush=True)
 
 
+def run_c3(args, rank, world, local_rank):
+    """8-layer MLP (1024 -> 2048, 6 x 2048 -> 2048, 2048 -> 100, ReLU), batch
+    4096, x ~ N(0,1), random labels, bf16 autocast forward, use_true_bf16, factor_update_freq 10,
+    momentum 0.9.  A step is forward + backward + IFKFAC.step (one refresh every 10 steps, so the
+    timed steps are a multiple of 10).  The same steps are timed with the per-layer apply
+    ("per_layer_apply") to show the batched solves of ifk_natgrad_batched."""
+    import copy
+    import torch
+    from ifkfac_b200.ifkfac import IFKFAC
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(0)
+    dims = [1024] + [2048] * 7 + [100]
+    layers = []
+    for i in range(8):
+        layers.append(torch.nn.Linear(dims[i], dims[i + 1]))
+        if i < 7:
+            layers.append(torch.nn.ReLU())
+    torch.manual_seed(0)
+    base = torch.nn.Sequential(*layers).to(dev)
+    x = torch.randn(4096, 1024, generator=g, device=dev)
+    y = torch.randint(0, 100, (4096,), generator=g, device=dev)
+    steps = max(10, (args.steps + 9) // 10 * 10)
+
+    def timed(batched):
+        model = copy.deepcopy(base)
+        opt = IFKFAC(model, lr=1e-3, damping=1e-2, factor_update_freq=10, momentum=0.9, use_true_bf16=True,
+                     batched_qr=args.c3_batched_qr)
+        if not batched:
+            opt._batched_natgrads = lambda modules: {}
+
+        def one():
+            opt.zero_grad()
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = model(x)
+            loss = torch.nn.functional.cross_entropy(out.float(), y)
+            loss.backward()
+            opt.step()
+            return loss
+
+        for _ in range(max(args.warmup, 10)):  # past the first refresh
+            one()
+        torch.cuda.synchronize()
+        if args.profile:
+            # a refresh step (the 20th) and a plain one, each in its own range, for a profiler
+            for k in range(10):
+                if k == 9:
+                    torch.cuda.nvtx.range_push("ifk_profile_step")
+                one()
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.nvtx.range_push("ifk_profile_plain_step")
+            one()
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.synchronize()
+            return 0.0, 0.0
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            loss = one()
+        b.record()
+        b.synchronize()
+        opt.cleanup()
+        return a.elapsed_time(b) / steps, float(loss.item())
+
+    # the apply variants alternate (batched, per-layer, batched, per-layer) so that
+    # the order of the runs in the process does not favour either; each keeps its best
+    if args.profile:
+        timed(not args.c3_per_layer_apply)
+        return
+    with ClockSampler(local_rank) as clk:
+        runs = [timed(not args.c3_per_layer_apply)]
+        if not args.c3_per_layer_apply:
+            runs += [timed(False), timed(True), timed(False)]
+    ms, loss = min(runs[0::2]) if not args.c3_per_layer_apply else runs[0]
+    ms_pl = None if args.c3_per_layer_apply else min(r[0] for r in runs[1::2])
+    out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
+           "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 10),
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic",
+           "config": {"workload": "C3 8-layer MLP 1024-2048x7-100, batch 4096, bf16 autocast, use_true_bf16, "
+                                  "factor_update_freq 10, momentum 0.9", "final_loss": loss,
+                      "timing": "eager, CUDA events around the step loop (host work included); best of 2 runs "
+                                "of each apply, alternated"},
+           "batched_qr": args.c3_batched_qr, "apply": "per-layer" if args.c3_per_layer_apply else "batched",
+           "per_layer_apply": {"ms_per_step": ms_pl, "value": 1000.0 / ms_pl} if ms_pl else None,
+           "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
 def cpu_baseline(scale=1.0):
     """The oracle port (scipy LAPACK fp32, the reference's algorithm) on host cores,
     timed on a bounded sample and extrapolated to one operator."""
@@ -536,6 +625,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=["c2", "c3"], default="c2",
+                    help="c2: the single-layer operator (the headline); c3: the 8-layer MLP training step")
+    ap.add_argument("--c3-batched-qr", action="store_true",
+                    help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
+    ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
     ap.add_argument("--schedule", choices=["one-launch", "per-tile"], default="one-launch",
                     help="fold schedule of the timed step (the other one is reported beside it)")
     ap.add_argument("--e2e-groups", default="1",
@@ -557,6 +651,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
+        return
+    if args.config == "c3":
+        if rank == 0:
+            run_c3(args, rank, world, local_rank)
         return
     if world > 1:
         import datetime

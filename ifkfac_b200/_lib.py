@@ -48,6 +48,9 @@ SIGNATURES = {
                            _vp, _sz, _vp]),
     "ifk_natgrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int,
                                    _vp, _vp]),
+    "ifk_natgrad_batched_workspace": (_sz, [_int, _vp, _vp]),
+    "ifk_natgrad_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _int,
+                                   _vp, _vp, _sz, _vp]),
     "ifk_natgrad_bias": (_int, [_vp, _vp, _i64, _int, _vp, _i64, _int, _vp, _sz, _vp]),
     "ifk_update_workspace": (_sz, [_i64]),
     "ifk_update": (_int, [_vp, _vp, _vp, _i64, _dbl, _dbl, _dbl, _dbl, _int, _vp, _sz, _vp]),

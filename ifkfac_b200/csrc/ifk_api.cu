@@ -591,6 +591,122 @@ int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_r
   return trsm_run(R_X, ld_rx, r_dtype, 0, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s);
 }
 
+// a layer's slice of the batched workspace: ifk_natgrad's | the bias solves' scratch
+static size_t natgrad_batched_slice(int64_t n_out, int64_t n_in) {
+  return ifk_natgrad_workspace(n_out, n_in) + align_up(trsm_persist_workspace(n_out, 1));
+}
+
+size_t ifk_natgrad_batched_workspace(int nlayers, const int64_t* n_out, const int64_t* n_in) {
+  if (nlayers <= 0 || !n_out || !n_in) return 0;
+  size_t b = 0;
+  for (int l = 0; l < nlayers; ++l) {
+    if (n_out[l] <= 0 || n_in[l] <= 0) return 0;
+    b += natgrad_batched_slice(n_out[l], n_in[l]);
+  }
+  return b;
+}
+
+int ifk_natgrad_batched(int nlayers, const float* const* grad_W, const int64_t* ld_g, const void* const* R_X,
+                        const int64_t* ld_rx, const void* const* R_G, const int64_t* ld_rg, int r_dtype,
+                        float* const* nat, const int64_t* ld_nat, const int64_t* n_out, const int64_t* n_in,
+                        const float* const* grad_b, float* const* nat_b, int prec, int* d_status, void* workspace,
+                        size_t workspace_bytes, ifk_stream_t stream) {
+  if (nlayers < 0 || (nlayers > 0 && (!grad_W || !ld_g || !R_X || !ld_rx || !R_G || !ld_rg || !nat || !ld_nat ||
+                                      !n_out || !n_in)))
+    return IFK_ERR_ARG;
+  if ((grad_b == nullptr) != (nat_b == nullptr)) return IFK_ERR_ARG;
+  auto has_bias = [&](int l) { return grad_b && grad_b[l]; };
+  for (int l = 0; l < nlayers; ++l)
+    if (grad_b && (grad_b[l] == nullptr) != (nat_b[l] == nullptr)) return IFK_ERR_ARG;
+  if (!dtype_ok(r_dtype)) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec)) return IFK_ERR_ARG;
+  for (int l = 0; l < nlayers; ++l) {
+    if (!grad_W[l] || !R_X[l] || !R_G[l] || !nat[l]) return IFK_ERR_ARG;
+    if (n_out[l] <= 0 || n_in[l] <= 0 || ld_g[l] < n_in[l] || ld_nat[l] < n_in[l] || ld_rx[l] < n_in[l] ||
+        ld_rg[l] < n_out[l])
+      return IFK_ERR_SHAPE;
+  }
+  if (nlayers == 0) return IFK_OK;
+  if (!workspace || !aligned(workspace) ||
+      workspace_bytes < ifk_natgrad_batched_workspace(nlayers, n_out, n_in))
+    return IFK_ERR_WORKSPACE;
+  if (prec == IFK_PREC_AUTO) prec = r_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  cudaStream_t s = S(stream);
+  // each layer owns the slice of the workspace ifk_natgrad would take, then its bias scratch
+  std::vector<char*> wsl((size_t)nlayers);
+  {
+    char* w = (char*)workspace;
+    for (int l = 0; l < nlayers; ++l) {
+      wsl[l] = w;
+      w += natgrad_batched_slice(n_out[l], n_in[l]);
+    }
+  }
+  // the layers of the persistent bf16 path share launches; the others go one by one
+  std::vector<int> batch;
+  for (int l = 0; l < nlayers; ++l) {
+    const bool pers = prec == IFK_PREC_BF16 && r_dtype == IFK_BF16 && trsm_persist_ok(R_G[l], ld_rg[l], n_out[l]) &&
+                      trsm_persist_ok(R_X[l], ld_rx[l], n_in[l]);
+    if (pers) {
+      batch.push_back(l);
+      continue;
+    }
+    int rc = ifk_natgrad(grad_W[l], ld_g[l], R_X[l], ld_rx[l], R_G[l], ld_rg[l], r_dtype, nat[l], ld_nat[l],
+                         n_out[l], n_in[l], prec, d_status, wsl[l], ifk_natgrad_workspace(n_out[l], n_in[l]),
+                         stream);
+    if (rc != IFK_OK) return rc;
+    if (has_bias(l)) {
+      rc = ifk_natgrad_bias(grad_b[l], R_G[l], ld_rg[l], r_dtype, nat_b[l], n_out[l], prec, nullptr, 0, stream);
+      if (rc != IFK_OK) return rc;
+    }
+  }
+  const int nb = (int)batch.size();
+  if (nb == 0) return IFK_OK;
+  // layout of a layer's slice: inverses of R_G | inverses of R_X | solve scratch (as ifk_natgrad)
+  std::vector<const __nv_bfloat16*> A((size_t)2 * nb);
+  std::vector<int64_t> ld((size_t)2 * nb), nn((size_t)2 * nb);
+  std::vector<void*> inv((size_t)2 * nb);
+  std::vector<TrsmProblem> pg((size_t)nb), px((size_t)nb), pl;
+  for (int i = 0; i < nb; ++i) {
+    const int l = batch[i];
+    if (nat[l] != grad_W[l] || ld_nat[l] != ld_g[l])
+      IFK_CUDA_TRY(cudaMemcpy2DAsync(nat[l], ld_nat[l] * sizeof(float), grad_W[l], ld_g[l] * sizeof(float),
+                                     n_in[l] * sizeof(float), n_out[l], cudaMemcpyDeviceToDevice, s));
+    uint8_t* inv_g = (uint8_t*)wsl[l];
+    uint8_t* inv_x = inv_g + align_up(trsm_persist_inverse_bytes(n_out[l]));
+    uint8_t* scratch = inv_x + align_up(trsm_persist_inverse_bytes(n_in[l]));
+    A[2 * i] = (const __nv_bfloat16*)R_G[l];
+    ld[2 * i] = ld_rg[l];
+    nn[2 * i] = n_out[l];
+    inv[2 * i] = inv_g;
+    A[2 * i + 1] = (const __nv_bfloat16*)R_X[l];
+    ld[2 * i + 1] = ld_rx[l];
+    nn[2 * i + 1] = n_in[l];
+    inv[2 * i + 1] = inv_x;
+    // left solves on the columns of nat, right solves on its transposed view
+    pg[i] = TrsmProblem{(const __nv_bfloat16*)R_G[l], ld_rg[l], nat[l], ld_nat[l], 1, n_out[l], n_in[l], inv_g, scratch};
+    px[i] = TrsmProblem{(const __nv_bfloat16*)R_X[l], ld_rx[l], nat[l], 1, ld_nat[l], n_in[l], n_out[l], inv_x, scratch};
+    if (has_bias(l)) {
+      // the bias: one more right-hand side of the left solves (R_G^-1 R_G^-T g_b), own scratch
+      if (nat_b[l] != grad_b[l])
+        IFK_CUDA_TRY(cudaMemcpyAsync(nat_b[l], grad_b[l], n_out[l] * sizeof(float), cudaMemcpyDeviceToDevice, s));
+      pl.push_back(TrsmProblem{(const __nv_bfloat16*)R_G[l], ld_rg[l], nat_b[l], 1, 1, n_out[l], 1, inv_g,
+                               wsl[l] + ifk_natgrad_workspace(n_out[l], n_in[l])});
+    }
+  }
+  std::vector<TrsmProblem> left(pg);
+  left.insert(left.end(), pl.begin(), pl.end());
+  int rc = trsm_persist_prepare_many(2 * nb, A.data(), ld.data(), nn.data(), inv.data(), s);
+  if (rc != IFK_OK) return rc;
+  // R_G^T T1 = g; R_G T2 = T1; R_X^T T3^T = T2^T; R_X T4^T = T3^T, each stage for every layer at once
+  rc = trsm_persist_run_many((int)left.size(), left.data(), 1, d_status, s);
+  if (rc != IFK_OK) return rc;
+  rc = trsm_persist_run_many((int)left.size(), left.data(), 0, d_status, s);
+  if (rc != IFK_OK) return rc;
+  rc = trsm_persist_run_many(nb, px.data(), 1, d_status, s);
+  if (rc != IFK_OK) return rc;
+  return trsm_persist_run_many(nb, px.data(), 0, d_status, s);
+}
+
 int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_dtype, float* nat_b,
                      int64_t n_out, int prec, void* workspace, size_t workspace_bytes,
                      ifk_stream_t stream) {

@@ -124,6 +124,21 @@ int trsm_persist_prepare(const __nv_bfloat16* A0, int64_t ld0, int64_t n0, void*
                          int64_t ld1, int64_t n1, void* inv1, cudaStream_t s);
 int trsm_persist_run(const __nv_bfloat16* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t cs,
                      int64_t n, int64_t N, const void* inv, void* ws, int* err, cudaStream_t s);
+// Several solves with the same op in one pack launch and one solve launch (groups
+// of TRSM_MAX_PROBLEMS); each problem has its own trsm_persist_workspace scratch.
+constexpr int TRSM_MAX_PROBLEMS = 64;
+struct TrsmProblem {
+  const __nv_bfloat16* A;
+  int64_t ldA;
+  float* B;
+  int64_t rs, cs, n, N;
+  const void* inv;
+  void* ws;
+};
+int trsm_persist_run_many(int np, const TrsmProblem* p, int trans, int* err, cudaStream_t s);
+// diagonal-block inverses of nm factors in one launch (groups of 2 TRSM_MAX_PROBLEMS)
+int trsm_persist_prepare_many(int nm, const __nv_bfloat16* const* A, const int64_t* ld, const int64_t* n,
+                              void* const* inv, cudaStream_t s);
 
 int update_run(float* W, float* buf, const float* nat, int64_t count, double lr, double mom,
                double wd, double clip, int buf_is_new, double* norm_ws, cudaStream_t s);

@@ -34,6 +34,7 @@ constexpr int NB2 = 128;  // diagonal block
 constexpr int NT = 32;    // right-hand-side columns per CTA
 constexpr int NSTAGE = 3;
 constexpr int TPB = 192;
+constexpr int MAXP = TRSM_MAX_PROBLEMS;
 
 constexpr uint32_t SZ_A = NB2 * NB2 * 2;  // 32 KB
 constexpr uint32_t SZ_X = NB2 * NT * 2;   // 8 KB
@@ -54,6 +55,45 @@ constexpr uint32_t X_N = 128, X_K = (NT / 8) * 128;    // X / Y tiles (MN-major)
 constexpr uint32_t TM_D0 = 0, TM_D1 = NT, TM_X = 2 * NT, TM_COLS = 128;
 constexpr size_t INV_SMEM = 2 * sizeof(float) * NB2 * (NB2 + 1);
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+// One launch serves up to MAXP problems (the layers of a batched natural
+// gradient); a block finds its problem by binary search over the prefix of the
+// blocks each problem takes.
+struct PackBatch {
+  const __nv_bfloat16* A[MAXP];
+  int64_t ldA[MAXP], n[MAXP];
+  uint8_t* tiles[MAXP];
+  int blk0[MAXP + 1];
+  int np, trans;
+};
+struct InvBatch {
+  const __nv_bfloat16* A[2 * MAXP];
+  int64_t ld[2 * MAXP], n[2 * MAXP];
+  uint8_t* inv[2 * MAXP];
+  int blk0[2 * MAXP + 1];
+  int nm;
+};
+struct SolveBatch {
+  const uint8_t* tiles[MAXP];
+  float* B[MAXP];
+  int64_t rs[MAXP], cs[MAXP], n[MAXP], N[MAXP];
+  const __nv_bfloat16* inv[MAXP];
+  __nv_bfloat16* xws[MAXP];
+  int vb[MAXP];
+  int blk0[MAXP + 1];
+  int np, trans;
+  int* err;
+};
+// problem q with blk0[q] <= block < blk0[q + 1]
+__device__ __forceinline__ int find_problem(const int* blk0, int np, int block) {
+  int lo = 0, hi = np;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (blk0[mid] <= block) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ uint32_t bar_addr(uint32_t sb, int i) { return sb + OFF_BAR + 8u * (uint32_t)i; }
 
@@ -104,10 +144,14 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
 // op = A^T: tile op(A)_{b,a} = A_ab^T, MN-major (mn = column, k = row).
 // Tile index b (b - 1) / 2 + a; one CTA per tile, staged through shared memory
 // so both the reads of A and the writes of the image are contiguous.
-__global__ void __launch_bounds__(256) pack_tiles_kernel(const __nv_bfloat16* A, int64_t ldA_, int64_t n, int trans,
-                                                         uint8_t* tiles) {
+__global__ void __launch_bounds__(256) pack_tiles_kernel(const __grid_constant__ PackBatch pb) {
   extern __shared__ __align__(16) uint8_t img[];
-  const int t = blockIdx.x;
+  const int q = find_problem(pb.blk0, pb.np, (int)blockIdx.x);
+  const __nv_bfloat16* A = pb.A[q];
+  const int64_t ldA_ = pb.ldA[q], n = pb.n[q];
+  const int trans = pb.trans;
+  uint8_t* tiles = pb.tiles[q];
+  const int t = (int)blockIdx.x - pb.blk0[q];
   int b = (int)((1.0 + sqrt(1.0 + 8.0 * t)) * 0.5);
   while (b * (b - 1) / 2 > t) --b;
   while ((b + 1) * b / 2 <= t) ++b;
@@ -130,19 +174,16 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(const __nv_bfloat16* A,
 // written as bf16 hi / lo in both operand layouts: the K-major tile of inv(A_bb)
 // (op = A) and the MN-major tile of its transpose (op = A^T).  Block b of matrix
 // m in [hi K, lo K, hi MN, lo MN] order (SZ_A each) at inv_m + b * 4 * SZ_A.
-// One launch covers two matrices: blocks [0, nblk0) of A0, then those of A1.
-// Ragged last block: identity pad.
-__global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __nv_bfloat16* A0, int64_t ld0, int64_t n0,
-                                                                  uint8_t* inv0, const __nv_bfloat16* A1,
-                                                                  int64_t ld1, int64_t n1, uint8_t* inv1) {
+// One launch covers every block of a list of matrices.  Ragged last block:
+// identity pad.
+__global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __grid_constant__ InvBatch ib) {
   extern __shared__ float dsm[];
   float (*U)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm);
   float (*Xs)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm + NB2 * (NB2 + 1));
-  const int nblk0 = (int)cdiv(n0, NB2);
-  const bool second = (int)blockIdx.x >= nblk0;
-  const __nv_bfloat16* A = second ? A1 : A0;
-  const int64_t ldA_ = second ? ld1 : ld0, n = second ? n1 : n0;
-  const int b = second ? (int)blockIdx.x - nblk0 : (int)blockIdx.x, q = threadIdx.x;
+  const int mat = find_problem(ib.blk0, ib.nm, (int)blockIdx.x);
+  const __nv_bfloat16* A = ib.A[mat];
+  const int64_t ldA_ = ib.ld[mat], n = ib.n[mat];
+  const int b = (int)blockIdx.x - ib.blk0[mat], q = threadIdx.x;
   const int64_t b0 = (int64_t)b * NB2;
   const int nb = (int)mn<int64_t>(NB2, n - b0);
   for (int idx = q; idx < NB2 * NB2; idx += NB2) {
@@ -166,7 +207,7 @@ __global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __nv_bfl
     Xs[r][q] = ((s0 + s1) + (s2 + s3)) / U[r][r];
   }
   __syncthreads();
-  uint8_t* o = (second ? inv1 : inv0) + (size_t)b * 4 * SZ_A;
+  uint8_t* o = ib.inv[mat] + (size_t)b * 4 * SZ_A;
   for (int it = q; it < NB2 * (NB2 / 8); it += NB2) {
     // K-major: 8 consecutive k = l of row m; MN-major (transpose): 8 consecutive mn = l of k = m
     const int m = it >> 4, l8 = it & 15;
@@ -183,20 +224,27 @@ __global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __nv_bfl
   }
 }
 
-__global__ void __launch_bounds__(TPB, 1) trsm_persist_kernel(const uint8_t* tiles, int trans,
-                                                             float* B, int64_t rs, int64_t cs, int64_t n,
-                                                             int64_t N, const __nv_bfloat16* inv,
-                                                             __nv_bfloat16* xws, int* err, int vb) {
+__global__ void __launch_bounds__(TPB, 1) trsm_persist_kernel(const __grid_constant__ SolveBatch sbt) {
   extern __shared__ __align__(1024) uint8_t sm[];
+  const int prob = find_problem(sbt.blk0, sbt.np, (int)blockIdx.x);
+  const int bx = (int)blockIdx.x - sbt.blk0[prob];  // this CTA's column group within its problem
+  const uint8_t* tiles = sbt.tiles[prob];
+  const int trans = sbt.trans;
+  float* B = sbt.B[prob];
+  const int64_t rs = sbt.rs[prob], cs = sbt.cs[prob], n = sbt.n[prob], N = sbt.N[prob];
+  const __nv_bfloat16* inv = sbt.inv[prob];
+  __nv_bfloat16* xws = sbt.xws[prob];
+  int* err = sbt.err;
+  const int vb = sbt.vb[prob];
   const uint32_t sb = tc::smem_u32(sm);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
   volatile int* abort_ = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nblk = (int)cdiv(n, NB2);
-  const int64_t c0 = (int64_t)blockIdx.x * NT;
+  const int64_t c0 = (int64_t)bx * NT;
   const int nc = (int)mn<int64_t>(NT, N - c0);
   // this CTA's bf16 copies of its solved blocks: nblk tiles of 8 KB (MN-major B operand)
-  uint8_t* xmine = reinterpret_cast<uint8_t*>(xws) + (size_t)blockIdx.x * nblk * SZ_X;
+  uint8_t* xmine = reinterpret_cast<uint8_t*>(xws) + (size_t)bx * nblk * SZ_X;
 
   if (warp == 0) tc::tmem_alloc(tslot, TM_COLS);
   if (tid == 0) {
@@ -409,33 +457,91 @@ bool trsm_persist_ok(const void* A, int64_t ldA, int64_t n) {
   return ((uintptr_t)A % 16) == 0 && ldA % 8 == 0 && n % 8 == 0 && n >= 8;
 }
 
+int trsm_persist_prepare_many(int nm, const __nv_bfloat16* const* A, const int64_t* ld, const int64_t* n,
+                              void* const* inv, cudaStream_t s) {
+  if (!attr_once()) return IFK_ERR_CUDA;
+  for (int base = 0; base < nm; base += 2 * MAXP) {
+    InvBatch ib;
+    ib.nm = nm - base < 2 * MAXP ? nm - base : 2 * MAXP;
+    int acc = 0;
+    for (int m = 0; m < ib.nm; ++m) {
+      ib.A[m] = A[base + m];
+      ib.ld[m] = ld[base + m];
+      ib.n[m] = n[base + m];
+      ib.inv[m] = (uint8_t*)inv[base + m];
+      ib.blk0[m] = acc;
+      acc += (int)cdiv(n[base + m], NB2);
+    }
+    ib.blk0[ib.nm] = acc;
+    if (acc == 0) continue;
+    diag_inverse_layout_kernel<<<(unsigned)acc, NB2, INV_SMEM, s>>>(ib);
+    IFK_CUDA_TRY(cudaGetLastError());
+  }
+  return IFK_OK;
+}
+
 int trsm_persist_prepare(const __nv_bfloat16* A0, int64_t ld0, int64_t n0, void* inv0, const __nv_bfloat16* A1,
                          int64_t ld1, int64_t n1, void* inv1, cudaStream_t s) {
+  const __nv_bfloat16* A[2] = {A0, A1};
+  const int64_t ld[2] = {ld0, ld1}, n[2] = {n0, n1};
+  void* inv[2] = {inv0, inv1};
+  return trsm_persist_prepare_many(A1 ? 2 : 1, A, ld, n, inv, s);
+}
+
+int trsm_persist_run_many(int np, const TrsmProblem* p, int trans, int* err, cudaStream_t s) {
   if (!attr_once()) return IFK_ERR_CUDA;
-  const int64_t blocks = cdiv(n0, NB2) + (A1 ? cdiv(n1, NB2) : 0);
-  diag_inverse_layout_kernel<<<(unsigned)blocks, NB2, INV_SMEM, s>>>(A0, ld0, n0, (uint8_t*)inv0, A1, ld1, n1,
-                                                                       (uint8_t*)inv1);
-  IFK_CUDA_TRY(cudaGetLastError());
+  for (int base = 0; base < np; base += MAXP) {
+    const int cnt = np - base < MAXP ? np - base : MAXP;
+    PackBatch pb;
+    SolveBatch sbt;
+    pb.np = sbt.np = cnt;
+    pb.trans = sbt.trans = trans;
+    sbt.err = err;
+    int tacc = 0, cacc = 0;
+    for (int q = 0; q < cnt; ++q) {
+      const TrsmProblem& P = p[base + q];
+      const int64_t nblk = cdiv(P.n, NB2);
+      // workspace of a problem: bf16 X copies | packed tiles
+      uint8_t* w = (uint8_t*)P.ws;
+      __nv_bfloat16* xws = (__nv_bfloat16*)w;
+      w += (size_t)cdiv(P.N, NT) * nblk * SZ_X;
+      pb.A[q] = P.A;
+      pb.ldA[q] = P.ldA;
+      pb.n[q] = P.n;
+      pb.tiles[q] = w;
+      pb.blk0[q] = tacc;
+      tacc += (int)(nblk * (nblk - 1) / 2);
+      sbt.tiles[q] = w;
+      sbt.B[q] = P.B;
+      sbt.rs[q] = P.rs;
+      sbt.cs[q] = P.cs;
+      sbt.n[q] = P.n;
+      sbt.N[q] = P.N;
+      sbt.inv[q] = (const __nv_bfloat16*)P.inv;
+      sbt.xws[q] = xws;
+      // 16-byte vector access to rows of B needs 16-byte aligned rows
+      sbt.vb[q] = (((uintptr_t)P.B % 16) == 0 && (P.rs * 4) % 16 == 0) ? 1 : 0;
+      sbt.blk0[q] = cacc;
+      cacc += (int)cdiv(P.N, NT);
+    }
+    pb.blk0[cnt] = tacc;
+    sbt.blk0[cnt] = cacc;
+    if (tacc > 0) {
+      pack_tiles_kernel<<<(unsigned)tacc, 256, SZ_A, s>>>(pb);
+      IFK_CUDA_TRY(cudaGetLastError());
+    }
+    if (cacc > 0) {
+      trsm_persist_kernel<<<(unsigned)cacc, TPB, SMEM, s>>>(sbt);
+      IFK_CUDA_TRY(cudaGetLastError());
+    }
+  }
   return IFK_OK;
 }
 
 int trsm_persist_run(const __nv_bfloat16* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t cs, int64_t n,
                      int64_t N, const void* inv, void* ws, int* err, cudaStream_t s) {
-  if (!attr_once()) return IFK_ERR_CUDA;
-  const int64_t nblk = cdiv(n, NB2);
-  // workspace: bf16 X copies | packed tiles
-  uint8_t* w = (uint8_t*)ws;
-  __nv_bfloat16* xws = (__nv_bfloat16*)w;
-  w += (size_t)cdiv(N, NT) * nblk * SZ_X;
-  uint8_t* tiles = w;
-  const int64_t ntiles = nblk * (nblk - 1) / 2;
-  if (ntiles > 0) pack_tiles_kernel<<<(unsigned)ntiles, 256, SZ_A, s>>>(A, ldA, n, trans, tiles);
-  // 16-byte vector access to rows of B needs 16-byte aligned rows
-  const int vb = (((uintptr_t)B % 16) == 0 && (rs * 4) % 16 == 0) ? 1 : 0;
-  trsm_persist_kernel<<<(unsigned)cdiv(N, NT), TPB, SMEM, s>>>(tiles, trans, B, rs, cs, n, N,
-                                                               (const __nv_bfloat16*)inv, xws, err, vb);
-  IFK_CUDA_TRY(cudaGetLastError());
-  return IFK_OK;
+  const TrsmProblem p{A, ldA, B, rs, cs, n, N, inv, ws};
+  return trsm_persist_run_many(1, &p, trans, err, s);
 }
 
 }  // namespace ifk

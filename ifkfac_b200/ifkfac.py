@@ -69,6 +69,10 @@ class IFKFAC(torch.optim.Optimizer):
         self.grad_clip = grad_clip
         self.gamma = gamma
         self.augment_bias = augment_bias
+        # use_true_bf16 asks for bf16 factors: their folds run in bf16 mode (tensor cores)
+        # whatever the dtype of the captured rows, unless a precision is given
+        if use_true_bf16 and precision == _lib.PREC_AUTO:
+            precision = _lib.PREC_BF16
         self.precision = precision
         self.hooks = RawActivationHooks(model, damping=damping, max_out_dim=max_out_dim,
                                         augment_bias=augment_bias, max_conv_rows=max_conv_rows,
@@ -147,6 +151,36 @@ class IFKFAC(torch.optim.Optimizer):
                             ws.data_ptr(), ws.numel(), _stream()), "ifk_natgrad")
         return nat
 
+    def _natgrad_many(self, items, biases=None):
+        """Natural gradients of several layers with one ifk_natgrad_batched call:
+        items are (g, R_X, R_G) with factors of one dtype on one device; biases
+        (optional, an entry per layer, None where a layer has no bias gradient)
+        come back solved by R_G^-1 R_G^-T as the second list."""
+        import ctypes
+        L = _lib.lib()
+        arr = lambda t, v: (t * len(v))(*v)
+        gs = [g.float().contiguous() for g, _, _ in items]
+        rx = [R_X.contiguous() for _, R_X, _ in items]
+        rg = [R_G.contiguous() for _, _, R_G in items]
+        nats = [torch.empty_like(g) for g in gs]
+        bs = [b.float().contiguous() if b is not None else None for b in (biases or [None] * len(gs))]
+        nbs = [torch.empty_like(b) if b is not None else None for b in bs]
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        n_out = [g.shape[0] for g in gs]
+        n_in = [g.shape[1] for g in gs]
+        dev = gs[0].device
+        ws = self._workspace(("natb", dev), L.ifk_natgrad_batched_workspace(
+            len(gs), arr(ctypes.c_int64, n_out), arr(ctypes.c_int64, n_in)), dev)
+        check(L.ifk_natgrad_batched(
+            len(gs), arr(ctypes.c_void_p, [g.data_ptr() for g in gs]), arr(ctypes.c_int64, n_in),
+            arr(ctypes.c_void_p, [r.data_ptr() for r in rx]), arr(ctypes.c_int64, n_in),
+            arr(ctypes.c_void_p, [r.data_ptr() for r in rg]), arr(ctypes.c_int64, n_out), _DT[rx[0].dtype],
+            arr(ctypes.c_void_p, [o.data_ptr() for o in nats]), arr(ctypes.c_int64, n_in),
+            arr(ctypes.c_int64, n_out), arr(ctypes.c_int64, n_in), arr(ctypes.c_void_p, [ptr(b) for b in bs]),
+            arr(ctypes.c_void_p, [ptr(b) for b in nbs]), self.precision, None, ws.data_ptr(),
+            ws.numel(), _stream()), "ifk_natgrad_batched")
+        return nats, nbs
+
     def _natgrad_bias(self, gb: torch.Tensor, R_G: torch.Tensor) -> torch.Tensor:
         L = _lib.lib()
         R_G = R_G.contiguous()
@@ -195,7 +229,46 @@ class IFKFAC(torch.optim.Optimizer):
                            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
                            _stream()), "ifk_update")
 
-    def _apply_preconditioner(self, module, lr, weight_decay, momentum) -> None:
+    def _layer_factors(self, module):
+        """(g2, R_X, R_G) of a layer that has square factors, else None."""
+        if module not in self._factors or module.weight.grad is None:
+            return None
+        R_X, R_G = self._factors[module]
+        if self.augment_bias and module.bias is not None:
+            R_X = R_X[:-1, :-1].contiguous()
+        if R_X.shape[0] != R_X.shape[1] or R_G.shape[0] != R_G.shape[1] or R_X.dtype != R_G.dtype:
+            return None
+        grad_w = module.weight.grad
+        g2 = grad_w.reshape(grad_w.shape[0], -1) if grad_w.dim() > 2 else grad_w
+        return g2, R_X, R_G
+
+    def _batched_natgrads(self, modules) -> dict:
+        """Natural gradients of every layer with square factors, the layers of one
+        factor dtype and device in one batched call (the bucketed apply of
+        ifkfac/ifkfac.py:315-423); a failed batch leaves its layers to the
+        per-layer path."""
+        groups = {}
+        for m in modules:
+            it = self._layer_factors(m)
+            if it is not None:
+                groups.setdefault((it[1].dtype, it[1].device), []).append((m, it))
+        out = {}
+        for lst in groups.values():
+            if len(lst) < 2:
+                continue
+            biases = [m.bias.grad if m.bias is not None and m.bias.grad is not None else None for m, _ in lst]
+            try:
+                nats, nbs = self._natgrad_many([it for _, it in lst], biases)
+            except IFKError as e:
+                logger.warning("IFKFAC: batched apply_vered failed (%s) — layers go one by one.", e)
+                continue
+            for (m, _), nat, nb in zip(lst, nats, nbs):
+                out[m] = (nat, nb)
+        return out
+
+    def _apply_preconditioner(self, module, lr, weight_decay, momentum, pre=None) -> None:
+        """pre: (natural gradient of the weight, of the bias or None) from the batched apply."""
+        nat_pre, nb_pre = pre if pre is not None else (None, None)
         weight = module.weight
         if weight.grad is None:
             return
@@ -210,7 +283,9 @@ class IFKFAC(torch.optim.Optimizer):
         grad_w = weight.grad
         g2 = grad_w.reshape(grad_w.shape[0], -1) if grad_w.dim() > 2 else grad_w
         try:
-            if R_X.shape[0] != R_X.shape[1] or R_G.shape[0] != R_G.shape[1]:
+            if nat_pre is not None:
+                nat = nat_pre
+            elif R_X.shape[0] != R_X.shape[1] or R_G.shape[0] != R_G.shape[1]:
                 nat = g2.float()
             else:
                 nat = self._natgrad(g2, R_X, R_G)
@@ -222,7 +297,7 @@ class IFKFAC(torch.optim.Optimizer):
                            buf_owner=module, clip=self.grad_clip)
         if module.bias is not None and module.bias.grad is not None:
             try:
-                nb = self._natgrad_bias(module.bias.grad, R_G)
+                nb = nb_pre if nb_pre is not None else self._natgrad_bias(module.bias.grad, R_G)
             except IFKError as e:
                 logger.warning("IFKFAC: bias solve failed (%s) — using raw gradient.", e)
                 nb = module.bias.grad.float()
@@ -240,13 +315,17 @@ class IFKFAC(torch.optim.Optimizer):
         if should_refresh(self._step_count, self.factor_update_freq):
             self._update_factors()
         t_pre = time.perf_counter()
+        todo = []
         for module in self.hooks.linear_layers:
             if module.weight.grad is None:
                 continue
             lr, wd, mom = self._get_module_hp(module)
             if lr is None:
                 continue
-            self._apply_preconditioner(module, lr, wd, mom)
+            todo.append((module, lr, wd, mom))
+        nats = self._batched_natgrads([m for m, _, _, _ in todo])
+        for module, lr, wd, mom in todo:
+            self._apply_preconditioner(module, lr, wd, mom, nats.get(module))
         self.timing["precondition"].append(time.perf_counter() - t_pre)
         self.timing["total_step"].append(time.perf_counter() - t_total)
         return loss

@@ -268,6 +268,36 @@ IFK_API int ifk_natgrad_noalloc(const float* grad_W, int64_t ld_g,
                         int64_t n_out, int64_t n_in, int prec, int* d_status,
                         ifk_stream_t stream);
 
+/* Workspace bytes for ifk_natgrad_batched: per layer, ifk_natgrad_workspace and
+ * the scratch of its bias solve. */
+IFK_API size_t ifk_natgrad_batched_workspace(int nlayers, const int64_t* n_out, const int64_t* n_in);
+
+/*
+ * ifk_natgrad for nlayers layers at once (host arrays of length nlayers).
+ * Layers on the persistent bf16 path (bf16 factors, IFK_PREC_BF16, orders
+ * that 16-byte copies address) share their launches: one launch of the
+ * diagonal-block inverses of every factor, then for each of the four solves
+ * one launch that packs the operand tiles of every layer and one that solves
+ * every layer, the CTAs dealt across the layers' column groups.  Other layers
+ * run one by one.  Each layer's result is the one ifk_natgrad gives.
+ * grad_b / nat_b (both NULL, or arrays with an entry per layer, NULL for a layer
+ * without bias): nat_b = R_G^-1 R_G^-T grad_b (n_out fp32, may alias), the
+ * layer's bias as one more right-hand side of its left solves (the persistent
+ * path) or ifk_natgrad_bias (the other layers).
+ *
+ * Replaces apply_vered_batched / _apply_vered_batched_impl and the graphed
+ * bucketed apply of the reference (ifkfac/triangular.py:430-544,
+ * ifkfac/ifkfac.py:315-423), with apply_vered_bias
+ * (ifkfac/triangular.py:659-705) for the biases.
+ */
+IFK_API int ifk_natgrad_batched(int nlayers, const float* const* grad_W, const int64_t* ld_g,
+                                const void* const* R_X, const int64_t* ld_rx, const void* const* R_G,
+                                const int64_t* ld_rg, int r_dtype, float* const* nat,
+                                const int64_t* ld_nat, const int64_t* n_out, const int64_t* n_in,
+                                const float* const* grad_b, float* const* nat_b, int prec,
+                                int* d_status, void* workspace, size_t workspace_bytes,
+                                ifk_stream_t stream);
+
 /*
  * nat_b = R_G^-1 R_G^-T grad_b (vectors of n_out fp32; may alias).
  * Replaces apply_vered_bias (ifkfac/triangular.py:659-705).
