@@ -210,20 +210,54 @@ def gen_hooks(ifk):
     np.savez_compressed(os.path.join(HERE, "hooks_seq_bias.npz"), **init, **out)
 
 
+def gen_ema(ifk):
+    """EMA blend (ifkfac/ifkfac.py:261-285): freq 2, gamma 0.4, so the refresh of
+    step 4 blends with the factors of step 2.  A second run with gamma 0 from the
+    same start gives the unblended step-4 factors (steps 1-3 do not depend on gamma)."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(64, 20, generator=g)
+    y = torch.randint(0, 5, (64,), generator=g)
+    torch.manual_seed(4)
+    init_model = nn.Sequential(nn.Linear(20, 24), nn.ReLU(), nn.Linear(24, 5))
+    init = {f"init_{k}": v.detach().numpy().copy() for k, v in init_model.state_dict().items()}
+    out = {"x": x.numpy(), "y": y.numpy(), **init}
+    for gamma, tag in ((0.4, "ema"), (0.0, "plain")):
+        model = nn.Sequential(nn.Linear(20, 24), nn.ReLU(), nn.Linear(24, 5))
+        model.load_state_dict(init_model.state_dict())
+        opt = ifk.IFKFAC(model, lr=5e-2, damping=1e-2, factor_update_freq=2, momentum=0.9, gamma=gamma)
+        with contextlib.redirect_stdout(io.StringIO()):
+            for s in range(1, 5):
+                loss = F.cross_entropy(model(x), y)
+                opt.zero_grad()
+                loss.backward()
+                opt.step()
+                if s in (2, 4):
+                    for i, m in enumerate(opt.hooks.linear_layers):
+                        out[f"{tag}_s{s}_RX{i}"] = _np(opt._factors[m][0])
+                        out[f"{tag}_s{s}_RG{i}"] = _np(opt._factors[m][1])
+        for i, m in enumerate(opt.hooks.linear_layers):
+            out[f"{tag}_W{i}"] = _np(m.weight)
+        opt.cleanup()
+    np.savez_compressed(os.path.join(HERE, "ema_blend.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference source tree")
+    ap.add_argument("--only", default=None, help="write one file: streaming, apply, batched, bf16, steps, hooks, ema")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import ifkfac as ifk
     from ifkfac import triangular as T, bf16_linalg as B
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    gen_streaming(T)
-    gen_apply(T)
-    gen_batched_and_tree(T)
-    gen_bf16(B)
-    gen_steps(ifk)
-    gen_hooks(ifk)
+    gens = {"streaming": lambda: gen_streaming(T), "apply": lambda: gen_apply(T),
+            "batched": lambda: gen_batched_and_tree(T), "bf16": lambda: gen_bf16(B),
+            "steps": lambda: gen_steps(ifk), "hooks": lambda: gen_hooks(ifk), "ema": lambda: gen_ema(ifk)}
+    for name, gen in gens.items():
+        if args.only in (None, name):
+            gen()
     print("golden vectors written to", HERE)
 
 

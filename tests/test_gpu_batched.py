@@ -158,3 +158,23 @@ def test_batched_bias_solves():
     # the weights are unchanged by the bias problems sharing their launches
     for g, RX, RG, nat in zip(gs, RXs, RGs, nats):
         assert torch.equal(nat, _single(g, RX, RG, _lib.PREC_BF16))
+
+
+@pytest.mark.parametrize("prec,tol", [(_lib.PREC_FP32, 1e-5), (_lib.PREC_BF16, 2e-2)])
+def test_ema_blend_matches_oracle(prec, tol):
+    """IFKFAC(gamma > 0) blends refreshed factors by the exact stacked QR of the
+    reference (ifkfac/ifkfac.py:261-285): fold sqrt(1-g) R_new into sqrt(g) R_old."""
+    import numpy as np
+    from oracle import ifk_oracle as ora
+    from ifkfac_b200.ifkfac import IFKFAC
+    model = torch.nn.Sequential(torch.nn.Linear(8, 8)).cuda()
+    opt = IFKFAC(model, gamma=0.3, precision=prec)
+    for n in (96, 200):
+        R_old = _factor(n, 1 + n, torch.float32)
+        R_new = _factor(n, 2 + n, torch.float32)
+        out = opt._blend(R_old, R_new).double().cpu().numpy()
+        truth = ora.ema_blend(R_old.double().cpu().numpy(), R_new.double().cpu().numpy(), 0.3)
+        assert np.linalg.norm(out - truth) / np.linalg.norm(truth) < tol
+        G = 0.3 * R_old.double().T @ R_old.double() + 0.7 * R_new.double().T @ R_new.double()
+        assert float(np.linalg.norm(out.T @ out - G.cpu().numpy()) / np.linalg.norm(G.cpu().numpy())) < 2 * tol
+    opt.cleanup()

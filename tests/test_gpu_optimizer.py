@@ -120,3 +120,28 @@ def test_bf16_autocast_capture_runs_on_tensor_cores():
     opt.step()
     assert all(v[0].dtype == torch.bfloat16 for v in opt._factors.values())
     opt.cleanup()
+
+
+def test_ema_blend_trajectory_matches_reference():
+    """gamma = 0.4, refresh every 2 steps: the step-4 factors are the exact blend of the
+    reference (ifkfac/ifkfac.py:261-285) and the weights follow its trajectory."""
+    from ifkfac_b200 import IFKFAC
+    g = load("ema_blend")
+    model = _load_model(nn.Sequential(nn.Linear(20, 24), nn.ReLU(), nn.Linear(24, 5)), g)
+    x = torch.from_numpy(g["x"]).cuda()
+    y = torch.from_numpy(g["y"]).cuda()
+    opt = IFKFAC(model, lr=5e-2, damping=1e-2, factor_update_freq=2, momentum=0.9, gamma=0.4)
+    for s in range(1, 5):
+        loss = F.cross_entropy(model(x), y)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        if s in (2, 4):
+            for i, m in enumerate(opt.hooks.linear_layers):
+                for j, f in enumerate(("RX", "RG")):
+                    e = rel(opt._factors[m][j].cpu().numpy(), g[f"ema_s{s}_{f}{i}"])
+                    assert e < 1e-4, (s, i, f, e)
+    for i, m in enumerate(opt.hooks.linear_layers):
+        e = rel(m.weight.detach().cpu().numpy(), g[f"ema_W{i}"])
+        assert e < 1e-4, (i, e)
+    opt.cleanup()

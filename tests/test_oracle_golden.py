@@ -131,3 +131,17 @@ def test_precond_update_rules():
     assert np.allclose(W2, W1 * (1 - 0.05) - 0.1 * b2, atol=1e-6)
     W3, _ = O.precond_update(W, None, g * 100, lr=1.0, momentum=0.0, weight_decay=0.0, grad_clip=1.0)
     assert abs(np.linalg.norm(W - W3) - 1.0) < 1e-5
+
+
+def test_ema_blend_restatement_matches_reference():
+    """oracle.ema_blend reproduces the reference's blended factors: the step-4 refresh
+    of a gamma = 0.4 run blends the step-2 factors with the step-4 ones (those of the
+    gamma = 0 run, identical up to step 3)."""
+    z = load("ema_blend")
+    for i in range(2):
+        for f in ("RX", "RG"):
+            old, new = z[f"ema_s2_{f}{i}"].astype(np.float64), z[f"plain_s4_{f}{i}"].astype(np.float64)
+            assert np.array_equal(z[f"ema_s2_{f}{i}"], z[f"plain_s2_{f}{i}"])
+            got = O.ema_blend(old, new, 0.4)
+            ref = z[f"ema_s4_{f}{i}"].astype(np.float64)
+            assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-5
