@@ -41,6 +41,7 @@ SIGNATURES = {
     "ifk_finalize_batched_workspace": (_sz, [_int, _vp]),
     "ifk_finalize_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp,
                                     _vp, _sz, _vp]),
+    "ifk_finalize_many": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp, _vp, _sz, _vp]),
     "ifk_finalize": (_int, [_vp, _i64, _i64, _i64, _dbl, _dbl, _vp, _i64, _int, _int, _vp, _vp, _sz,
                             _vp]),
     "ifk_natgrad_workspace": (_sz, [_i64, _i64]),

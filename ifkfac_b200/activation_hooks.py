@@ -293,6 +293,7 @@ class RawActivationHooks:
         L = _lib.lib()
         self.last_status = None
         self.status_index = {}
+        ready = []
         for module in self._linear_layers:
             fx, fg = self._fx[module], self._fg[module]
             if fx is None or fg is None or fx.rows_seen == 0 or fg.rows_seen == 0:
@@ -307,26 +308,46 @@ class RawActivationHooks:
                 if rows_G < fg.n:
                     raise IFKFACRankError(f"Layer {module}: accumulated {rows_G} rows for δ, "
                                           f"but need >= n_out={fg.n} (batched mode).")
-            dev = fx.R.device
-            if self.last_status is None:
-                # one device status word per layer: the fused finite check of the damping fold
-                self.last_status = torch.zeros(len(self._linear_layers), dtype=torch.int32, device=dev)
-            self.status_index[module] = len(self.status_index)
-            outs = [torch.empty(f.n, f.n, dtype=out_dtype, device=dev) for f in (fx, fg)]
-            import ctypes
-            arr = lambda t, v: (t * len(v))(*v)
-            ns = [fx.n, fg.n]
-            ws = self._workspace(("fin", dev), L.ifk_finalize_batched_workspace(2, arr(ctypes.c_int64, ns)), dev)
-            st = status if status is not None else self.last_status[self.status_index[module]:]
+            ready.append((module, fx, fg, rows_X, rows_G))
+        if not ready:
+            return factors
+        import ctypes
+        arr = lambda t, v: (t * len(v))(*v)
+        dev = ready[0][1].R.device
+        # one device status word per layer: the fused finite check of the damping fold
+        self.last_status = torch.zeros(len(self._linear_layers), dtype=torch.int32, device=dev)
+        # the layers of one precision finalize together (ifk_finalize_batched: the
+        # damping folds of up to 16 factors share a launch)
+        groups = {}
+        for module, fx, fg, rows_X, rows_G in ready:
             prec = _lib.PREC_BF16 if (out_dtype == torch.bfloat16 or fx.prec == _lib.PREC_BF16) else self.precision
-            _lib.check(L.ifk_finalize_batched(
-                2, arr(ctypes.c_void_p, [fx.R.data_ptr(), fg.R.data_ptr()]), arr(ctypes.c_int64, ns),
-                arr(ctypes.c_int64, [fx.rows_R, fg.rows_R]), arr(ctypes.c_int64, ns),
-                arr(ctypes.c_double, [float(rows_X), float(rows_G)]), float(self.damping),
+            groups.setdefault((prec, fx.R.device), []).append((module, fx, fg, rows_X, rows_G))
+        for (prec, dev), lst in groups.items():
+            fs, outs, rows, sts = [], [], [], []
+            for module, fx, fg, rows_X, rows_G in lst:
+                self.status_index[module] = len(self.status_index)
+                pair = [torch.empty(f.n, f.n, dtype=out_dtype, device=dev) for f in (fx, fg)]
+                factors[module] = (pair[0], pair[1])
+                fs += [fx, fg]
+                outs += pair
+                rows += [float(rows_X), float(rows_G)]
+            ns = [f.n for f in fs]
+            ws = self._workspace(("fin", dev), L.ifk_finalize_batched_workspace(len(fs), arr(ctypes.c_int64, ns)),
+                                 dev)
+            # one status word per layer (both of its factors write it): the caller's word
+            # when given, else the layer's entry of last_status
+            base = self.last_status.data_ptr()
+            sts = []
+            for module, *_ in lst:
+                p = status.data_ptr() if status is not None else base + 4 * self.status_index[module]
+                sts += [p, p]
+            _lib.check(L.ifk_finalize_many(
+                len(fs), arr(ctypes.c_void_p, [f.R.data_ptr() for f in fs]), arr(ctypes.c_int64, ns),
+                arr(ctypes.c_int64, [f.rows_R for f in fs]), arr(ctypes.c_int64, ns),
+                arr(ctypes.c_double, rows), float(self.damping),
                 arr(ctypes.c_void_p, [o.data_ptr() for o in outs]), arr(ctypes.c_int64, ns),
-                _lib.BF16 if out_dtype == torch.bfloat16 else _lib.F32, prec, st.data_ptr(),
-                ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream), "ifk_finalize_batched")
-            factors[module] = (outs[0], outs[1])
+                _lib.BF16 if out_dtype == torch.bfloat16 else _lib.F32, prec, arr(ctypes.c_void_p, sts),
+                ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream), "ifk_finalize_many")
         return factors
 
     def clear(self) -> None:

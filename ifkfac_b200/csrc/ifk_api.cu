@@ -451,11 +451,12 @@ size_t ifk_finalize_batched_workspace(int nfactors, const int64_t* n) {
   return b;
 }
 
-int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
-                         const int64_t* rows_R, const int64_t* n, const double* rows_total,
-                         double damping, void* const* R_out, const int64_t* ld_out, int out_dtype,
-                         int prec, int* d_status, void* workspace, size_t workspace_bytes,
-                         ifk_stream_t stream) {
+}  // extern "C"
+
+static int finalize_many(int nfactors, const float* const* R_in, const int64_t* ldR, const int64_t* rows_R,
+                         const int64_t* n, const double* rows_total, double damping, void* const* R_out,
+                         const int64_t* ld_out, int out_dtype, int prec, int* d_status, int* const* f_status,
+                         void* workspace, size_t workspace_bytes, ifk_stream_t stream) {
   if (nfactors < 0 ||
       (nfactors > 0 && (!R_in || !ldR || !rows_R || !n || !rows_total || !R_out || !ld_out)))
     return IFK_ERR_ARG;
@@ -492,7 +493,8 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
           pd[q] = pfold_desc(Rf[q], xw_ld(n[f]), n[f], n[f]);
           pfold_add(pd[q], nullptr, 0, n[f], 2, (float)std::sqrt(damping), 1);
         }
-        rc = run_persistent(cnt, pd, ws, d_status, s);
+        // a timed-out wait of the shared launch is reported to the group's first factor
+        rc = run_persistent(cnt, pd, ws, d_status ? d_status : (f_status ? f_status[base] : nullptr), s);
       } else {
         FoldBatch b;
         b.nf = 0;
@@ -512,7 +514,7 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
           a.tiles = (int)cdiv(n[f], SUB);
           a.K = (int)cdiv(n[f], NB);
           a.tri = 1;
-          a.err = d_status;
+          a.err = f_status ? f_status[f] : d_status;
           rc = fill_scaled_identity(a.X, a.ldX, n[f], (float)std::sqrt(damping), s);
           if (rc != IFK_OK) return rc;
         }
@@ -522,11 +524,31 @@ int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* 
     }
     for (int q = 0; q < cnt; ++q) {
       const int f = base + q;
-      const int rc = finish_factor(R_out[f], ld_out[f], out_dtype, Rf[q], xw_ld(n[f]), n[f], d_status, s);
+      int* st = f_status ? f_status[f] : d_status;
+      const int rc = finish_factor(R_out[f], ld_out[f], out_dtype, Rf[q], xw_ld(n[f]), n[f], st, s);
       if (rc != IFK_OK) return rc;
     }
   }
   return IFK_OK;
+}
+
+extern "C" {
+
+int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
+                         const int64_t* rows_R, const int64_t* n, const double* rows_total,
+                         double damping, void* const* R_out, const int64_t* ld_out, int out_dtype,
+                         int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                         ifk_stream_t stream) {
+  return finalize_many(nfactors, R_in, ldR, rows_R, n, rows_total, damping, R_out, ld_out, out_dtype, prec, d_status,
+                       nullptr, workspace, workspace_bytes, stream);
+}
+
+int ifk_finalize_many(int nfactors, const float* const* R_in, const int64_t* ldR, const int64_t* rows_R,
+                      const int64_t* n, const double* rows_total, double damping, void* const* R_out,
+                      const int64_t* ld_out, int out_dtype, int prec, int* const* d_status, void* workspace,
+                      size_t workspace_bytes, ifk_stream_t stream) {
+  return finalize_many(nfactors, R_in, ldR, rows_R, n, rows_total, damping, R_out, ld_out, out_dtype, prec,
+                       nullptr, d_status, workspace, workspace_bytes, stream);
 }
 
 // Workspace of the persistent bf16 solves: inverses of R_G | inverses of R_X |

@@ -25,7 +25,7 @@ struct FoldArgs {
 };
 
 // Up to MAX_FOLDS independent folds share one wave schedule (blockIdx.z selects the fold).
-constexpr int MAX_FOLDS = 8;
+constexpr int MAX_FOLDS = 16;
 struct FoldBatch {
   FoldArgs f[MAX_FOLDS];
   int nf;

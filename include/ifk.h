@@ -212,14 +212,29 @@ IFK_API size_t ifk_finalize_batched_workspace(int nfactors, const int64_t* n);
 
 /*
  * ifk_finalize on nfactors factors in one wave schedule (host arrays of
- * length nfactors; every factor must be square).  Used to refresh R_X and
- * R_G of a layer together.
+ * length nfactors; every factor must be square; the damping folds of up to 16
+ * factors share a launch).  Used to refresh R_X and R_G of a layer together.
  */
 IFK_API int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
                          const int64_t* rows_R, const int64_t* n, const double* rows_total,
                          double damping, void* const* R_out, const int64_t* ld_out,
                          int out_dtype, int prec, int* d_status, void* workspace,
                          size_t workspace_bytes, ifk_stream_t stream);
+
+/*
+ * ifk_finalize_batched with a status word per factor: d_status is a host array
+ * of nfactors device pointers (entries may be NULL), and factor f's finite
+ * check writes to d_status[f] only, so a caller that refreshes many layers at
+ * once can still skip just the layers whose factors are not finite, as the
+ * reference does per layer (ifkfac/ifkfac.py:231-237).  A timed-out wait of a
+ * shared launch is reported to the word of the first factor of its group of
+ * 16.  Same workspace as ifk_finalize_batched.
+ */
+IFK_API int ifk_finalize_many(int nfactors, const float* const* R_in, const int64_t* ldR,
+                              const int64_t* rows_R, const int64_t* n, const double* rows_total,
+                              double damping, void* const* R_out, const int64_t* ld_out,
+                              int out_dtype, int prec, int* const* d_status, void* workspace,
+                              size_t workspace_bytes, ifk_stream_t stream);
 
 /* ---- natural gradient ---------------------------------------------------- */
 

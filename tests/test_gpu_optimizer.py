@@ -145,3 +145,32 @@ def test_ema_blend_trajectory_matches_reference():
         e = rel(m.weight.detach().cpu().numpy(), g[f"ema_W{i}"])
         assert e < 1e-4, (i, e)
     opt.cleanup()
+
+
+def test_nonfinite_factor_skips_only_its_layer():
+    """A refresh finalizes every layer in shared launches; a layer whose factor is not
+    finite is skipped on its own (ifkfac/ifkfac.py:231-237) while the others get
+    their factors, and the skipped layer takes the plain gradient step."""
+    from ifkfac_b200 import IFKFAC
+    torch.manual_seed(5)
+    model = nn.Sequential(nn.Linear(16, 32), nn.ReLU(), nn.Linear(32, 32), nn.ReLU(), nn.Linear(32, 4)).cuda()
+    x = torch.randn(128, 16, device="cuda")
+    y = torch.randint(0, 4, (128,), device="cuda")
+    opt = IFKFAC(model, lr=1e-2, damping=1e-2, factor_update_freq=1, momentum=0.0)
+    layers = opt.hooks.linear_layers
+    loss = F.cross_entropy(model(x), y)
+    opt.zero_grad()
+    loss.backward()
+    opt.hooks._fx[layers[1]].R[0, 0] = float("nan")  # the running factor of layer 1 goes bad
+    w1 = layers[1].weight.detach().clone()
+    g1 = layers[1].weight.grad.detach().clone()
+    opt.step()
+    torch.cuda.synchronize()
+    assert layers[0] in opt._factors and layers[2] in opt._factors
+    assert layers[1] not in opt._factors
+    for m in (layers[0], layers[2]):
+        for R in opt._factors[m]:
+            assert torch.isfinite(R).all()
+    # no preconditioner for layer 1: plain SGD on its weight (ifkfac/ifkfac.py:443-448)
+    assert torch.allclose(layers[1].weight.detach(), w1 - 1e-2 * g1, rtol=0, atol=1e-7)
+    opt.cleanup()
