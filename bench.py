@@ -557,6 +557,91 @@ def run_c3(args, rank, world, local_rank):
     print(json.dumps(out), flush=True)
 
 
+def run_c4(args, rank, world, local_rank):
+    """a GPT-2-small-shaped decoder (12 blocks, d 768, 12 heads, MLP 3072,
+    seq 1024, batch 8: p = 8192 tokens; vocab 50257, uniform random token ids), random init,
+    bf16 autocast, K-FAC on every Linear of the blocks (qkv 768->2304, proj, fc 768->3072,
+    fc2 3072->768; the 50257-wide head excluded by max_out_dim = 4096), use_true_bf16,
+    damping 1e-3, every token's rows (max_seq_rows = 0), batched_qr, momentum 0.9,
+    factor_update_freq 10.  A step is forward + backward + IFKFAC.step."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from ifkfac_b200.ifkfac import IFKFAC
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    d, heads, seq, batch, vocab = 768, 12, 1024, 8, 50257
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln1, self.ln2 = nn.LayerNorm(d), nn.LayerNorm(d)
+            self.qkv, self.proj = nn.Linear(d, 3 * d), nn.Linear(d, d)
+            self.fc, self.fc2 = nn.Linear(d, 4 * d), nn.Linear(4 * d, d)
+
+        def forward(self, x):
+            B, T, _ = x.shape
+            q, k, v = self.qkv(self.ln1(x)).split(d, dim=2)
+            q, k, v = (t.view(B, T, heads, d // heads).transpose(1, 2) for t in (q, k, v))
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            x = x + self.proj(a.transpose(1, 2).reshape(B, T, d))
+            return x + self.fc2(F.gelu(self.fc(self.ln2(x))))
+
+    class GPT(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.tok, self.pos = nn.Embedding(vocab, d), nn.Embedding(seq, d)
+            self.blocks = nn.ModuleList([Block() for _ in range(12)])
+            self.ln, self.head = nn.LayerNorm(d), nn.Linear(d, vocab, bias=False)
+
+        def forward(self, idx):
+            x = self.tok(idx) + self.pos(torch.arange(idx.shape[1], device=idx.device))
+            for b in self.blocks:
+                x = b(x)
+            return self.head(self.ln(x))
+
+    torch.manual_seed(0)
+    model = GPT().to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    idx = torch.randint(0, vocab, (batch, seq + 1), generator=g, device=dev)
+    x, y = idx[:, :-1], idx[:, 1:]
+    opt = IFKFAC(model, lr=1e-3, damping=1e-3, factor_update_freq=10, momentum=0.9, use_true_bf16=True,
+                 max_out_dim=4096, max_seq_rows=0, batched_qr=True)
+
+    def one():
+        opt.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = model(x)
+        loss = F.cross_entropy(logits.float().reshape(-1, vocab), y.reshape(-1))
+        loss.backward()
+        opt.step()
+        return loss
+
+    steps = max(10, (args.steps + 9) // 10 * 10)
+    for _ in range(max(args.warmup, 10)):
+        one()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            loss = one()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
+           "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 10),
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic",
+           "config": {"workload": "C4 GPT-2-small-shaped decoder, 12 x (qkv, proj, fc, fc2) under K-FAC, "
+                                  "8 x 1024 tokens, bf16 autocast, use_true_bf16, damping 1e-3, batched_qr",
+                      "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
+                      "timing": "eager, CUDA events around the step loop (host work included)"},
+           "clocks": clk.summary()}
+    opt.cleanup()
+    print(json.dumps(out), flush=True)
+
+
 def cpu_baseline(scale=1.0):
     """The oracle port (scipy LAPACK fp32, the reference's algorithm) on host cores,
     timed on a bounded sample and extrapolated to one operator."""
@@ -625,8 +710,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["c2", "c3"], default="c2",
-                    help="c2: the single-layer operator (the headline); c3: the 8-layer MLP training step")
+    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c2",
+                    help="c2: the single-layer operator (the headline); c3: the 8-layer MLP training step; "
+                         "c4: the GPT-2-small-shaped decoder training step")
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
@@ -652,9 +738,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
         return
-    if args.config == "c3":
+    if args.config in ("c3", "c4"):
         if rank == 0:
-            run_c3(args, rank, world, local_rank)
+            (run_c3 if args.config == "c3" else run_c4)(args, rank, world, local_rank)
         return
     if world > 1:
         import datetime

@@ -563,7 +563,15 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   const int h = (int)mn<int64_t>(SUB, G.rows - row0);
   const int64_t cs = (int64_t)cb * WB;
   const int wc = (int)mn<int64_t>(WB, F.n - cs);
-  // rank bound: the rows folded so far, this sub-tile's included
+  // Rank bound: the rows folded so far, this sub-tile's included.  Past it the
+  // sub-tile holds rounding residuals only, as long as every reflector consumed a
+  // row of it.  A dependent column (duplicated, constant or all-zero activations)
+  // has a zero or rounding-noise pivot, spends its reflector on that and leaves one
+  // row direction of the sub-tile past the bound, which is dropped.  Once R is
+  // square the loss is a few times this fold's bf16 rounding (measured, relative
+  // in R^T R: 1.6e-3 with 5 of 3072 columns dependent, 3.7e-3 with 150, 5.9e-3
+  // with 150 of 768; 1.1e-3 with every column factored).  The fp32 wave fold
+  // factors every column and stays exact.
   const int64_t lim = mn<int64_t>(F.n, F.rows_R + G.row_off + row0 + h);
   const int kfirst = G.tri ? (int)(row0 / NB) : 0;
   int* prog = F.prog + (size_t)t * F.CB + cb;

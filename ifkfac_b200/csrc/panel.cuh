@@ -111,6 +111,14 @@ __device__ __forceinline__ void psync() {
 // beta; 1/xn2 is taken alongside the square root:
 //   aj > 0:  v0 = -xn2 / u, 1/v0 = -u / xn2, tj = -v0 / beta = xn2 / (u beta)
 //   aj <= 0: 1/v0 = 1/u, tj = -u / beta.
+// A residual with |x| below the fp32 resolution of the diagonal (|x| < 2^-24 |aj|:
+// beta rounds to |aj|) or |x|^2 below XN2_MIN is dropped, and the reflector reduces
+// to the sign flip.  Leaving x in place perturbs column j by at most 2^-24 |aj| (or
+// 1e-15), inside Householder's backward error; without the cut, an exactly dependent
+// column (duplicate or constant activations: its residual cancels to a denormal)
+// makes 1/xn2 and (1/beta)^2 leave the fp32 range and the panel turns NaN.  A NaN
+// xn2 fails both tests and still propagates to the finite check.
+constexpr float XN2_MIN = 1e-30f;
 __device__ __forceinline__ void reflector(float aj, float xn2, float& tj, float& beta, float& inv_v0) {
   const float s = fmaf(aj, aj, xn2);
   const float rs = rsqrtf(s);
@@ -119,8 +127,9 @@ __device__ __forceinline__ void reflector(float aj, float xn2, float& tj, float&
   const bool pos = aj > 0.f;
   const float u = pos ? aj + nrm : aj - nrm;
   const float ru = __fdividef(1.f, u);
-  if (xn2 == 0.f) {
-    // nothing to annihilate; flip the row if its diagonal is negative
+  const float ea = aj * 0x1p-24f;
+  if (xn2 < XN2_MIN || xn2 < ea * ea) {
+    // nothing to annihilate at fp32 resolution; flip the row if its diagonal is negative
     tj = aj >= 0.f ? 0.f : 2.f;
     beta = fabsf(aj);
     inv_v0 = 0.f;

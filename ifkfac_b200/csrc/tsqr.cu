@@ -29,15 +29,17 @@ constexpr int PT = 256;  // threads of the panel and SIMT update kernels
 static_assert(SUB == PT, "panel kernel maps one thread to one row");
 constexpr int LDP = NB + 1;
 
-__device__ __forceinline__ bool task_active(const FoldArgs& a, int t, int k, int64_t* lim_out) {
+// Task (t, k) of the wave schedule.  Every sub-tile factors every panel (no
+// rank bound): while R is trapezoidal, a sub-tile past the rows folded so far
+// holds only rounding residuals in exact arithmetic, but an exactly or
+// numerically dependent column (duplicated or constant activations) spends a
+// reflector on rounding noise and leaves a true row direction there, which a
+// bound at rows_R + rows would drop.  This is the fp32 path, so it keeps them.
+// (The persistent bf16 fold keeps the bound; its own rounding is coarser than
+// that loss.)  Only the zero block of a trapezoidal chunk is skipped.
+__device__ __forceinline__ bool task_active(const FoldArgs& a, int t, int k) {
   if (t < 0 || t >= a.tiles || k < 0 || k >= a.K) return false;
-  const int64_t row0 = (int64_t)t * SUB;
-  const int64_t h = mn<int64_t>(SUB, a.rows - row0);
-  if (a.tri && (int64_t)k * NB + NB <= row0) return false;  // sub-tile is zero left of its diagonal
-  const int64_t lim = mn<int64_t>(a.n, a.rows_R + row0 + h);       // rank bound: columns that can be reduced
-  if ((int64_t)k * NB >= lim) return false;
-  *lim_out = lim;
-  return true;
+  return !(a.tri && (int64_t)k * NB + NB <= (int64_t)t * SUB);  // sub-tile is zero left of its diagonal
 }
 
 // ---- panel factorisation: see panel.cuh -----------------------------------------
@@ -50,8 +52,7 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
   const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
-  int64_t lim;
-  if (!task_active(a, t, k, &lim)) return;
+  if (!task_active(a, t, k)) return;
 
   extern __shared__ __align__(1024) float smraw[];
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(smraw);
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
   const int h = (int)mn<int64_t>(SUB, a.rows - row0);
   const int64_t c0 = (int64_t)k * NB;
   const int nbk = (int)mn<int64_t>(NB, a.n - c0);
-  const int nact = (int)mx<int64_t>(0, mn<int64_t>(nbk, lim - c0));
+  const int nact = nbk;
 
   // X_t panel -> P: 16-byte loads, 8 in flight per thread
   for (int q0 = tid; q0 < SUB * NB / 4; q0 += 8 * PT2) {
@@ -125,8 +126,7 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
   const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
-  int64_t lim;
-  if (!task_active(a, t, k, &lim)) return;
+  if (!task_active(a, t, k)) return;
   const int64_t c0 = (int64_t)k * NB;
   const int64_t cs = (int64_t)blockIdx.y * WC;
   if (cs < c0 + NB || cs >= a.n) return;

@@ -47,13 +47,10 @@ constexpr uint32_t B2_MN = 128, B2_K = (NB / 8) * 128;   // 128, 1024
 
 constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
 
+// Task (t, k) of the wave schedule (every panel is factored: see tsqr.cu).
 __device__ __forceinline__ bool task_active_tc(const FoldArgs& a, int t, int k) {
   if (t < 0 || t >= a.tiles || k < 0 || k >= a.K) return false;
-  const int64_t row0 = (int64_t)t * SUB;
-  const int64_t h = mn<int64_t>(SUB, a.rows - row0);
-  if (a.tri && (int64_t)k * NB + NB <= row0) return false;
-  const int64_t lim = mn<int64_t>(a.n, a.rows_R + row0 + h);
-  return (int64_t)k * NB < lim;
+  return !(a.tri && (int64_t)k * NB + NB <= (int64_t)t * SUB);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,

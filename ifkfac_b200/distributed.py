@@ -32,13 +32,16 @@ Merge = Callable[[torch.Tensor, int, torch.Tensor, int], int]
 
 
 def fold_merge(R_a: torch.Tensor, rows_a: int, R_b: torch.Tensor, rows_b: int, prec: int = 0) -> int:
-    """[R_a; R_b] -> R_a on the device: the meaningful rows of R_b folded into R_a
-    (precision mode ``prec``, ``_lib.PREC_*``)."""
+    """[R_a; R_b] -> R_a on the device: the rows of R_b folded into R_a
+    (precision mode ``prec``, ``_lib.PREC_*``).  A trapezoidal R_b (rows_b < n)
+    is folded whole: exactly dependent columns (zero pivots) can leave some of
+    its content below row rows_b.  The merged factor has min(n, rows_a + rows_b)
+    meaningful rows."""
     n = R_a.shape[1]
-    k = min(rows_b, n)
-    if k == 0:
+    if min(rows_b, n) == 0:
         return rows_a
-    return triangular.fold_(R_a, rows_a, R_b[:k], prec=prec, trapezoidal_chunk=True)
+    triangular.fold_(R_a, rows_a, R_b, prec=prec, trapezoidal_chunk=True)
+    return min(n, rows_a + rows_b)
 
 
 def tree_merge(factors: Sequence[torch.Tensor], rows: Sequence[int],
