@@ -642,6 +642,75 @@ def run_c4(args, rank, world, local_rank):
     print(json.dumps(out), flush=True)
 
 
+def run_laplace(args, rank, world, local_rank):
+    """Next-row f4, the K-FAC Laplace posterior (ifkfac/laplace.py) of one 4096 x 4096
+    layer, N = 50000, prior precision 1e-2.  Square roots R_A, R_G come from folding
+    16384 bf16 rows each.  Ours: the precision factors C (ifk_finalize, two in one call
+    each) and draws C_G^-1 xi C_A^-T (ifk_posterior_sample), bf16 mode.  Beside it, on
+    the same GPU, the reference's route: svd(R) of both factors (torch/cuSOLVER) and
+    the draw U_G diag xi diag U_A^T (two fp32 GEMMs); and the oracle on host cores."""
+    import time
+    import torch
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import Factor, fold_segments
+    from ifkfac_b200.laplace import posterior_factors, posterior_sample
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n, p, N, lam = N_DIM, 16384, 50000, 1e-2
+    g = torch.Generator(device=dev).manual_seed(0)
+    Rs = []
+    for _ in range(2):
+        s = torch.exp(torch.rand(n, generator=g, device=dev) * math.log(100.0))
+        f = Factor(n, dev, _lib.PREC_BF16)
+        fold_segments((f,), ([(torch.randn(p, n, generator=g, device=dev) * s).bfloat16()],), None)
+        Rs.append((f.R / math.sqrt(p)).contiguous())
+    torch.cuda.synchronize()
+    xi = torch.randn(n, n, generator=g, device=dev)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            out = fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps, out
+
+    with ClockSampler(local_rank) as clk:
+        t_fac, C = timed(lambda: posterior_factors(Rs, N, lam, torch.bfloat16, _lib.PREC_BF16), 5)
+        t_draw, dW = timed(lambda: posterior_sample(xi, C[0], C[1], _lib.PREC_BF16), max(args.steps, 10))
+        C32 = posterior_factors(Rs, N, lam, torch.float32, _lib.PREC_FP32)
+        t_draw32, _ = timed(lambda: posterior_sample(xi, C32[0], C32[1], _lib.PREC_FP32), 5)
+        t_svd, evd = timed(lambda: [torch.linalg.svd(R) for R in Rs], 1)
+        U_A, U_G = evd[0][2].T.contiguous(), evd[1][2].T.contiguous()
+        sA = 1.0 / torch.sqrt(math.sqrt(N) * evd[0][1] ** 2 + math.sqrt(lam))
+        sG = 1.0 / torch.sqrt(math.sqrt(N) * evd[1][1] ** 2 + math.sqrt(lam))
+        t_evd, _ = timed(lambda: U_G @ (xi * sG[:, None] * sA[None, :]) @ U_A.T, max(args.steps, 10))
+    assert torch.isfinite(dW).all()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import ifk_oracle as O
+        RA, RG = (R.double().cpu().numpy() for R in Rs)
+        t0 = time.perf_counter()
+        CA, CG = O.posterior_factor(RA, N, lam), O.posterior_factor(RG, N, lam)
+        t1 = time.perf_counter()
+        O.posterior_sample(CA, CG, xi.double().cpu().numpy())
+        t2 = time.perf_counter()
+        cpu = {"value": 1.0 / (t2 - t1), "unit": "draws/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": "one fp64 factor pair build (%.2f s) and one draw on the host" % (t1 - t0)}
+    out = {"metric": "K-FAC Laplace posterior draws/s (one 4096 x 4096 layer)", "value": 1000.0 / t_draw,
+           "unit": "draws/s", "n_gpus": 1, "ms_per_draw": t_draw, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "f4 Laplace: C = qr([N^1/4 R; lambda^1/4 I]) per side, draw C_G^-1 xi C_A^-T",
+                      "N": N, "prior_precision": lam},
+           "factor_build_ms": t_fac, "draw_fp32_mode_ms": t_draw32,
+           "reference_route_gpu": {"svd_of_both_factors_ms": t_svd, "evd_draw_ms": t_evd},
+           "cpu_baseline": cpu, "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
 def cpu_baseline(scale=1.0):
     """The oracle port (scipy LAPACK fp32, the reference's algorithm) on host cores,
     timed on a bounded sample and extrapolated to one operator."""
@@ -710,9 +779,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c2",
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "laplace"], default="c2",
                     help="c2: the single-layer operator (the headline); c3: the 8-layer MLP training step; "
-                         "c4: the GPT-2-small-shaped decoder training step")
+                         "c4: the GPT-2-small-shaped decoder training step; laplace: K-FAC Laplace draws")
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
@@ -738,9 +807,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
         return
-    if args.config in ("c3", "c4"):
+    if args.config in ("c3", "c4", "laplace"):
         if rank == 0:
-            (run_c3 if args.config == "c3" else run_c4)(args, rank, world, local_rank)
+            {"c3": run_c3, "c4": run_c4, "laplace": run_laplace}[args.config](args, rank, world, local_rank)
         return
     if world > 1:
         import datetime

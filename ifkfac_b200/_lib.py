@@ -47,6 +47,9 @@ SIGNATURES = {
     "ifk_natgrad_workspace": (_sz, [_i64, _i64]),
     "ifk_natgrad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
                            _vp, _sz, _vp]),
+    "ifk_posterior_sample_workspace": (_sz, [_i64, _i64]),
+    "ifk_posterior_sample": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
+                                    _vp, _sz, _vp]),
     "ifk_natgrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int,
                                    _vp, _vp]),
     "ifk_natgrad_batched_workspace": (_sz, [_int, _vp, _vp]),

@@ -565,10 +565,12 @@ size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {
                            natgrad_persist_bytes(n_out, n_in)));
 }
 
-int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
-                int64_t ld_rg, int r_dtype, float* nat, int64_t ld_nat, int64_t n_out, int64_t n_in,
-                int prec, int* d_status, void* workspace, size_t workspace_bytes,
-                ifk_stream_t stream) {
+// The solves of ifk_natgrad (both = true: R_G^-1 R_G^-T g R_X^-1 R_X^-T) or of
+// ifk_posterior_sample (both = false: R_G^-1 g R_X^-T, the transposed stages left out).
+static int kron_solves(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
+                       int64_t ld_rg, int r_dtype, float* nat, int64_t ld_nat, int64_t n_out, int64_t n_in,
+                       int prec, int* d_status, void* workspace, size_t workspace_bytes, ifk_stream_t stream,
+                       bool both) {
   if (!grad_W || !R_X || !R_G || !nat) return IFK_ERR_ARG;
   if (n_out <= 0 || n_in <= 0 || ld_g < n_in || ld_nat < n_in || ld_rx < n_in || ld_rg < n_out)
     return IFK_ERR_SHAPE;
@@ -594,23 +596,41 @@ int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_r
     uint8_t* scratch = inv_x + align_up(trsm_persist_inverse_bytes(n_in));
     rc = trsm_persist_prepare(rg, ld_rg, n_out, inv_g, rx, ld_rx, n_in, inv_x, s);
     if (rc != IFK_OK) return rc;
-    rc = trsm_persist_run(rg, ld_rg, 1, nat, ld_nat, 1, n_out, n_in, inv_g, scratch, d_status, s);
+    if (both) rc = trsm_persist_run(rg, ld_rg, 1, nat, ld_nat, 1, n_out, n_in, inv_g, scratch, d_status, s);
     if (rc != IFK_OK) return rc;
     rc = trsm_persist_run(rg, ld_rg, 0, nat, ld_nat, 1, n_out, n_in, inv_g, scratch, d_status, s);
     if (rc != IFK_OK) return rc;
-    rc = trsm_persist_run(rx, ld_rx, 1, nat, 1, ld_nat, n_in, n_out, inv_x, scratch, d_status, s);
+    if (both) rc = trsm_persist_run(rx, ld_rx, 1, nat, 1, ld_nat, n_in, n_out, inv_x, scratch, d_status, s);
     if (rc != IFK_OK) return rc;
     return trsm_persist_run(rx, ld_rx, 0, nat, 1, ld_nat, n_in, n_out, inv_x, scratch, d_status, s);
   }
   // left: R_G^T T1 = g ; R_G T2 = T1   (columns of nat are independent right-hand sides)
-  rc = trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s);
+  rc = both ? trsm_run(R_G, ld_rg, r_dtype, 1, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s) : IFK_OK;
   if (rc != IFK_OK) return rc;
   rc = trsm_run(R_G, ld_rg, r_dtype, 0, nat, ld_nat, 1, n_out, n_in, prec, workspace, d_status, s);
   if (rc != IFK_OK) return rc;
   // right: R_X^T T3^T = T2^T ; R_X T4^T = T3^T on the transposed view of nat
-  rc = trsm_run(R_X, ld_rx, r_dtype, 1, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s);
+  rc = both ? trsm_run(R_X, ld_rx, r_dtype, 1, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s) : IFK_OK;
   if (rc != IFK_OK) return rc;
   return trsm_run(R_X, ld_rx, r_dtype, 0, nat, 1, ld_nat, n_in, n_out, prec, workspace, d_status, s);
+}
+
+int ifk_natgrad(const float* grad_W, int64_t ld_g, const void* R_X, int64_t ld_rx, const void* R_G,
+                int64_t ld_rg, int r_dtype, float* nat, int64_t ld_nat, int64_t n_out, int64_t n_in,
+                int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                ifk_stream_t stream) {
+  return kron_solves(grad_W, ld_g, R_X, ld_rx, R_G, ld_rg, r_dtype, nat, ld_nat, n_out, n_in, prec, d_status,
+                     workspace, workspace_bytes, stream, true);
+}
+
+size_t ifk_posterior_sample_workspace(int64_t n_out, int64_t n_in) { return ifk_natgrad_workspace(n_out, n_in); }
+
+int ifk_posterior_sample(const float* xi, int64_t ld_xi, const void* C_A, int64_t ld_ca, const void* C_G,
+                         int64_t ld_cg, int c_dtype, float* out, int64_t ld_out, int64_t n_out, int64_t n_in,
+                         int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                         ifk_stream_t stream) {
+  return kron_solves(xi, ld_xi, C_A, ld_ca, C_G, ld_cg, c_dtype, out, ld_out, n_out, n_in, prec, d_status,
+                     workspace, workspace_bytes, stream, false);
 }
 
 // a layer's slice of the batched workspace: ifk_natgrad's | the bias solves' scratch

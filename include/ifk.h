@@ -259,6 +259,31 @@ IFK_API int ifk_natgrad(const float* grad_W, int64_t ld_g,
                 int64_t n_out, int64_t n_in, int prec, int* d_status,
                 void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
+/* ---- K-FAC Laplace posterior draw ---------------------------------------- */
+
+/* Workspace bytes for ifk_posterior_sample (that of ifk_natgrad). */
+IFK_API size_t ifk_posterior_sample_workspace(int64_t n_out, int64_t n_in);
+
+/*
+ * out = C_G^-1 xi C_A^-T (n_out x n_in fp32; xi and out may alias), by two
+ * blocked triangular solves: a draw of a layer's weight perturbation from the
+ * K-FAC Laplace posterior when xi holds iid N(0, 1) entries and C_A, C_G are
+ * the upper-triangular factors of the per-side posterior precisions,
+ *   C_A^T C_A = sqrt(N) A + sqrt(lambda) I,   C_G^T C_G = sqrt(N) G + sqrt(lambda) I,
+ * i.e. ifk_finalize of R_A (R_A^T R_A = A) with rows_total = N^-1/2 and
+ * damping = sqrt(lambda).  out then has covariance
+ * (C_A^T C_A)^-1 (x) (C_G^T C_G)^-1, the posterior of LaplacePosterior
+ * (ifkfac/laplace.py:58-109, drawn at :127-149 as
+ * U_G diag((sqrt(N) d_G + sqrt(lambda))^-1/2) xi diag(..) U_A^T from
+ * eigendecompositions): the same distribution from the triangular square
+ * root, with no eigensolver.  Arguments and status as ifk_natgrad.
+ */
+IFK_API int ifk_posterior_sample(const float* xi, int64_t ld_xi,
+                         const void* C_A, int64_t ld_ca, const void* C_G, int64_t ld_cg,
+                         int c_dtype, float* out, int64_t ld_out,
+                         int64_t n_out, int64_t n_in, int prec, int* d_status,
+                         void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
 /* Largest factor order ifk_natgrad_noalloc accepts. */
 #define IFK_NOALLOC_MAX_N 4096
 

@@ -243,10 +243,44 @@ def gen_ema(ifk):
     np.savez_compressed(os.path.join(HERE, "ema_blend.npz"), **out)
 
 
+def gen_laplace(ifk):
+    """K-FAC Laplace draw (ifkfac/laplace.py:58-149): two layers whose EVD
+    factors come from svd(R) (A = R^T R: U_A = right singular vectors, d_A =
+    squared singular values, :27-29), prior precision 0.5, N = 100.  The draw's
+    xi are replayed from the same seeded generator in the reference's order."""
+    import torch.nn as nn
+    g = torch.Generator().manual_seed(11)
+    torch.manual_seed(11)
+    model = nn.Sequential(nn.Linear(12, 16), nn.ReLU(), nn.Linear(16, 6))
+    layers = [model[0], model[2]]
+    N, lam = 100, 0.5
+    out = {"N": np.array(N), "lam": np.array(lam)}
+    evd = {}
+    for i, m in enumerate(layers):
+        n_out, n_in = m.weight.shape
+        for tag, n in (("A", n_in), ("G", n_out)):
+            Xs = _scaled(g, 3 * n, n, torch.float32)
+            R = torch.linalg.qr(Xs, mode="r")[1]
+            R = R * torch.sign(torch.diagonal(R)).unsqueeze(1)
+            _, sv, Vh = torch.linalg.svd(R)
+            out[f"R_{tag}{i}"], out[f"U_{tag}{i}"], out[f"d_{tag}{i}"] = _np(R), _np(Vh.T), _np(sv ** 2)
+        evd[m] = (torch.from_numpy(out[f"U_A{i}"]), torch.from_numpy(out[f"d_A{i}"]),
+                  torch.from_numpy(out[f"U_G{i}"]), torch.from_numpy(out[f"d_G{i}"]))
+        out[f"Wmap{i}"] = _np(m.weight)
+    post = ifk.LaplacePosterior(model, evd, prior_precision=lam, dataset_size=N)
+    with contextlib.redirect_stdout(io.StringIO()):
+        post.sample_in_place(generator=torch.Generator().manual_seed(5))
+    replay = torch.Generator().manual_seed(5)
+    for i, m in enumerate(layers):
+        out[f"xi{i}"] = _np(torch.randn(*m.weight.shape, dtype=torch.float32, generator=replay))
+        out[f"Wsample{i}"] = _np(m.weight)
+    np.savez_compressed(os.path.join(HERE, "laplace.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference source tree")
-    ap.add_argument("--only", default=None, help="write one file: streaming, apply, batched, bf16, steps, hooks, ema")
+    ap.add_argument("--only", default=None, help="write one file: streaming, apply, batched, bf16, steps, hooks, ema, laplace")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import ifkfac as ifk
@@ -254,7 +288,8 @@ def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     gens = {"streaming": lambda: gen_streaming(T), "apply": lambda: gen_apply(T),
             "batched": lambda: gen_batched_and_tree(T), "bf16": lambda: gen_bf16(B),
-            "steps": lambda: gen_steps(ifk), "hooks": lambda: gen_hooks(ifk), "ema": lambda: gen_ema(ifk)}
+            "steps": lambda: gen_steps(ifk), "hooks": lambda: gen_hooks(ifk), "ema": lambda: gen_ema(ifk),
+            "laplace": lambda: gen_laplace(ifk)}
     for name, gen in gens.items():
         if args.only in (None, name):
             gen()

@@ -145,3 +145,28 @@ def test_ema_blend_restatement_matches_reference():
             got = O.ema_blend(old, new, 0.4)
             ref = z[f"ema_s4_{f}{i}"].astype(np.float64)
             assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-5
+
+
+def test_laplace_draw_restatement_matches_reference():
+    """LaplacePosterior.sample_in_place (ifkfac/laplace.py:127-146) from EVD
+    factors of svd(R): the restated draw gives the reference's weights, and the
+    triangular form (posterior_factor / posterior_sample) has the same posterior
+    precision P = U diag(sqrt(N) d + sqrt(lambda)) U^T, so the same distribution."""
+    g = load("laplace")
+    N, lam = int(g["N"]), float(g["lam"])
+    for i in range(2):
+        W = g[f"Wmap{i}"] + O.laplace_sample_evd(g[f"U_A{i}"], g[f"d_A{i}"], g[f"U_G{i}"], g[f"d_G{i}"],
+                                                 g[f"xi{i}"], N, lam)
+        assert rel(W, g[f"Wsample{i}"]) < 1e-6
+        for tag in ("A", "G"):
+            R = g[f"R_{tag}{i}"].astype(np.float64)
+            C = O.posterior_factor(R, N, lam)
+            U, d = g[f"U_{tag}{i}"].astype(np.float64), g[f"d_{tag}{i}"].astype(np.float64)
+            P = U @ np.diag(math.sqrt(N) * d + math.sqrt(lam)) @ U.T
+            assert rel(C.T @ C, P) < 1e-5
+        # same covariance per side: (C^T C)^-1 = U diag(s^2) U^T
+        for tag in ("A", "G"):
+            C = O.posterior_factor(g[f"R_{tag}{i}"].astype(np.float64), N, lam)
+            U, d = g[f"U_{tag}{i}"].astype(np.float64), g[f"d_{tag}{i}"].astype(np.float64)
+            S = U @ np.diag(O.laplace_scales(d, N, lam) ** 2) @ U.T
+            assert rel(np.linalg.inv(C.T @ C), S) < 1e-5
