@@ -532,6 +532,35 @@ def run_c3(args, rank, world, local_rank):
         opt.cleanup()
         return a.elapsed_time(b) / steps, float(loss.item())
 
+    def timed_classic():
+        """The control (next row f4): ClassicKFAC on the same model and steps (Gram
+        matrices of the captured rows, explicit inverses every 10 steps)."""
+        from ifkfac_b200.classic_kfac import ClassicKFAC
+        model = copy.deepcopy(base)
+        opt = ClassicKFAC(model, lr=1e-3, damping=1e-2, factor_update_freq=10, decomp_update_freq=10, momentum=0.9)
+
+        def one():
+            opt.zero_grad()
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = model(x)
+            loss = torch.nn.functional.cross_entropy(out.float(), y)
+            loss.backward()
+            opt.step()
+            return loss
+
+        for _ in range(max(args.warmup, 10)):
+            one()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            loss = one()
+        b.record()
+        b.synchronize()
+        opt.cleanup()
+        ms = a.elapsed_time(b) / steps
+        return {"ms_per_step": ms, "value": 1000.0 / ms, "final_loss": float(loss.item())}
+
     # the apply variants alternate (batched, per-layer, batched, per-layer) so that
     # the order of the runs in the process does not favour either; each keeps its best
     if args.profile:
@@ -541,6 +570,7 @@ def run_c3(args, rank, world, local_rank):
         runs = [timed(not args.c3_per_layer_apply)]
         if not args.c3_per_layer_apply:
             runs += [timed(False), timed(True), timed(False)]
+        classic = timed_classic() if args.c3_classic else None
     ms, loss = min(runs[0::2]) if not args.c3_per_layer_apply else runs[0]
     ms_pl = None if args.c3_per_layer_apply else min(r[0] for r in runs[1::2])
     out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
@@ -553,6 +583,7 @@ def run_c3(args, rank, world, local_rank):
                                 "of each apply, alternated"},
            "batched_qr": args.c3_batched_qr, "apply": "per-layer" if args.c3_per_layer_apply else "batched",
            "per_layer_apply": {"ms_per_step": ms_pl, "value": 1000.0 / ms_pl} if ms_pl else None,
+           "classic_kfac": classic,
            "clocks": clk.summary()}
     print(json.dumps(out), flush=True)
 
@@ -785,6 +816,8 @@ def main():
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
+    ap.add_argument("--c3-classic", action="store_true",
+                    help="c3: also time the ClassicKFAC comparator on the same model and steps")
     ap.add_argument("--schedule", choices=["one-launch", "per-tile"], default="one-launch",
                     help="fold schedule of the timed step (the other one is reported beside it)")
     ap.add_argument("--e2e-groups", default="1",

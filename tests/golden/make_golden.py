@@ -277,10 +277,44 @@ def gen_laplace(ifk):
     np.savez_compressed(os.path.join(HERE, "laplace.npz"), **out)
 
 
+def gen_classic(ifk):
+    """ClassicKFAC (ifkfac/classic_kfac.py) trajectories on CPU: an MLP with weight
+    decay, momentum and an EMA of the Gram factors (freq 2, decomp freq 2), and a
+    small conv net (im2col factors, kfac_hooks.py:151-174); parameters after every
+    step."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+    out = {}
+    g = torch.Generator().manual_seed(21)
+    cases = {
+        "mlp": (lambda: nn.Sequential(nn.Linear(10, 14), nn.Tanh(), nn.Linear(14, 4)),
+                torch.randn(48, 10, generator=g), torch.randint(0, 4, (48,), generator=g)),
+        "conv": (lambda: nn.Sequential(nn.Conv2d(2, 3, 3, padding=1), nn.ReLU(), nn.Flatten(), nn.Linear(3 * 25, 4)),
+                 torch.randn(16, 2, 5, 5, generator=g), torch.randint(0, 4, (16,), generator=g)),
+    }
+    for tag, (make, x, y) in cases.items():
+        torch.manual_seed(21)
+        model = make()
+        out[f"{tag}_x"], out[f"{tag}_y"] = x.numpy(), y.numpy()
+        for k, v in model.state_dict().items():
+            out[f"{tag}_init_{k}"] = v.numpy().copy()
+        opt = ifk.ClassicKFAC(model, lr=5e-2, damping=1e-2, factor_update_freq=2, decomp_update_freq=2,
+                              weight_decay=1e-3, momentum=0.9, gamma=0.3)
+        for s in range(1, 6):
+            loss = F.cross_entropy(model(x), y)
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+            for k, v in model.state_dict().items():
+                out[f"{tag}_s{s}_{k}"] = v.numpy().copy()
+        opt.cleanup()
+    np.savez_compressed(os.path.join(HERE, "classic.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference source tree")
-    ap.add_argument("--only", default=None, help="write one file: streaming, apply, batched, bf16, steps, hooks, ema, laplace")
+    ap.add_argument("--only", default=None, help="write one file: streaming, apply, batched, bf16, steps, hooks, ema, laplace, classic")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import ifkfac as ifk
@@ -289,7 +323,7 @@ def main():
     gens = {"streaming": lambda: gen_streaming(T), "apply": lambda: gen_apply(T),
             "batched": lambda: gen_batched_and_tree(T), "bf16": lambda: gen_bf16(B),
             "steps": lambda: gen_steps(ifk), "hooks": lambda: gen_hooks(ifk), "ema": lambda: gen_ema(ifk),
-            "laplace": lambda: gen_laplace(ifk)}
+            "laplace": lambda: gen_laplace(ifk), "classic": lambda: gen_classic(ifk)}
     for name, gen in gens.items():
         if args.only in (None, name):
             gen()
