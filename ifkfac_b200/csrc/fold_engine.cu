@@ -214,11 +214,11 @@ __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t b
                : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// Wait for this thread's bulk stores, then release *flag to other CTAs.
+// Wait for this thread's bulk stores, then release *flag to other CTAs (the
+// proxy fence orders the copy engine's writes before the release store).
 __device__ __forceinline__ void bulk_publish(int* flag) {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   asm volatile("fence.proxy.async.global;" ::: "memory");
-  __threadfence();
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
 }
 
@@ -259,13 +259,11 @@ __device__ __forceinline__ bool cta_wait_flag(const int* flag, const PFBatch& b,
 }
 
 // Publish v at *flag once every thread's global writes so far are visible:
-// the barrier orders them before thread 0's fence, whose release is cumulative.
+// the barrier orders them before thread 0's release store, and a gpu-scope
+// release is cumulative over what happens before it (no separate fence).
 __device__ __forceinline__ void cta_publish_value(int* flag, int v) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    st_release(flag, v);
-  }
+  if (threadIdx.x == 0) st_release(flag, v);
 }
 
 // fp32 values of segment row gi, columns gj .. gj + 31 of the fold (gi < rows and
@@ -634,12 +632,8 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       refresh_a1(c);
       a1_valid = true;
       // Panel k - 1 is applied to the block's R rows (written before the
-      // previous apply's last barrier); by now those writes have mostly
-      // drained, so the fence before the release is short.
-      if (tid == 0) {
-        __threadfence();
-        st_release(prog, k);
-      }
+      // barrier above): thread 0's release store publishes them.
+      if (tid == 0) st_release(prog, k);
     }
     AP_MARK(6);
     if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
