@@ -673,6 +673,194 @@ def run_c4(args, rank, world, local_rank):
     print(json.dumps(out), flush=True)
 
 
+def run_c1(args, rank, world, local_rank):
+    """BASELINE config 1, the reference's CPU-runnable case: Linear(128->256)-ReLU-Linear(256->10),
+    fp32, x (256, 128) ~ N(0, 1), random labels, cross-entropy, lr 1e-3, damping 1e-2,
+    factor_update_freq 1 (a refresh every step), momentum 0.9, 100 steps.  Beside it, the
+    same step with the curvature path in the oracle port on the host cores (forward and
+    backward in torch on the CPU; QR, damping fold, solves and update in scipy LAPACK)."""
+    import time
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from ifkfac_b200.ifkfac import IFKFAC
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    base = nn.Sequential(nn.Linear(128, 256), nn.ReLU(), nn.Linear(256, 10))
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(256, 128, generator=g)
+    y = torch.randint(0, 10, (256,), generator=g)
+    import copy
+    model = copy.deepcopy(base).to(dev)
+    xd, yd = x.to(dev), y.to(dev)
+    opt = IFKFAC(model, lr=1e-3, damping=1e-2, factor_update_freq=1, momentum=0.9)
+
+    def one():
+        opt.zero_grad()
+        loss = F.cross_entropy(model(xd), yd)
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(max(args.warmup, 3)):
+        one()
+    torch.cuda.synchronize()
+    steps = 100
+    with ClockSampler(local_rank) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            loss = one()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    opt.cleanup()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import ifk_oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        m = copy.deepcopy(base)
+        lin = [m[0], m[2]]
+        caps = {}
+        hs = [l.register_forward_hook(lambda mod, i, o: caps.__setitem__((mod, "x"), i[0].detach())) for l in lin]
+        hs += [l.register_full_backward_hook(lambda mod, gi, go: caps.__setitem__((mod, "g"), go[0].detach()))
+               for l in lin]
+        bufs = {}
+
+        def cpu_step():
+            m.zero_grad()
+            F.cross_entropy(m(x), y).backward()
+            for l in lin:
+                X, D = caps[(l, "x")].numpy(), caps[(l, "g")].numpy()
+                RX = O.get_factor(O.streaming_tsqr_update(None, X), X.shape[0], 1e-2)
+                RG = O.get_factor(O.streaming_tsqr_update(None, D), D.shape[0], 1e-2)
+                if RX is None or RG is None:  # trapezoidal (fewer rows than columns): plain step
+                    continue
+                nat = O.apply_vered(l.weight.grad.numpy(), RX, RG)
+                W, bufs[l] = O.precond_update(l.weight.detach().numpy(), bufs.get(l), nat, 1e-3, 0.9, 0.0, None)
+                nb = O.apply_vered_bias(l.bias.grad.numpy(), RG)
+                with torch.no_grad():
+                    l.weight.copy_(torch.from_numpy(W))
+                    l.bias.sub_(1e-3 * torch.from_numpy(nb))
+
+        cpu_step()
+        n_cpu = 20
+        t0 = time.perf_counter()
+        for _ in range(n_cpu):
+            cpu_step()
+        cpu_s = (time.perf_counter() - t0) / n_cpu
+        for h in hs:
+            h.remove()
+        cpu = {"value": 1.0 / cpu_s, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{n_cpu} steps: torch CPU forward/backward, oracle (scipy LAPACK) curvature and update"}
+    out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
+           "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic",
+           "config": {"workload": "C1 Linear(128-256)-ReLU-Linear(256-10), batch 256, fp32, refresh every step",
+                      "final_loss": float(loss.item()),
+                      "timing": "eager, CUDA events around the step loop (host work included)"},
+           "cpu_baseline": cpu, "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
+def run_c5(args, rank, world, local_rank):
+    """BASELINE config 5 on one GPU: a Llama-1B-shaped decoder (16 blocks, d 2048, 32 query
+    and 8 key/value heads, SwiGLU MLP 8192, vocab 128256 with the head tied to the
+    embedding, RMSNorm; no rotary embedding, which does not change a K-FAC shape),
+    random init, bf16 autocast, batch 4 x 2048 tokens, uniform random token ids.  K-FAC on
+    the 112 Linear layers of the blocks (q, k, v, o, gate, up, down), use_true_bf16,
+    damping 1e-3, factor_update_freq 20, the reference's default 2048 rows per layer and
+    step (max_seq_rows None), batched_qr.  The survey's C5 runs p = 32768 on 8 GPUs; this
+    is its one-GPU, default-rows form.  A step is forward + backward + IFKFAC.step."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from ifkfac_b200.ifkfac import IFKFAC
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    d, nh, nkv, ff, vocab, nblk, seq, batch = 2048, 32, 8, 8192, 128256, 16, 2048, 4
+    hd = d // nh
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.n1, self.n2 = nn.RMSNorm(d), nn.RMSNorm(d)
+            self.q, self.k, self.v = nn.Linear(d, d, bias=False), nn.Linear(d, nkv * hd, bias=False), \
+                nn.Linear(d, nkv * hd, bias=False)
+            self.o = nn.Linear(d, d, bias=False)
+            self.gate, self.up = nn.Linear(d, ff, bias=False), nn.Linear(d, ff, bias=False)
+            self.down = nn.Linear(ff, d, bias=False)
+
+        def forward(self, x):
+            B, T, _ = x.shape
+            h = self.n1(x)
+            q = self.q(h).view(B, T, nh, hd).transpose(1, 2)
+            k = self.k(h).view(B, T, nkv, hd).transpose(1, 2)
+            v = self.v(h).view(B, T, nkv, hd).transpose(1, 2)
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            x = x + self.o(a.transpose(1, 2).reshape(B, T, d))
+            h = self.n2(x)
+            return x + self.down(F.silu(self.gate(h)) * self.up(h))
+
+    class Llama(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.tok = nn.Embedding(vocab, d)
+            nn.init.normal_(self.tok.weight, std=0.02)  # tied head: N(0, 1) rows would give logits ~ 45
+            self.blocks = nn.ModuleList([Block() for _ in range(nblk)])
+            self.norm = nn.RMSNorm(d)
+
+        def forward(self, idx):
+            x = self.tok(idx)
+            for b in self.blocks:
+                x = b(x)
+            return F.linear(self.norm(x), self.tok.weight)  # tied head: not a K-FAC layer
+
+    torch.manual_seed(0)
+    model = Llama().to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    idx = torch.randint(0, vocab, (batch, seq + 1), generator=g, device=dev)
+    x, y = idx[:, :-1], idx[:, 1:]
+    opt = IFKFAC(model, lr=1e-4, damping=1e-3, factor_update_freq=20, momentum=0.9, use_true_bf16=True,
+                 batched_qr=True)
+
+    def one():
+        opt.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = model(x)
+        loss = F.cross_entropy(logits.float().reshape(-1, vocab), y.reshape(-1))
+        loss.backward()
+        opt.step()
+        return loss
+
+    steps = max(20, (args.steps + 19) // 20 * 20)
+    for _ in range(max(args.warmup, 20)):  # past the first refresh
+        one()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            loss = one()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
+           "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 20),
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic",
+           "config": {"workload": "C5 Llama-1B-shaped decoder on one GPU, 16 x (q, k, v, o, gate, up, down) "
+                                  "under K-FAC, 4 x 2048 tokens, 2048 rows per layer and step, bf16 autocast, "
+                                  "use_true_bf16, damping 1e-3, factor_update_freq 20, batched_qr",
+                      "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
+                      "timing": "eager, CUDA events around the step loop (host work included)"},
+           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9, "clocks": clk.summary()}
+    opt.cleanup()
+    print(json.dumps(out), flush=True)
+
+
 def run_laplace(args, rank, world, local_rank):
     """Next-row f4, the K-FAC Laplace posterior (ifkfac/laplace.py) of one 4096 x 4096
     layer, N = 50000, prior precision 1e-2.  Square roots R_A, R_G come from folding
@@ -810,9 +998,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "laplace"], default="c2",
-                    help="c2: the single-layer operator (the headline); c3: the 8-layer MLP training step; "
-                         "c4: the GPT-2-small-shaped decoder training step; laplace: K-FAC Laplace draws")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "laplace"], default="c2",
+                    help="c1: the reference's CPU-runnable MLP; c2: the single-layer operator (the headline); "
+                         "c3: the 8-layer MLP training step; "
+                         "c4: the GPT-2-small-shaped decoder training step; c5: the Llama-1B-shaped one on one GPU; "
+                         "laplace: K-FAC Laplace draws")
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
@@ -840,9 +1030,10 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
         return
-    if args.config in ("c3", "c4", "laplace"):
+    if args.config in ("c1", "c3", "c4", "c5", "laplace"):
         if rank == 0:
-            {"c3": run_c3, "c4": run_c4, "laplace": run_laplace}[args.config](args, rank, world, local_rank)
+            runs = {"c1": run_c1, "c3": run_c3, "c4": run_c4, "c5": run_c5, "laplace": run_laplace}
+            runs[args.config](args, rank, world, local_rank)
         return
     if world > 1:
         import datetime
