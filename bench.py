@@ -660,10 +660,11 @@ def run_c4(args, rank, world, local_rank):
         b.record()
         b.synchronize()
     ms = a.elapsed_time(b) / steps
+    ksum = kernel_summary(one, 20) if args.kernel_summary else None
     out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
            "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 10),
            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic",
+           "data": "synthetic", "kernel_summary": ksum,
            "config": {"workload": "C4 GPT-2-small-shaped decoder, 12 x (qkv, proj, fc, fc2) under K-FAC, "
                                   "8 x 1024 tokens, bf16 autocast, use_true_bf16, damping 1e-3, batched_qr",
                       "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
@@ -671,6 +672,31 @@ def run_c4(args, rank, world, local_rank):
            "clocks": clk.summary()}
     opt.cleanup()
     print(json.dumps(out), flush=True)
+
+
+def kernel_summary(step_fn, steps, top=20):
+    """Device time per kernel over `steps` extra calls of step_fn, under torch.profiler
+    (CUPTI activity records, no kernel replay): the `top` kernels by total time, as
+    ms per step and share of the kernels' total."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step_fn()
+        torch.cuda.synchronize()
+    rows = []
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", None)
+        if t is None:
+            t = e.cuda_time_total
+        if t > 0:
+            rows.append((t, e.key, e.count))
+    rows.sort(reverse=True)
+    tot = sum(r[0] for r in rows)
+    return {"steps": steps, "kernels_ms_per_step": round(tot / 1e3 / steps, 2),
+            "top": [{"kernel": k[:100], "ms_per_step": round(t / 1e3 / steps, 3), "share": round(t / tot, 4),
+                     "launches_per_step": round(c / steps, 1)} for t, k, c in rows[:top]]}
 
 
 def run_c1(args, rank, world, local_rank):
@@ -847,6 +873,7 @@ def run_c5(args, rank, world, local_rank):
         b.record()
         b.synchronize()
     ms = a.elapsed_time(b) / steps
+    ksum = kernel_summary(one, 20) if args.kernel_summary else None
     out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
            "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 20),
            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -856,7 +883,8 @@ def run_c5(args, rank, world, local_rank):
                                   "use_true_bf16, damping 1e-3, factor_update_freq 20, batched_qr",
                       "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
                       "timing": "eager, CUDA events around the step loop (host work included)"},
-           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9, "clocks": clk.summary()}
+           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9, "clocks": clk.summary(),
+           "kernel_summary": ksum}
     opt.cleanup()
     print(json.dumps(out), flush=True)
 
@@ -1006,6 +1034,8 @@ def main():
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
+    ap.add_argument("--kernel-summary", action="store_true",
+                    help="c4, c5: after the timed steps, profile 20 more (torch.profiler) and add the top kernels")
     ap.add_argument("--c3-classic", action="store_true",
                     help="c3: also time the ClassicKFAC comparator on the same model and steps")
     ap.add_argument("--schedule", choices=["one-launch", "per-tile"], default="one-launch",

@@ -162,14 +162,15 @@ struct PFold {
   int64_t ldR;
   int64_t n, rows_R;
   int T, K, CB, nseg;
+  int seg0;      // first of its nseg segments in PFBatch::seg
   int* prog;     // [T][CB]: k < K: panels < k applied to the block's R rows; K + s: own-panel stage s
   int* pflag;    // [T][K]
   uint8_t* img;  // [T][K][PIMG]
-  PSeg seg[MAX_SEGS];
 };
 
 struct PFBatch {
-  PFold f[MAX_FOLDS];
+  PFold f[PFOLD_MAX_FOLDS];
+  PSeg seg[PFOLD_MAX_BATCH_SEGS];
   int nf;
   int nwaves;
   int ntasks;
@@ -178,6 +179,7 @@ struct PFBatch {
   int* status;  // caller's status word (may be null)
   int wave_off[MAXW + 1];
 };
+static_assert(sizeof(PFBatch) <= 32000, "launch parameters of one persistent fold launch (limit 32764 bytes)");
 
 __device__ __forceinline__ void st16(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -555,8 +557,9 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(3, TR_NOW());
   const int tid = threadIdx.x, warp = tid >> 5;
   int si = 0;  // segment of sub-tile t
-  while (si + 1 < F.nseg && F.seg[si + 1].t0 <= t) ++si;
-  const PSeg& G = F.seg[si];
+  const PSeg* SG = b.seg + F.seg0;
+  while (si + 1 < F.nseg && SG[si + 1].t0 <= t) ++si;
+  const PSeg& G = SG[si];
   const int64_t row0 = (int64_t)(t - G.t0) * SUB;  // first row of the sub-tile within its segment
   const int h = (int)mn<int64_t>(SUB, G.rows - row0);
   const int64_t cs = (int64_t)cb * WB;
@@ -952,14 +955,14 @@ size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n) {
 int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s) {
   const int sms = num_sms();
   if (sms <= 0) return IFK_ERR_CUDA;
-  if (nf > MAX_FOLDS) return IFK_ERR_SHAPE;
+  if (nf > PFOLD_MAX_FOLDS) return IFK_ERR_SHAPE;
   PFBatch b;
   b.nf = 0;
   b.status = status;
   b.ctr = (int*)ws;
   b.abort_ = (int*)ws + 1;
   char* w = (char*)ws + 256;
-  int maxw = 0;
+  int maxw = 0, nsegs_total = 0;
   for (int q = 0; q < nf; ++q) {  // flags first, so one memset clears them all
     const PFoldDesc& D = d[q];
     const int64_t T = pfold_subtiles(D);
@@ -974,13 +977,16 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
     F.K = (int)cdiv(F.n, NB);
     F.CB = (int)cdiv(F.n, WB);
     F.nseg = 0;
+    F.seg0 = nsegs_total;
     int t0 = 0;
     int64_t off = 0;
     for (int g = 0; g < D.nseg; ++g) {
       const PFoldSeg& E = D.seg[g];
       if (E.rows <= 0) continue;
       if (E.tri && g + 1 < D.nseg) return IFK_ERR_SHAPE;  // only the last segment may be trapezoidal
-      PSeg& P = F.seg[F.nseg++];
+      if (nsegs_total == PFOLD_MAX_BATCH_SEGS) return IFK_ERR_SHAPE;  // callers split
+      PSeg& P = b.seg[nsegs_total++];
+      ++F.nseg;
       P.X = E.X;
       P.ldX = E.ldX;
       P.rows = E.rows;

@@ -73,15 +73,16 @@ int plan_pieces(const PFoldDesc& D, const PFoldSeg* segs, int nseg, std::vector<
   return IFK_OK;
 }
 
-// Persistent tensor-core folds: groups of MAX_FOLDS folds share launches; a fold
-// longer than one launch allows continues in the group's next launch.  Fold f
+// Persistent tensor-core folds: groups of PFOLD_MAX_FOLDS folds share launches (a
+// launch takes at most PFOLD_MAX_BATCH_SEGS segments; more go to a second launch);
+// a fold longer than one launch allows continues in the group's next launch.  Fold f
 // takes its segments from segs[f] (nsegs[f] of them) when segs is given, else
 // from in[f].seg.
 int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStream_t s,
                    const PFoldSeg* const* segs = nullptr, const int* nsegs = nullptr) {
-  std::vector<PFoldDesc> pieces[MAX_FOLDS];
-  for (int base = 0; base < nf; base += MAX_FOLDS) {
-    const int cnt = std::min(MAX_FOLDS, nf - base);
+  for (int base = 0; base < nf; base += PFOLD_MAX_FOLDS) {
+    const int cnt = std::min(PFOLD_MAX_FOLDS, nf - base);
+    std::vector<std::vector<PFoldDesc>> pieces(cnt);
     size_t most = 0;
     for (int q = 0; q < cnt; ++q) {
       const PFoldDesc& D = in[base + q];
@@ -91,12 +92,24 @@ int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStrea
       most = std::max(most, pieces[q].size());
     }
     for (size_t i = 0; i < most; ++i) {
-      PFoldDesc d[MAX_FOLDS];
-      int m = 0;
-      for (int q = 0; q < cnt; ++q)
-        if (i < pieces[q].size()) d[m++] = pieces[q][i];
-      const int rc = pfold_run(m, d, ws, status, s);
-      if (rc != IFK_OK) return rc;
+      std::vector<PFoldDesc> d;
+      int nseg = 0;
+      for (int q = 0; q < cnt; ++q) {
+        if (i >= pieces[q].size()) continue;
+        const PFoldDesc& P = pieces[q][i];
+        if (!d.empty() && nseg + P.nseg > PFOLD_MAX_BATCH_SEGS) {
+          const int rc = pfold_run((int)d.size(), d.data(), ws, status, s);
+          if (rc != IFK_OK) return rc;
+          d.clear();
+          nseg = 0;
+        }
+        d.push_back(P);
+        nseg += P.nseg;
+      }
+      if (!d.empty()) {
+        const int rc = pfold_run((int)d.size(), d.data(), ws, status, s);
+        if (rc != IFK_OK) return rc;
+      }
     }
   }
   return IFK_OK;
@@ -205,20 +218,14 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   cudaStream_t s = S(stream);
   if (prec == IFK_PREC_BF16) {
-    PFoldDesc d[MAX_FOLDS];
-    int cnt = 0;
+    std::vector<PFoldDesc> d;
     for (int f = 0; f < nfolds; ++f) {
       if (rows[f] == 0) continue;
-      d[cnt] = pfold_desc(R[f], ldR[f], n[f], rows_R[f]);
-      pfold_add(d[cnt++], chunk[f], ld_chunk[f], rows[f], chunk_dtype == IFK_BF16 ? 1 : 0, 0.f,
+      d.push_back(pfold_desc(R[f], ldR[f], n[f], rows_R[f]));
+      pfold_add(d.back(), chunk[f], ld_chunk[f], rows[f], chunk_dtype == IFK_BF16 ? 1 : 0, 0.f,
                 (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0);
-      if (cnt == MAX_FOLDS) {
-        const int rc = run_persistent(cnt, d, workspace, d_status, s);
-        if (rc != IFK_OK) return rc;
-        cnt = 0;
-      }
     }
-    return cnt ? run_persistent(cnt, d, workspace, d_status, s) : IFK_OK;
+    return d.empty() ? IFK_OK : run_persistent((int)d.size(), d.data(), workspace, d_status, s);
   }
   char* ws = (char*)workspace;
   FoldBatch b;

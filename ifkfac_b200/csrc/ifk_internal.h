@@ -41,6 +41,10 @@ int64_t xw_ld(int64_t n);
 // ident * I (n rows, the damping rows).  Only the last segment may be
 // trapezoidal (row i zero left of column i).
 constexpr int MAX_SEGS = 12;
+// One persistent launch takes up to PFOLD_MAX_FOLDS folds with PFOLD_MAX_BATCH_SEGS
+// segments between them (the launch parameters hold both tables).
+constexpr int PFOLD_MAX_FOLDS = 64;
+constexpr int PFOLD_MAX_BATCH_SEGS = 256;
 struct PFoldSeg {
   const void* X;
   int64_t ldX;

@@ -163,3 +163,21 @@ def test_segments_argument_errors():
     assert call(300, n, x.data_ptr()) == _lib.OK
     torch.cuda.synchronize()
     assert int(st.item()) == 0
+
+
+def test_many_folds_share_launches_bitwise():
+    """40 folds of mixed widths in one call (they share a launch: up to 64 folds and
+    256 segments per launch) give every factor bit for bit as folding it alone."""
+    from ifkfac_b200.engine import Factor, fold_segments
+    g = torch.Generator(device="cuda").manual_seed(7)
+    ns = [64 + 8 * (i % 33) for i in range(40)]
+    chunks = [[torch.randn(300 + 37 * (i % 5), n, generator=g, device="cuda").bfloat16() for _ in range(1 + i % 3)]
+              for i, n in enumerate(ns)]
+    together = [Factor(n, "cuda", _lib.PREC_BF16) for n in ns]
+    fold_segments(together, chunks, None)
+    for n, cs, f in zip(ns, chunks, together):
+        alone = Factor(n, "cuda", _lib.PREC_BF16)
+        fold_segments([alone], [cs], None)
+        torch.cuda.synchronize()
+        assert int(f.status.item()) == 0
+        assert torch.equal(f.R, alone.R)
