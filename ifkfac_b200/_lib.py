@@ -62,10 +62,14 @@ SIGNATURES = {
 }
 
 
+PER_SEGMENT_DTYPE = -1  # chunk_dtype of ifk_tsqr_fold_segments: each segment's own
+
+
 class Segment(ctypes.Structure):
     """``ifk_segment`` of include/ifk.h: rows of a chunk for ifk_tsqr_fold_segments."""
     _fields_ = [("chunk", ctypes.c_void_p), ("ld", ctypes.c_int64), ("rows", ctypes.c_int64),
-                ("row_index", ctypes.c_void_p), ("src_rows", ctypes.c_int64), ("cols", ctypes.c_int64)]
+                ("row_index", ctypes.c_void_p), ("src_rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class IFKError(RuntimeError):

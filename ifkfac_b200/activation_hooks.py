@@ -211,23 +211,30 @@ class RawActivationHooks:
         return ws
 
     def _fold_lists(self, table, items) -> None:
-        """Fold (module, [chunks]) pairs: every module's chunks in arrival order,
-        the modules of one dtype and device together, by ifk_tsqr_fold_segments
-        (no concatenation; the bucketed flush of ifkfac/activation_hooks.py:370-457
-        and the deferred drain of :347-364)."""
-        by_dt: Dict[Tuple, List] = {}
-        for module, chunks in items:
+        """Fold (module, [chunks]) pairs of one table (see _fold_entries)."""
+        self._fold_entries([(table, m, chunks) for m, chunks in items])
+
+    def _fold_entries(self, entries) -> None:
+        """Fold (table, module, [chunks]) entries: every module's chunks in arrival
+        order, all of them in one ifk_tsqr_fold_segments call per device (no
+        concatenation; the bucketed flush of ifkfac/activation_hooks.py:370-457 and
+        the deferred drain of :347-364).  With an explicit precision the chunks may
+        mix fp32 and bf16 (each segment carries its type); with PREC_AUTO the
+        precision follows the chunk type, so the dtypes fold in separate calls."""
+        groups: Dict[Tuple, List] = {}
+        for table, module, chunks in entries:
             rs = [as_rows(c) for c in chunks]
             rs = [r for r in rs if r.rows > 0]
             if not rs:
                 continue
             if not rs[0].x.is_cuda:
                 raise ValueError("ifkfac_b200 hooks need CUDA activations (no CPU path)")
-            by_dt.setdefault((rs[0].dtype, rs[0].device), []).append((module, rs))
-        for (dt, dev), lst in by_dt.items():
-            fs = [self._factor(table, m, rs[0].cols, dev) for m, rs in lst]
+            key = (rs[0].device, None if self.precision != _lib.PREC_AUTO else rs[0].dtype)
+            groups.setdefault(key, []).append((table, module, rs))
+        for (dev, dt), lst in groups.items():
+            fs = [self._factor(table, m, rs[0].cols, dev) for table, m, rs in lst]
             key = ("fold", dev)
-            self._ws[key] = fold_segments(fs, [rs for _, rs in lst], self._ws.get(key))
+            self._ws[key] = fold_segments(fs, [rs for _, _, rs in lst], self._ws.get(key))
 
     def _fold_now(self, table, module, chunk) -> None:
         self._fold_lists(table, [(module, [chunk])])
@@ -266,20 +273,21 @@ class RawActivationHooks:
         """Batched mode: fold every pending chunk (no-op otherwise)."""
         if not self.batched:
             return
-        for pending, table in ((self._pending_X, self._fx), (self._pending_G, self._fg)):
-            items = [(m, chunks) for m, chunks in pending.items() if chunks]
-            for m, _ in items:
-                pending[m] = []
-            if items:
-                self._fold_lists(table, items)
+        self._fold_pending(((self._pending_X, self._fx), (self._pending_G, self._fg)))
 
     def _drain_deferred(self) -> None:
-        for raw, table in ((self._raw_X, self._fx), (self._raw_G, self._fg)):
-            items = [(m, chunks) for m, chunks in raw.items() if chunks]
-            for m, _ in items:
-                raw[m] = []
-            if items:
-                self._fold_lists(table, items)
+        self._fold_pending(((self._raw_X, self._fx), (self._raw_G, self._fg)))
+
+    def _fold_pending(self, sources) -> None:
+        """X and delta chunks of every layer in one call (they share launches)."""
+        entries = []
+        for pending, table in sources:
+            for m, chunks in pending.items():
+                if chunks:
+                    entries.append((table, m, chunks))
+                    pending[m] = []
+        if entries:
+            self._fold_entries(entries)
 
     # ---- factors ----
     def get_factors(self, out_dtype: torch.dtype = torch.float32,

@@ -315,8 +315,9 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
                            const double* ident_tail, int prec, int* d_status, void* workspace,
                            size_t workspace_bytes, ifk_stream_t stream) {
   if (nfolds < 0 || (nfolds > 0 && (!R || !ldR || !rows_R || !n || !nseg))) return IFK_ERR_ARG;
-  if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
-  if (!prec_ok(prec)) return IFK_ERR_ARG;
+  const bool per_seg = chunk_dtype == IFK_PER_SEGMENT_DTYPE;
+  if (!dtype_ok(chunk_dtype) && !per_seg) return IFK_ERR_DTYPE;
+  if (!prec_ok(prec) || (per_seg && prec == IFK_PREC_AUTO)) return IFK_ERR_ARG;
   bool any = false;
   for (int f = 0; f < nfolds; ++f) {
     if (!R[f] || nseg[f] < 0 || (nseg[f] > 0 && !segs)) return IFK_ERR_ARG;
@@ -331,6 +332,7 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
       if (E.cols != n[f] && E.cols != n[f] - 1) return IFK_ERR_SHAPE;
       if (E.cols < 1 || E.ld < E.cols) return IFK_ERR_SHAPE;
       if (E.row_index && E.src_rows <= 0) return IFK_ERR_SHAPE;
+      if (per_seg && !dtype_ok(E.dtype)) return IFK_ERR_DTYPE;
       any = true;
     }
     any = any || (ident_tail && ident_tail[f] > 0);
@@ -356,7 +358,7 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
         P.X = E.chunk;
         P.ldX = E.ld;
         P.rows = E.rows;
-        P.xkind = chunk_dtype == IFK_BF16 ? 1 : 0;
+        P.xkind = (per_seg ? E.dtype : chunk_dtype) == IFK_BF16 ? 1 : 0;
         P.ident = 0.f;
         P.tri = 0;
         P.ridx = E.row_index;
@@ -387,8 +389,8 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
     for (int g = 0; g < nseg[f]; ++g) {
       const ifk_segment& E = segs[base + g];
       if (E.rows == 0) continue;
-      const int rc = fold_fp32(R[f], ldR[f], rr, E.chunk, E.ld, E.rows, n[f], chunk_dtype, 0, 0.f, prec, d_status,
-                               workspace, s, E.row_index, E.src_rows, E.cols);
+      const int rc = fold_fp32(R[f], ldR[f], rr, E.chunk, E.ld, E.rows, n[f], per_seg ? E.dtype : chunk_dtype, 0, 0.f,
+                               prec, d_status, workspace, s, E.row_index, E.src_rows, E.cols);
       if (rc != IFK_OK) return rc;
       rr = std::min<int64_t>(n[f], rr + E.rows);
     }

@@ -186,15 +186,19 @@ def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence], ws: t
             cs.append(r)
             dts.add(r.dtype)
         segs.append(cs)
-    if len(dts) > 1:
-        raise TypeError("all chunks of a segmented fold must share one dtype")
-    dt = _DT[dts.pop()] if dts else _lib.BF16
+    precs = {f.prec for f in factors}
+    if len(precs) > 1:
+        raise ValueError("the factors of one segmented fold share a precision mode")
+    if len(dts) > 1 and precs.pop() == _lib.PREC_AUTO:
+        raise TypeError("with PREC_AUTO all chunks of a segmented fold share one dtype (the precision follows it)")
+    dt = _DT[next(iter(dts))] if len(dts) == 1 else (_lib.PER_SEGMENT_DTYPE if dts else _lib.BF16)
     nf = len(factors)
     flat = [r for cs in segs for r in cs]
     arr = (_lib.Segment * max(len(flat), 1))()
     for i, r in enumerate(flat):
         arr[i] = _lib.Segment(r.x.data_ptr(), r.x.stride(0), r.rows,
-                              r.index.data_ptr() if r.index is not None else None, r.x.shape[0], r.x.shape[1])
+                              r.index.data_ptr() if r.index is not None else None, r.x.shape[0], r.x.shape[1],
+                              _DT[r.dtype], 0)
     ns = _arr(ctypes.c_int64, [f.n for f in factors])
     nseg = _arr(ctypes.c_int, [len(cs) for cs in segs])
     tail = _arr(ctypes.c_double, [float(v) for v in ident_tail]) if ident_tail is not None else None

@@ -138,7 +138,8 @@ IFK_API int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ld
  * column of ones is appended (the augmented-bias column of
  * ifkfac/activation_hooks.py:541-543).  src_rows is the chunk's row count: an
  * index outside [0, src_rows) reads as a zero row and sets IFK_ERR_ARG in the
- * status word.
+ * status word.  dtype (IFK_F32 or IFK_BF16) is the chunk's element type when
+ * the call's chunk_dtype is IFK_PER_SEGMENT_DTYPE, and is ignored otherwise.
  */
 typedef struct ifk_segment {
   const void* chunk;
@@ -147,7 +148,13 @@ typedef struct ifk_segment {
   const int64_t* row_index;
   int64_t src_rows;
   int64_t cols;
+  int32_t dtype;
+  int32_t reserved;
 } ifk_segment;
+
+/* chunk_dtype of ifk_tsqr_fold_segments: each segment gives its own (needs an
+ * explicit IFK_PREC_FP32 or IFK_PREC_BF16). */
+#define IFK_PER_SEGMENT_DTYPE (-1)
 
 /* Workspace bytes for ifk_tsqr_fold_segments (same arguments). */
 IFK_API size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
@@ -160,7 +167,9 @@ IFK_API size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, co
  * (one sub-tile of rows after another), while the fold of segment s + 1
  * overlaps that of segment s.  Fold f has nseg[f] segments; `segs` is flat,
  * fold after fold.  The segments need not be adjacent in memory; all have
- * element type chunk_dtype.  When ident_tail is not NULL and
+ * element type chunk_dtype, or each its own (IFK_PER_SEGMENT_DTYPE, with an
+ * explicit precision).  Folds of one call share launches (up to 64 folds and
+ * 256 segments per launch).  When ident_tail is not NULL and
  * ident_tail[f] > 0, n[f] more rows ident_tail[f] * I follow the segments
  * (the damping rows of ifk_finalize at the caller's scale: a caller that then
  * runs ifk_finalize with damping 0 and rows_total p gets the damped factor of

@@ -56,19 +56,19 @@ def test_segment_struct_matches_header():
     body = re.search(r"typedef struct ifk_segment \{(.*?)\} ifk_segment;", open(_lib.HEADER).read(), re.S).group(1)
     fields = re.findall(r"(\w+);", body)
     assert fields == [f for f, _ in _lib.Segment._fields_]
-    assert ctypes.sizeof(_lib.Segment) == 48
-    assert _lib.Segment.cols.offset == 40
+    assert ctypes.sizeof(_lib.Segment) == 56
+    assert _lib.Segment.cols.offset == 40 and _lib.Segment.dtype.offset == 48
 
 
 def test_segment_fold_argument_errors_before_any_gpu_work():
     L = _lib.lib()
     a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
     n = 64
-    seg = lambda rows=100, ld=64, cols=64, chunk=0x1000, idx=None, src=0: (_lib.Segment * 1)(
-        _lib.Segment(chunk, ld, rows, idx, src, cols))
-    call = lambda segs, ntail=None, rows_R=0: L.ifk_tsqr_fold_segments(
-        1, (ctypes.c_void_p * 1)(0x2000), a64(n), a64(rows_R), a64(n), (ctypes.c_int * 1)(1), segs, _lib.BF16,
-        (ctypes.c_double * 1)(ntail) if ntail is not None else None, _lib.PREC_BF16, None, None, 0, None)
+    seg = lambda rows=100, ld=64, cols=64, chunk=0x1000, idx=None, src=0, dt=0: (_lib.Segment * 1)(
+        _lib.Segment(chunk, ld, rows, idx, src, cols, dt, 0))
+    call = lambda segs, ntail=None, rows_R=0, cdt=_lib.BF16, prec=_lib.PREC_BF16: L.ifk_tsqr_fold_segments(
+        1, (ctypes.c_void_p * 1)(0x2000), a64(n), a64(rows_R), a64(n), (ctypes.c_int * 1)(1), segs, cdt,
+        (ctypes.c_double * 1)(ntail) if ntail is not None else None, prec, None, None, 0, None)
     assert call(seg(cols=62)) == _lib.ERR_SHAPE            # neither n nor n - 1 columns
     assert call(seg(cols=63, ld=62)) == _lib.ERR_SHAPE     # leading dimension below the columns
     assert call(seg(rows=-1)) == _lib.ERR_SHAPE
@@ -78,6 +78,10 @@ def test_segment_fold_argument_errors_before_any_gpu_work():
     assert call(seg(), rows_R=n + 1) == _lib.ERR_SHAPE
     assert call(seg(rows=0)) == _lib.OK                    # nothing to fold
     assert call(seg(cols=63)) == _lib.ERR_WORKSPACE        # valid (bias column), but no workspace
+    per = _lib.PER_SEGMENT_DTYPE
+    assert call(seg(dt=_lib.BF16), cdt=per) == _lib.ERR_WORKSPACE          # per-segment dtype, valid
+    assert call(seg(dt=5), cdt=per) == _lib.ERR_DTYPE                      # a segment's dtype is checked
+    assert call(seg(dt=_lib.F32), cdt=per, prec=_lib.PREC_AUTO) == _lib.ERR_ARG  # needs an explicit precision
     ws = L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(1), seg(rows=1000), None)
     assert ws >= L.ifk_tsqr_fold_workspace(1000, n) // 2 and ws > 0
     wt = L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(1), seg(rows=1000),

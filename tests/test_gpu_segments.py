@@ -181,3 +181,26 @@ def test_many_folds_share_launches_bitwise():
         torch.cuda.synchronize()
         assert int(f.status.item()) == 0
         assert torch.equal(f.R, alone.R)
+
+
+@pytest.mark.parametrize("prec", [_lib.PREC_BF16, _lib.PREC_FP32])
+def test_mixed_dtype_segments_in_one_call(prec):
+    """fp32 and bf16 chunks in one call (each segment carries its type; an explicit
+    precision): every factor as folding its chunks one call at a time."""
+    from ifkfac_b200.engine import Factor, fold_segments
+    g = torch.Generator(device="cuda").manual_seed(9)
+    mk = lambda r, n, dt: torch.randn(r, n, generator=g, device="cuda").to(dt)
+    lists = [[mk(300, 96, torch.float32), mk(200, 96, torch.float32)],
+             [mk(500, 160, torch.bfloat16)],
+             [mk(260, 128, torch.float32), mk(300, 128, torch.bfloat16), mk(90, 128, torch.float32)]]
+    together = [Factor(c[0].shape[1], "cuda", prec) for c in lists]
+    fold_segments(together, lists, None)
+    for cs, f in zip(lists, together):
+        alone = Factor(cs[0].shape[1], "cuda", prec)
+        for c in cs:
+            fold_segments([alone], [[c]], None)
+        torch.cuda.synchronize()
+        assert int(f.status.item()) == 0
+        assert torch.equal(f.R, alone.R)
+    with pytest.raises(TypeError):
+        fold_segments([Factor(96, "cuda")], [[mk(10, 96, torch.float32), mk(10, 96, torch.bfloat16)]], None)
