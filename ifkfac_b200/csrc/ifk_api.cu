@@ -541,6 +541,75 @@ static int finalize_many(int nfactors, const float* const* R_in, const int64_t* 
   return IFK_OK;
 }
 
+namespace {
+
+int pad_grid(int64_t total) { return (int)std::min<int64_t>(cdiv(total, 256), 4096); }
+
+size_t natgrad_persist_bytes(int64_t n_out, int64_t n_in) {
+  return align_up(trsm_persist_inverse_bytes(n_out)) + align_up(trsm_persist_inverse_bytes(n_in)) +
+         align_up(std::max(trsm_persist_workspace(n_out, n_in), trsm_persist_workspace(n_in, n_out)));
+}
+
+// Orders that are not multiples of 8 (the persistent solves copy 16-byte rows):
+// the solves run on [[R, 0], [0, I]] of order pad8(n) and a zero-padded right-hand
+// side, which leave the leading block exactly as the unpadded solves define it.
+int64_t pad8(int64_t n) { return (n + 7) / 8 * 8; }
+bool needs_pad(int64_t n_out, int64_t n_in) { return n_out % 8 != 0 || n_in % 8 != 0; }
+// the padded copies after the persistent area of the padded orders:
+// R_G' | R_X' (bf16) | B' (fp32, p_out x p_in) | b' (fp32, p_out)
+size_t pad_copies_bytes(int64_t n_out, int64_t n_in) {
+  const int64_t po = pad8(n_out), pi = pad8(n_in);
+  return align_up((size_t)po * po * 2) + align_up((size_t)pi * pi * 2) + align_up((size_t)po * pi * 4) +
+         align_up((size_t)po * 4);
+}
+size_t padded_natgrad_bytes(int64_t n_out, int64_t n_in) {
+  return align_up(natgrad_persist_bytes(pad8(n_out), pad8(n_in))) + pad_copies_bytes(n_out, n_in);
+}
+
+__global__ void pad_factor_kernel(const __nv_bfloat16* R, int64_t ld, int64_t n, __nv_bfloat16* P, int64_t np) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < np * np; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / np, c = i % np;
+    P[i] = (r < n && c < n) ? R[r * ld + c] : __float2bfloat16(r == c ? 1.f : 0.f);
+  }
+}
+
+struct Padded {
+  __nv_bfloat16 *Rg, *Rx;
+  float *B, *b;
+  uint8_t *inv_g, *inv_x, *scratch;
+  int64_t po, pi;
+};
+// Lay the padded problem out in ws and fill it: factors, zero-padded gradient (and bias).
+int pad_problem(uint8_t* ws, const void* R_G, int64_t ld_rg, const void* R_X, int64_t ld_rx, const float* g,
+                int64_t ld_g, const float* gb, int64_t n_out, int64_t n_in, Padded& P, cudaStream_t s) {
+  P.po = pad8(n_out);
+  P.pi = pad8(n_in);
+  P.inv_g = ws;
+  P.inv_x = P.inv_g + align_up(trsm_persist_inverse_bytes(P.po));
+  P.scratch = P.inv_x + align_up(trsm_persist_inverse_bytes(P.pi));
+  uint8_t* q = ws + align_up(natgrad_persist_bytes(P.po, P.pi));
+  P.Rg = (__nv_bfloat16*)q;
+  q += align_up((size_t)P.po * P.po * 2);
+  P.Rx = (__nv_bfloat16*)q;
+  q += align_up((size_t)P.pi * P.pi * 2);
+  P.B = (float*)q;
+  q += align_up((size_t)P.po * P.pi * 4);
+  P.b = (float*)q;
+  pad_factor_kernel<<<pad_grid(P.po * P.po), 256, 0, s>>>((const __nv_bfloat16*)R_G, ld_rg, n_out, P.Rg, P.po);
+  pad_factor_kernel<<<pad_grid(P.pi * P.pi), 256, 0, s>>>((const __nv_bfloat16*)R_X, ld_rx, n_in, P.Rx, P.pi);
+  IFK_CUDA_TRY(cudaGetLastError());
+  IFK_CUDA_TRY(cudaMemsetAsync(P.B, 0, (size_t)P.po * P.pi * 4, s));
+  IFK_CUDA_TRY(cudaMemcpy2DAsync(P.B, P.pi * sizeof(float), g, ld_g * sizeof(float), n_in * sizeof(float), n_out,
+                                 cudaMemcpyDeviceToDevice, s));
+  if (gb) {
+    IFK_CUDA_TRY(cudaMemsetAsync(P.b, 0, (size_t)P.po * 4, s));
+    IFK_CUDA_TRY(cudaMemcpyAsync(P.b, gb, n_out * sizeof(float), cudaMemcpyDeviceToDevice, s));
+  }
+  return IFK_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int ifk_finalize_batched(int nfactors, const float* const* R_in, const int64_t* ldR,
@@ -563,15 +632,11 @@ int ifk_finalize_many(int nfactors, const float* const* R_in, const int64_t* ldR
 // Workspace of the persistent bf16 solves: inverses of R_G | inverses of R_X |
 // scratch of the larger solve (the left solves are n_out x n_out against n_in
 // right-hand sides, the right ones the reverse).
-static size_t natgrad_persist_bytes(int64_t n_out, int64_t n_in) {
-  return align_up(trsm_persist_inverse_bytes(n_out)) + align_up(trsm_persist_inverse_bytes(n_in)) +
-         align_up(std::max(trsm_persist_workspace(n_out, n_in), trsm_persist_workspace(n_in, n_out)));
-}
-
 size_t ifk_natgrad_workspace(int64_t n_out, int64_t n_in) {
   if (n_out <= 0 || n_in <= 0) return 0;
-  return align_up(std::max(std::max(trsm_tc_workspace(n_out), trsm_tc_workspace(n_in)),
-                           natgrad_persist_bytes(n_out, n_in)));
+  size_t b = std::max(std::max(trsm_tc_workspace(n_out), trsm_tc_workspace(n_in)), natgrad_persist_bytes(n_out, n_in));
+  if (needs_pad(n_out, n_in)) b = std::max(b, padded_natgrad_bytes(n_out, n_in));
+  return align_up(b);
 }
 
 // The solves of ifk_natgrad (both = true: R_G^-1 R_G^-T g R_X^-1 R_X^-T) or of
@@ -590,11 +655,30 @@ static int kron_solves(const float* grad_W, int64_t ld_g, const void* R_X, int64
       (!workspace || !aligned(workspace) || workspace_bytes < ifk_natgrad_workspace(n_out, n_in)))
     return IFK_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
+  int rc;
+  if (prec == IFK_PREC_BF16 && r_dtype == IFK_BF16 && needs_pad(n_out, n_in)) {
+    // the persistent solves on the padded problem, then the leading block back
+    Padded P;
+    rc = pad_problem((uint8_t*)workspace, R_G, ld_rg, R_X, ld_rx, grad_W, ld_g, nullptr, n_out, n_in, P, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_prepare(P.Rg, P.po, P.po, P.inv_g, P.Rx, P.pi, P.pi, P.inv_x, s);
+    if (rc != IFK_OK) return rc;
+    if (both) rc = trsm_persist_run(P.Rg, P.po, 1, P.B, P.pi, 1, P.po, P.pi, P.inv_g, P.scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_run(P.Rg, P.po, 0, P.B, P.pi, 1, P.po, P.pi, P.inv_g, P.scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    if (both) rc = trsm_persist_run(P.Rx, P.pi, 1, P.B, 1, P.pi, P.pi, P.po, P.inv_x, P.scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    rc = trsm_persist_run(P.Rx, P.pi, 0, P.B, 1, P.pi, P.pi, P.po, P.inv_x, P.scratch, d_status, s);
+    if (rc != IFK_OK) return rc;
+    IFK_CUDA_TRY(cudaMemcpy2DAsync(nat, ld_nat * sizeof(float), P.B, P.pi * sizeof(float), n_in * sizeof(float),
+                                   n_out, cudaMemcpyDeviceToDevice, s));
+    return IFK_OK;
+  }
   if (nat != grad_W || ld_nat != ld_g) {
     IFK_CUDA_TRY(cudaMemcpy2DAsync(nat, ld_nat * sizeof(float), grad_W, ld_g * sizeof(float),
                                    n_in * sizeof(float), n_out, cudaMemcpyDeviceToDevice, s));
   }
-  int rc;
   if (prec == IFK_PREC_BF16 && r_dtype == IFK_BF16 && trsm_persist_ok(R_G, ld_rg, n_out) &&
       trsm_persist_ok(R_X, ld_rx, n_in)) {
     // persistent tensor-core solves; the diagonal-block inverses of both factors in one launch
@@ -644,7 +728,8 @@ int ifk_posterior_sample(const float* xi, int64_t ld_xi, const void* C_A, int64_
 
 // a layer's slice of the batched workspace: ifk_natgrad's | the bias solves' scratch
 static size_t natgrad_batched_slice(int64_t n_out, int64_t n_in) {
-  return ifk_natgrad_workspace(n_out, n_in) + align_up(trsm_persist_workspace(n_out, 1));
+  return ifk_natgrad_workspace(n_out, n_in) +
+         align_up(std::max(trsm_persist_workspace(n_out, 1), trsm_persist_workspace(pad8(n_out), 1)));
 }
 
 size_t ifk_natgrad_batched_workspace(int nlayers, const int64_t* n_out, const int64_t* n_in) {
@@ -693,10 +778,12 @@ int ifk_natgrad_batched(int nlayers, const float* const* grad_W, const int64_t* 
     }
   }
   // the layers of the persistent bf16 path share launches; the others go one by one
+  // (orders that are not multiples of 8 join them on their padded problem, as ifk_natgrad does)
   std::vector<int> batch;
+  const bool bf = prec == IFK_PREC_BF16 && r_dtype == IFK_BF16;
   for (int l = 0; l < nlayers; ++l) {
-    const bool pers = prec == IFK_PREC_BF16 && r_dtype == IFK_BF16 && trsm_persist_ok(R_G[l], ld_rg[l], n_out[l]) &&
-                      trsm_persist_ok(R_X[l], ld_rx[l], n_in[l]);
+    const bool pers = bf && (needs_pad(n_out[l], n_in[l]) ||
+                             (trsm_persist_ok(R_G[l], ld_rg[l], n_out[l]) && trsm_persist_ok(R_X[l], ld_rx[l], n_in[l])));
     if (pers) {
       batch.push_back(l);
       continue;
@@ -717,8 +804,30 @@ int ifk_natgrad_batched(int nlayers, const float* const* grad_W, const int64_t* 
   std::vector<int64_t> ld((size_t)2 * nb), nn((size_t)2 * nb);
   std::vector<void*> inv((size_t)2 * nb);
   std::vector<TrsmProblem> pg((size_t)nb), px((size_t)nb), pl;
+  std::vector<std::pair<int, Padded>> padded;
   for (int i = 0; i < nb; ++i) {
     const int l = batch[i];
+    if (needs_pad(n_out[l], n_in[l])) {
+      Padded P;
+      int rc = pad_problem((uint8_t*)wsl[l], R_G[l], ld_rg[l], R_X[l], ld_rx[l], grad_W[l], ld_g[l],
+                           has_bias(l) ? grad_b[l] : nullptr, n_out[l], n_in[l], P, s);
+      if (rc != IFK_OK) return rc;
+      A[2 * i] = P.Rg;
+      ld[2 * i] = P.po;
+      nn[2 * i] = P.po;
+      inv[2 * i] = P.inv_g;
+      A[2 * i + 1] = P.Rx;
+      ld[2 * i + 1] = P.pi;
+      nn[2 * i + 1] = P.pi;
+      inv[2 * i + 1] = P.inv_x;
+      pg[i] = TrsmProblem{P.Rg, P.po, P.B, P.pi, 1, P.po, P.pi, P.inv_g, P.scratch};
+      px[i] = TrsmProblem{P.Rx, P.pi, P.B, 1, P.pi, P.pi, P.po, P.inv_x, P.scratch};
+      if (has_bias(l))
+        pl.push_back(TrsmProblem{P.Rg, P.po, P.b, 1, 1, P.po, 1, P.inv_g,
+                                 wsl[l] + ifk_natgrad_workspace(n_out[l], n_in[l])});
+      padded.emplace_back(l, P);
+      continue;
+    }
     if (nat[l] != grad_W[l] || ld_nat[l] != ld_g[l])
       IFK_CUDA_TRY(cudaMemcpy2DAsync(nat[l], ld_nat[l] * sizeof(float), grad_W[l], ld_g[l] * sizeof(float),
                                      n_in[l] * sizeof(float), n_out[l], cudaMemcpyDeviceToDevice, s));
@@ -755,7 +864,17 @@ int ifk_natgrad_batched(int nlayers, const float* const* grad_W, const int64_t* 
   if (rc != IFK_OK) return rc;
   rc = trsm_persist_run_many(nb, px.data(), 1, d_status, s);
   if (rc != IFK_OK) return rc;
-  return trsm_persist_run_many(nb, px.data(), 0, d_status, s);
+  rc = trsm_persist_run_many(nb, px.data(), 0, d_status, s);
+  if (rc != IFK_OK) return rc;
+  for (const auto& e : padded) {  // the leading blocks of the padded problems
+    const int l = e.first;
+    const Padded& P = e.second;
+    IFK_CUDA_TRY(cudaMemcpy2DAsync(nat[l], ld_nat[l] * sizeof(float), P.B, P.pi * sizeof(float),
+                                   n_in[l] * sizeof(float), n_out[l], cudaMemcpyDeviceToDevice, s));
+    if (has_bias(l))
+      IFK_CUDA_TRY(cudaMemcpyAsync(nat_b[l], P.b, n_out[l] * sizeof(float), cudaMemcpyDeviceToDevice, s));
+  }
+  return IFK_OK;
 }
 
 int ifk_natgrad_bias(const float* grad_b, const void* R_G, int64_t ld_rg, int r_dtype, float* nat_b,

@@ -178,3 +178,22 @@ def test_ema_blend_matches_oracle(prec, tol):
         G = 0.3 * R_old.double().T @ R_old.double() + 0.7 * R_new.double().T @ R_new.double()
         assert float(np.linalg.norm(out.T @ out - G.cpu().numpy()) / np.linalg.norm(G.cpu().numpy())) < 2 * tol
     opt.cleanup()
+
+
+@pytest.mark.parametrize("n_out,n_in", [(100, 2048), (10, 256), (3, 5), (1000, 1001), (2047, 96)])
+def test_padded_orders_on_the_persistent_solves(n_out, n_in):
+    """Orders that are not multiples of 8 solve on [[R, 0], [0, I]] padded to the next
+    multiple of 8 with a zero-padded right-hand side: the leading block is the natural
+    gradient (held to the fp64 solve with the same bf16 factors), in both entry points
+    bit for bit."""
+    RX, RG = _factor(n_in, 3 + n_in, torch.bfloat16), _factor(n_out, 5 + n_out, torch.bfloat16)
+    g = torch.randn(n_out, n_in, generator=torch.Generator(device="cuda").manual_seed(n_out), device="cuda")
+    one = _single(g, RX, RG, _lib.PREC_BF16)
+    many = _batched([g], [RX], [RG], _lib.PREC_BF16)[0]
+    torch.cuda.synchronize()
+    assert torch.equal(one, many)
+    X, G = RX.double(), RG.double()
+    t = torch.linalg.solve_triangular(G, torch.linalg.solve_triangular(G.T, g.double(), upper=False), upper=True)
+    truth = torch.linalg.solve_triangular(X, torch.linalg.solve_triangular(X.T, t.T, upper=False), upper=True).T
+    rel = float((one.double() - truth).norm() / truth.norm())
+    assert rel < 5e-3, rel
