@@ -343,11 +343,15 @@ struct Ctx {
   uint64_t* bar;     // MMA completion
   uint64_t* ibar;    // [2] image buffer loads
   int* s_next;       // shared flag: the next panel's R rows may be staged
+  int* s_ready;      // shared flag: the next panel is published and its R rows are final
   uint32_t phase;
   uint32_t ipar;     // bit b: parity of the next load phase of image buffer b
-  int ipend;         // thread 0: bit b set while a load into buffer b is in flight
+  int ipend;         // lookahead thread: bit b set while a load into buffer b is in flight
   bool ok;
 };
+// The thread that polls ahead and issues the image loads (warp 1), so that its
+// flag loads run beside thread 0's MMA issue.
+constexpr int LA = 32;
 __device__ __forceinline__ uint32_t img_off(int b) { return b ? OFF_IMG1 : OFF_IMG0; }
 
 __device__ __forceinline__ void mma_wait(Ctx& c) {
@@ -418,19 +422,33 @@ struct ApplyOpts {
   int nbk_next = 0;
 };
 
-// Stage this thread's 32 R entries of panel rows k0 .. k0 + nbk - 1 in OFF_RN
-// (element (j, col) at j * WB + col) by asynchronous 4-byte copies; entries
-// outside the panel or the block are zero-filled.
+// Stage R rows k0 .. k0 + nbk - 1 of the block in OFF_RN (element (j, col) at
+// j * WB + col) by asynchronous copies; entries outside the panel or the block
+// are zero-filled.  With 16-byte aligned rows every thread copies 8 chunks of 4
+// columns, else 32 single entries.  Each thread waits for its own copies
+// (cp.async.wait_all) before a CTA barrier that precedes the reads.
 __device__ __forceinline__ void stage_r_rows(const Ctx& c, const PFold& F, int64_t k0, int nbk, int64_t cs,
                                              int wc, int col, int jh) {
-  const uint32_t dst = c.sb + OFF_RN + (uint32_t)((jh * 32) * WB + col) * 4u;
-  const float* src = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+  if ((F.ldR & 3) == 0 && (((uintptr_t)F.R) & 15) == 0) {
 #pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const bool v = jh * 32 + e < nbk && col < wc;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst + (uint32_t)(e * WB * 4)),
-                 "l"(v ? src + (int64_t)e * F.ldR : F.R), "r"(v ? 4 : 0)
-                 : "memory");
+    for (int m = 0; m < (NB * WB / 4) / TPB; ++m) {
+      const int idx = (int)threadIdx.x + m * TPB;
+      const int j = idx / (WB / 4), c4 = (idx % (WB / 4)) * 4;
+      const int nv = j < nbk ? (wc - c4 < 4 ? (wc - c4 > 0 ? wc - c4 : 0) : 4) : 0;
+      const uint32_t dst = c.sb + OFF_RN + (uint32_t)(j * WB + c4) * 4u;
+      const float* src = nv ? F.R + (k0 + j) * F.ldR + cs + c4 : F.R;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(nv * 4) : "memory");
+    }
+  } else {
+    const uint32_t dst = c.sb + OFF_RN + (uint32_t)((jh * 32) * WB + col) * 4u;
+    const float* src = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const bool v = jh * 32 + e < nbk && col < wc;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst + (uint32_t)(e * WB * 4)),
+                   "l"(v ? src + (int64_t)e * F.ldR : F.R), "r"(v ? 4 : 0)
+                   : "memory");
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -448,18 +466,26 @@ __device__ __forceinline__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, 
   AP_DECL
   if (tid == 0) {
     constexpr uint32_t id1 = tc::idesc_bf16(128, NB, true, true);
-#pragma unroll 1
-    for (int s = 0; s < SUB / 16; ++s) {
-      const uint64_t ad = tc::sdesc(c.sb + OFF_A1 + s * 2 * A1_K, A1_K, A1_MN);
-      const uint64_t bd = tc::sdesc(img + s * 2 * Y_I, Y_I, Y_J);
-      tc::mma_bf16(c.tm + TM_D1, ad, bd, id1, s > 0);
-    }
+    const uint64_t ad = tc::sdesc(c.sb + OFF_A1, A1_K, A1_MN);
+    const uint64_t bd = tc::sdesc(img, Y_I, Y_J);
+#pragma unroll
+    for (int s = 0; s < SUB / 16; ++s)
+      tc::mma_bf16(c.tm + TM_D1, ad + tc::doff(s * 2 * A1_K), bd + tc::doff(s * 2 * Y_I), id1, s > 0);
     tc::commit(c.bar);
+    AP_MARK(10);
+  } else if (tid == LA) {
+    // Lookahead: the next panel's images go into the other buffer if it is
+    // published; its R rows are staged during GEMM2 if sub-tile t - 1 has
+    // finished them.  When both hold, the next apply skips its flag waits.
     if (o.next_flag) {
-      if (ld_acquire(o.next_flag) >= 1) img_issue(c, o.buf ^ 1, o.next_img);
-      *c.s_next = !o.prev_prog || ld_acquire(o.prev_prog) >= o.prev_need;
+      const bool pub = ld_acquire(o.next_flag) >= 1;
+      if (pub) img_issue(c, o.buf ^ 1, o.next_img);
+      const bool fin = !o.prev_prog || ld_acquire(o.prev_prog) >= o.prev_need;
+      *c.s_next = fin;
+      *c.s_ready = pub && fin;
     } else {
       *c.s_next = 0;
+      *c.s_ready = 0;
     }
   }
   // this thread's 32 R entries, read once while GEMM1 runs (staged by this thread
@@ -477,6 +503,7 @@ __device__ __forceinline__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, 
     for (int e = 0; e < 32; ++e) rr[e] = (jh * 32 + e < nbk && col < wc) ? rp[(int64_t)e * F.ldR] : 0.f;
   }
   mma_wait(c);
+  AP_MARK(11);
   AP_MARK(1);
   {
     float w[32];
@@ -495,54 +522,87 @@ __device__ __forceinline__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, 
   AP_MARK(2);
   if (tid == 0) {
     constexpr uint32_t id2 = tc::idesc_bf16(128, NB, false, false);
-#pragma unroll 1
+    const uint64_t ah = tc::sdesc(c.sb + OFF_A2H, A2_K, A2_MN);
+    const uint64_t al = tc::sdesc(c.sb + OFF_A2L, A2_K, A2_MN);
+    const uint64_t bh = tc::sdesc(img + IMG_TH, B2_K, B2_MN);
+    const uint64_t bl = tc::sdesc(img + IMG_TL, B2_K, B2_MN);
+#pragma unroll
     for (int s = 0; s < NB / 16; ++s) {
-      const uint64_t ah = tc::sdesc(c.sb + OFF_A2H + s * 2 * A2_K, A2_K, A2_MN);
-      const uint64_t al = tc::sdesc(c.sb + OFF_A2L + s * 2 * A2_K, A2_K, A2_MN);
-      const uint64_t bh = tc::sdesc(img + IMG_TH + s * 2 * B2_K, B2_K, B2_MN);
-      const uint64_t bl = tc::sdesc(img + IMG_TL + s * 2 * B2_K, B2_K, B2_MN);
-      tc::mma_bf16(c.tm + TM_D2, ah, bh, id2, s > 0);
-      tc::mma_bf16(c.tm + TM_D2, ah, bl, id2, 1);
-      tc::mma_bf16(c.tm + TM_D2, al, bh, id2, 1);
+      const uint64_t da = tc::doff(s * 2 * A2_K), db = tc::doff(s * 2 * B2_K);
+      tc::mma_bf16(c.tm + TM_D2, ah + da, bh + db, id2, s > 0);
+      tc::mma_bf16(c.tm + TM_D2, ah + da, bl + db, id2, 1);
+      tc::mma_bf16(c.tm + TM_D2, al + da, bh + db, id2, 1);
     }
     tc::commit(c.bar);
+    AP_MARK(12);
   }
   // rr[] is in registers: the staging area takes the next panel's rows while GEMM2 runs
   if (*(volatile int*)c.s_next) stage_r_rows(c, F, o.k0_next, o.nbk_next, cs, wc, col, jh);
+  AP_MARK(13);
   mma_wait(c);
   AP_MARK(3);
-  {
-    float w[32];
-    tc::tmem_ld32(lane_base + TM_D2 + jh * 32, w);
-    float* rp = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+  float w[32];
+  tc::tmem_ld32(lane_base + TM_D2 + jh * 32, w);
+  // GEMM2 has completed: W2 goes over W^T hi
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      float v[8];
+  for (int g = 0; g < 4; ++g) {
+    float v[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = g * 8 + e;
-        v[e] = w[j];
-        if (jh * 32 + j < nbk && rcol) rp[(int64_t)j * F.ldR] = rr[j] - v[e];
-      }
-      // GEMM2 has completed: W2 goes over W^T hi
-      store8(c.sb + OFF_B3 + tc::cm_off<true>(col, jh * 32 + g * 8, A2_MN, A2_K), v);
-    }
+    for (int e = 0; e < 8; ++e) v[e] = w[g * 8 + e];
+    store8(c.sb + OFF_B3 + tc::cm_off<true>(col, jh * 32 + g * 8, A2_MN, A2_K), v);
+  }
+  // The new R rows go to global memory by 16-byte stores of whole row pieces when
+  // R's rows are 16-byte aligned: this thread's column is transposed through the
+  // A1 area, which GEMM3 does not read (GEMM1 has completed; the next refresh
+  // rewrites it after a barrier).
+  const bool vec_r = (F.ldR & 3) == 0 && (((uintptr_t)F.R) & 15) == 0;
+  float* stg = reinterpret_cast<float*>(c.sm + OFF_A1);  // element (j, column) at j * WB + column
+  if (vec_r) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stg[(jh * 32 + j) * WB + col] = rr[j] - w[j];
   }
   sync_for_mma();
   AP_MARK(4);
   if (tid == 0) {
     // D3 += (-Y) W2: negate-A bit of the instruction descriptor
     constexpr uint32_t id3 = tc::idesc_bf16(128, WB, false, false) | (1u << 13);
-#pragma unroll 1
+    const uint64_t ad = tc::sdesc(img, Y_J, Y_I);
+    const uint64_t bd = tc::sdesc(c.sb + OFF_B3, A2_K, A2_MN);
+#pragma unroll
     for (int mh = 0; mh < 2; ++mh) {
-#pragma unroll 1
-      for (int s = 0; s < NB / 16; ++s) {
-        const uint64_t ad = tc::sdesc(img + mh * 16 * Y_I + s * 2 * Y_J, Y_J, Y_I);
-        const uint64_t bd = tc::sdesc(c.sb + OFF_B3 + s * 2 * A2_K, A2_K, A2_MN);
-        tc::mma_bf16(c.tm + TM_D3 + mh * WB, ad, bd, id3, 1);
-      }
+#pragma unroll
+      for (int s = 0; s < NB / 16; ++s)
+        tc::mma_bf16(c.tm + TM_D3 + mh * WB, ad + tc::doff(mh * 16 * Y_I + s * 2 * Y_J),
+                     bd + tc::doff(s * 2 * A2_K), id3, 1);
     }
     tc::commit(c.bar);
+    AP_MARK(14);
+  }
+  // the block's R rows of the panel, written while GEMM3 runs; published by the
+  // release that follows the next CTA barrier
+  if (vec_r) {
+    const int lo = skip_half0 ? NB : 0;  // first column written (NB is a multiple of 4)
+#pragma unroll
+    for (int m = 0; m < (NB * WB / 4) / TPB; ++m) {
+      const int idx = tid + m * TPB;
+      const int j = idx / (WB / 4), c4 = (idx % (WB / 4)) * 4;
+      if (j < nbk && c4 >= lo && c4 < wc) {
+        const float4 v = *reinterpret_cast<const float4*>(stg + j * WB + c4);
+        float* dst = F.R + (k0 + j) * F.ldR + cs + c4;
+        if (c4 + 4 <= wc) {
+          *reinterpret_cast<float4*>(dst) = v;
+        } else {  // the block's last columns
+          dst[0] = v.x;
+          if (c4 + 1 < wc) dst[1] = v.y;
+          if (c4 + 2 < wc) dst[2] = v.z;
+        }
+      }
+    }
+  } else {
+    float* rp = F.R + (k0 + jh * 32) * F.ldR + cs + col;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (jh * 32 + j < nbk && rcol) rp[(int64_t)j * F.ldR] = rr[j] - w[j];
   }
   mma_wait(c);
   AP_MARK(5);
@@ -620,7 +680,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   // has finished them by then.
   const int kend = (int)mn<int64_t>(2 * cb, cdiv(lim, NB));
   int buf = 0;
-  bool rpre = false;
+  bool rpre = false, ready = false;
 #pragma unroll 1
   for (int k = kfirst; k < kend; ++k) {
 #ifdef IFK_TRACE
@@ -629,6 +689,8 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     AP_DECL
     // the operand image of X depends on the previous apply only: refresh it before waiting
     if (!a1_valid) {
+      // this thread's staged R rows are complete before the barrier (other threads read them)
+      if (rpre) asm volatile("cp.async.wait_all;" ::: "memory");
       tc::fence_before();
       __syncthreads();
       tc::fence_after();
@@ -639,13 +701,21 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       if (tid == 0) st_release(prog, k);
     }
     AP_MARK(6);
-    if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
-    if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
+    // skipped when the previous apply's lookahead saw panel k published and its R rows final
+    if (!ready) {
+      if (!cta_wait_flag(F.pflag + (size_t)t * F.K + k, b, s_ok)) return;
+      AP_MARK(7);
+      if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
+    }
     AP_MARK(9);
     TR_SET(21, TR_NOW());
     TR_ADD(9, TR_NOW() - w0);
     TR_ADD(10, 1);
-    if (tid == 0 && !(c.ipend & (1 << buf))) img_issue(c, buf, F.img + ((size_t)t * F.K + k) * PIMG);
+    if (tid == LA && !(c.ipend & (1 << buf))) {
+      // not prefetched: this thread acquires the flag itself before the copy
+      ld_acquire(F.pflag + (size_t)t * F.K + k);
+      img_issue(c, buf, F.img + ((size_t)t * F.K + k) * PIMG);
+    }
     img_wait(c, buf);
     sync_for_mma();
     if (!c.ok) return;
@@ -663,6 +733,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     }
     apply_panel(c, F, (int64_t)k * NB, (int)mn<int64_t>(NB, F.n - (int64_t)k * NB), cs, wc, false, o);
     rpre = *(volatile int*)c.s_next != 0;
+    ready = *(volatile int*)c.s_ready != 0;
     buf ^= 1;
     a1_valid = false;
 #ifdef IFK_TRACE
@@ -835,6 +906,7 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
   int* s_ok = reinterpret_cast<int*>(sm + OFF_BAR + 20);
   uint64_t* ibar = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 24);  // [2]
   int* s_next = reinterpret_cast<int*>(sm + OFF_BAR + 40);
+  int* s_ready = reinterpret_cast<int*>(sm + OFF_BAR + 44);
   const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) tc::tmem_alloc(tslot, TM_COLS);
   if (tid == 0) {
@@ -852,6 +924,7 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
   c.bar = bar;
   c.ibar = ibar;
   c.s_next = s_next;
+  c.s_ready = s_ready;
   c.phase = 0;
   c.ipar = 0;
   c.ipend = 0;
@@ -877,8 +950,8 @@ __global__ void __launch_bounds__(TPB, 1) fold_persistent_kernel(const __grid_co
   }
   // a task that gave up may leave a bulk store of panel images, a bulk load of
   // images or staged R rows in flight: wait for them (bounded) before exiting
-  if (tid == 0) {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (tid == LA) {
     for (int q = 0; q < 2; ++q)
       if (c.ipend & (1 << q)) tc::mbar_wait(ibar + q, (c.ipar >> q) & 1u);
   }

@@ -22,22 +22,17 @@ __device__ __forceinline__ long long ptime() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-#define PH_DECL                  \
-  long long ph_last = ptime();   \
-  long long ph_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#define PH_MARK(i)                     \
-  do {                                 \
-    if (threadIdx.x == 0) {            \
-      const long long t_ = ptime();    \
-      ph_acc[i] += t_ - ph_last;       \
-      ph_last = t_;                    \
-    }                                  \
+#define PH_DECL long long ph_last = ptime();
+#define PH_MARK(i)                                                          \
+  do {                                                                      \
+    if (threadIdx.x == 0) {                                                 \
+      const long long t_ = ptime();                                         \
+      atomicAdd(&g_panel_phase[i], (unsigned long long)(t_ - ph_last));     \
+      ph_last = t_;                                                         \
+    }                                                                       \
   } while (0)
-#define PH_FLUSH()                                                                   \
-  if (threadIdx.x == 0) {                                                            \
-    for (int q_ = 0; q_ < 8; ++q_) atomicAdd(&g_panel_phase[q_], (unsigned long long)ph_acc[q_]); \
-    atomicAdd(&g_panel_phase[8], 1ull);                                              \
-  }
+#define PH_FLUSH()                                   \
+  if (threadIdx.x == 0) atomicAdd(&g_panel_phase[8], 1ull);
 #else
 #define PH_DECL
 #define PH_MARK(i) do { } while (0)

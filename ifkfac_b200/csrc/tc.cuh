@@ -36,6 +36,11 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
+// Descriptor increment that moves its start address by `bytes` (a multiple of
+// 16).  Shared-memory addresses stay below 256 KB, so the 14-bit start field
+// does not carry into the next field.
+__host__ __device__ constexpr uint64_t doff(uint32_t bytes) { return (uint64_t)(bytes >> 4); }
+
 // Instruction descriptor of kind::f16 with bf16 A/B and fp32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
