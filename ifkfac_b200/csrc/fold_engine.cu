@@ -268,6 +268,48 @@ __device__ __forceinline__ void cta_publish_value(int* flag, int v) {
   if (threadIdx.x == 0) st_release(flag, v);
 }
 
+// Own-panel stages of a task in its progress counter (after the apply stages
+// 0 .. K): panel q of the block publishes the R diagonal block rows of its leaf
+// s at stage K + 1 + 5q + s as soon as that leaf ends; stage K + 5 marks the
+// first panel applied to the block's second half and K + 9 the task done.
+__host__ __device__ constexpr int stage_leaf(int K, int q, int s) { return K + 1 + 5 * q + s; }
+__host__ __device__ constexpr int stage_half(int K) { return K + 5; }
+__host__ __device__ constexpr int stage_done(int K) { return K + 9; }
+
+// Leaf hooks of the fold's own panels: leaf s of sub-tile t starts once
+// sub-tile t - 1 has published the R diagonal block rows of its leaf s (those
+// rows are then final for t - 1), so consecutive sub-tiles factor the same
+// panel one leaf apart; the rows go back to R when the leaf ends.
+struct FoldLeafHook {
+  float* R;
+  int64_t ldR, c0;
+  int nbk, stage0;
+  const int* prev_prog;  // null for the first sub-tile
+  int* prog;
+  const PFBatch* b;
+  int* s_ok;
+  template <class SM>
+  __device__ __forceinline__ bool before_leaf(SM& S, int s) {
+    if (prev_prog && !cta_wait_ge(prev_prog, stage0 + s, *b, s_ok)) return false;
+    const int L0 = s * panel::LEAF;
+    for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
+      const int i = L0 + idx / NB, j = idx % NB;
+      S.Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? R[(c0 + i) * ldR + c0 + j] : 0.f;
+    }
+    __syncthreads();
+    return true;
+  }
+  template <class SM>
+  __device__ __forceinline__ void after_leaf(SM& S, int s) {
+    const int L0 = s * panel::LEAF;
+    for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
+      const int i = L0 + idx / NB, j = idx % NB;
+      if (i < nbk && j < nbk && j >= i) R[(c0 + i) * ldR + c0 + j] = S.Rk[i * LDP + j];
+    }
+    cta_publish_value(prog, stage0 + s);
+  }
+};
+
 // fp32 values of segment row gi, columns gj .. gj + 31 of the fold (gi < rows and
 // the valid count already bounded by the fold's width).  Gathered rows come from
 // row ridx[gi] of X; an index outside X gives a zero row and IFK_ERR_ARG.
@@ -639,7 +681,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   const int* prev_prog = t > 0 ? F.prog + (size_t)(t - 1) * F.CB + cb : nullptr;
 
   if (G.tri && cs + WB <= row0) {  // block entirely left of the sub-tile's diagonal: nothing to do
-    cta_publish_value(prog, F.K + 3);
+    cta_publish_value(prog, stage_done(F.K));
     return;
   }
   TR_SET(4, TR_NOW());
@@ -745,11 +787,12 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 
   // ---- factor the block's own panels ----
   // Stages of this phase, published in prog and awaited from COL(t-1, cb):
-  //   K + 1: R diagonal block of panel 2cb written; K + 2: panel 2cb applied to
-  //   the block's second half (R rows of panel 2cb final); K + 3: R diagonal
-  //   block of panel 2cb + 1 written.  A panel this sub-tile skips (beyond its
-  //   rank bound, or left of its diagonal in a trapezoidal fold) is skipped by
-  //   every earlier sub-tile too, or by every later one, so its stage passes at once.
+  //   stage_leaf(K, q, s): rows of leaf s of panel 2cb + q's R diagonal block
+  //   written; stage_half(K): panel 2cb applied to the block's second half (R
+  //   rows of panel 2cb final); stage_done(K).  A panel this sub-tile skips
+  //   (beyond its rank bound, or left of its diagonal in a trapezoidal fold) is
+  //   skipped by every earlier sub-tile too, or by every later one, so its stages
+  //   pass at once.
   TR_SET(6, TR_NOW());
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
   int* pending_img = nullptr;  // flag of panel images whose bulk store is in flight
@@ -758,12 +801,11 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     const int kk = 2 * cb + q;
     const int64_t c0 = (int64_t)kk * NB;
     if (kk >= F.K || c0 >= lim || kk < kfirst) {
-      cta_publish_value(prog, F.K + 1 + 2 * q);
+      cta_publish_value(prog, q == 0 ? stage_half(F.K) : stage_done(F.K));
       continue;
     }
     const int nbk = (int)mn<int64_t>(NB, F.n - c0);
     const int nact = (int)mn<int64_t>(nbk, lim - c0);
-    if (t > 0 && !cta_wait_ge(prev_prog, F.K + 1 + 2 * q, b, s_ok)) return;
 #ifdef IFK_TRACE
     const long long l0 = TR_NOW();
     TR_SET(18 + q, l0);
@@ -784,17 +826,15 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
         for (int e = 0; e < 32; ++e) S.P[(g * 32 + e) * panel::SP + r] = v[e];
       }
     }
-    for (int idx = tid; idx < NB * NB; idx += TPB) {
-      const int i = idx / NB, j = idx % NB;
-      S.Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? F.R[(c0 + i) * F.ldR + c0 + j] : 0.f;
-    }
     __syncthreads();
 #ifdef IFK_TRACE
     const long long p0 = TR_NOW();
     const long long k0 = clock64();
     TR_ADD(8, p0 - l0);
 #endif
-    panel::panel_factor<SUB>(S, nbk, nact);
+    // the R diagonal block is read and written leaf by leaf (FoldLeafHook)
+    FoldLeafHook hook{F.R, F.ldR, c0, nbk, stage_leaf(F.K, q, 0), t > 0 ? prev_prog : nullptr, prog, &b, s_ok};
+    if (!panel::panel_factor<SUB>(S, nbk, nact, hook)) return;
 #ifdef IFK_TRACE
     const long long p1 = TR_NOW();
     TR_ADD(11, p1 - p0);
@@ -824,28 +864,19 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       store8(c.sb + OFF_IMG0 + IMG_TH + off, hi);
       store8(c.sb + OFF_IMG0 + IMG_TL + off, lo);
     }
-    for (int idx = tid; idx < NB * NB; idx += TPB) {
-      const int i = idx / NB, j = idx % NB;
-      if (i < nbk && j < nbk && j >= i) F.R[(c0 + i) * F.ldR + c0 + j] = S.Rk[i * LDP + j];
-    }
-    // The R diagonal block (stage K + 1 + 2q) goes out at once; the images go
-    // by a bulk store.  The first panel's images are released only before the
-    // second panel's overwrite them (the copy runs under the apply to the
-    // block's second half and the second panel); the second panel's at once.
+    // The images go by a bulk store.  The first panel's images are released only
+    // before the second panel's overwrite them (the copy runs under the apply to
+    // the block's second half and the second panel); the second panel's at once.
     tc::fence_async_smem();
     __syncthreads();
     if (tid == 0) bulk_store(F.img + ((size_t)t * F.K + kk) * PIMG, c.sb + OFF_IMG0, PIMG);
     const bool half = q == 0 && wc > NB;
     if (half) {
-      cta_publish_value(prog, F.K + 1 + 2 * q);
       TR_SET(16, TR_NOW());
       pending_img = F.pflag + (size_t)t * F.K + kk;
     } else {
       __syncthreads();
-      if (tid == 0) {
-        bulk_publish(F.pflag + (size_t)t * F.K + kk);
-        st_release(prog, F.K + 1 + 2 * q);
-      }
+      if (tid == 0) bulk_publish(F.pflag + (size_t)t * F.K + kk);
     }
     TR_ADD(13, TR_NOW() - p1);
     if (q == 0) {
@@ -854,12 +885,12 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 #endif
       if (half) {
         // the first panel also acts on the block's second half
-        if (t > 0 && !cta_wait_ge(prev_prog, F.K + 2, b, s_ok)) return;
+        if (t > 0 && !cta_wait_ge(prev_prog, stage_half(F.K), b, s_ok)) return;
         refresh_a1(c);
         sync_for_mma();
         apply_panel(c, F, c0, nbk, cs, wc, true, ApplyOpts{});  // own images: buffer 0
       }
-      cta_publish_value(prog, F.K + 2);
+      cta_publish_value(prog, stage_half(F.K));
       TR_SET(17, TR_NOW());
       TR_ADD(14, TR_NOW() - h0);
     }
@@ -869,7 +900,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     __syncthreads();
   }
   tc::fence_before();
-  cta_publish_value(prog, F.K + 3);
+  cta_publish_value(prog, stage_done(F.K));
   TR_SET(7, TR_NOW());
   TR_FLUSH();
 }

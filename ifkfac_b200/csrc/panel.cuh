@@ -15,13 +15,10 @@ namespace panel {
 __device__ unsigned long long g_panel_phase[16];
 #endif
 #ifdef IFK_TRACE_PANEL
-// Time spent in each phase of panel_factor (ns, summed over panels; slot 8
-// counts panels).  Thread 0 keeps the sums in registers.
-__device__ __forceinline__ long long ptime() {
-  long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
+// Time spent in each phase of panel_factor (SM cycles, summed over panels; slot 8
+// counts panels).
+// SM cycle counter (cheap to read; thread 0 only, so deltas are on one SM)
+__device__ __forceinline__ long long ptime() { return clock64(); }
 #define PH_DECL long long ph_last = ptime();
 #define PH_MARK(i)                                                          \
   do {                                                                      \
@@ -294,14 +291,29 @@ __device__ __forceinline__ void gram_steps(PanelSmemT<ROWS>& S, int L0, int jl, 
   if (lane == 0) S.jend = jend;
 }
 
+// Leaf hooks of panel_factor.  Rows L0 .. L0 + 15 of the R diagonal block are
+// read and written by leaf L0 / 16 only, so a caller may load them just before
+// that leaf (before_leaf, which ends with a barrier of the panel's threads and
+// returns false to abandon the panel) and store them as soon as it ends
+// (after_leaf, called after the leaf's last barrier).  NoLeafHook: the caller
+// loads and stores the whole block around the call.
+struct NoLeafHook {
+  template <class SM>
+  __device__ __forceinline__ bool before_leaf(SM&, int) { return true; }
+  template <class SM>
+  __device__ __forceinline__ void after_leaf(SM&, int) {}
+};
+
 // Factor the panel in S.P (ROWS x NB fp32, column-major; rows beyond the
 // sub-tile are zero) under the R diagonal block S.Rk.  nbk panel columns exist,
 // the first nact carry reflectors (the rest lie beyond the rank bound and get
 // identity reflectors).  On return S.P holds Y, S.Rk the new R block
 // (non-negative diagonal), S.Tm the compact-WY T (row-major) and S.tau the
 // tau's.  Threads 0 .. ROWS-1 call it; it begins and ends with a barrier of them.
-template <int ROWS>
-static __device__ __noinline__ void panel_factor(PanelSmemT<ROWS>& S, const int nbk, const int nact) {
+// Returns false when a hook abandoned the panel (every thread returns together).
+template <int ROWS, class Hook = NoLeafHook>
+static __device__ __noinline__ bool panel_factor(PanelSmemT<ROWS>& S, const int nbk, const int nact,
+                                                 Hook hook = Hook()) {
   constexpr int SP = Geo<ROWS>::SP;
   constexpr int PT = ROWS;
   const int tid = threadIdx.x;
@@ -319,6 +331,9 @@ static __device__ __noinline__ void panel_factor(PanelSmemT<ROWS>& S, const int 
   for (int s = 0; s < NLEAF; ++s) {
     const int L0 = s * LEAF;
     if (L0 >= nbk) break;
+    if (!hook.before_leaf(S, s)) return false;
+    // the leaf; every exit from it ('continue') follows a barrier of the panel's threads
+    do {
     const int nl = nact - L0 < LEAF ? nact - L0 : LEAF;  // reflectors of this leaf (may be <= 0)
     float a[LEAF];
 #pragma unroll
@@ -456,6 +471,8 @@ static __device__ __noinline__ void panel_factor(PanelSmemT<ROWS>& S, const int 
     }
     psync<ROWS>();
     PH_MARK(6);
+    } while (0);
+    hook.after_leaf(S, s);
   }
   // T assembly: T_{01} = -T_0 G_{01} T_1, T_{23} likewise, then the 32 x 32 coupling
   float* Tmp = S.Zp;
@@ -471,6 +488,7 @@ static __device__ __noinline__ void panel_factor(PanelSmemT<ROWS>& S, const int 
   psync<ROWS>();
   PH_MARK(7);
   PH_FLUSH()
+  return true;
 }
 
 }  // namespace panel

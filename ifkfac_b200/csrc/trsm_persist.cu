@@ -319,12 +319,11 @@ __global__ void __launch_bounds__(TPB, 1) trsm_persist_kernel(const __grid_const
           if (!ok) break;
           tc::fence_after();
           const uint32_t a0 = sb + (uint32_t)st * SZ_STAGE, x0 = a0 + SZ_A;
-#pragma unroll 1
-          for (int k = 0; k < NB2 / 16; ++k) {
-            const uint64_t ad = tc::sdesc(a0 + k * 2 * A_K, A_K, A_MN);
-            const uint64_t bd = tc::sdesc(x0 + k * 2 * X_K, X_K, X_N);
-            tc::mma_bf16(tm + dbuf, ad, bd, idK, (i > 0 || k > 0) ? 1u : 0u);
-          }
+          const uint64_t ad = tc::sdesc(a0, A_K, A_MN), bd = tc::sdesc(x0, X_K, X_N);
+          tc::mma_bf16(tm + dbuf, ad, bd, idK, i > 0 ? 1u : 0u);
+#pragma unroll
+          for (int k = 1; k < NB2 / 16; ++k)
+            tc::mma_bf16(tm + dbuf, ad + tc::doff(k * 2 * A_K), bd + tc::doff(k * 2 * X_K), idK, 1u);
           commit_to(bar_addr(sb, B_EMPTY + st));
           ++g;
         }
@@ -333,15 +332,16 @@ __global__ void __launch_bounds__(TPB, 1) trsm_persist_kernel(const __grid_const
         ok = wait_phase(bar_addr(sb, B_YRDY), row & 1, abort_) && wait_phase(bar_addr(sb, B_INVF), row & 1, abort_);
         if (!ok) break;
         tc::fence_after();
-#pragma unroll 1
-        for (int k = 0; k < NB2 / 16; ++k) {
-          const uint64_t ah = tc::sdesc(sb + OFF_IH + k * 2 * A_K, A_K, A_MN);
-          const uint64_t al = tc::sdesc(sb + OFF_IL + k * 2 * A_K, A_K, A_MN);
-          const uint64_t bh = tc::sdesc(sb + OFF_YH + k * 2 * X_K, X_K, X_N);
-          const uint64_t bl = tc::sdesc(sb + OFF_YL + k * 2 * X_K, X_K, X_N);
-          tc::mma_bf16(tm + TM_X, ah, bh, idI, k > 0);
-          tc::mma_bf16(tm + TM_X, ah, bl, idI, 1);
-          tc::mma_bf16(tm + TM_X, al, bh, idI, 1);
+        {
+          const uint64_t ah = tc::sdesc(sb + OFF_IH, A_K, A_MN), al = tc::sdesc(sb + OFF_IL, A_K, A_MN);
+          const uint64_t bh = tc::sdesc(sb + OFF_YH, X_K, X_N), bl = tc::sdesc(sb + OFF_YL, X_K, X_N);
+#pragma unroll
+          for (int k = 0; k < NB2 / 16; ++k) {
+            const uint64_t da = tc::doff(k * 2 * A_K), dx = tc::doff(k * 2 * X_K);
+            tc::mma_bf16(tm + TM_X, ah + da, bh + dx, idI, k > 0);
+            tc::mma_bf16(tm + TM_X, ah + da, bl + dx, idI, 1);
+            tc::mma_bf16(tm + TM_X, al + da, bh + dx, idI, 1);
+          }
         }
         commit_to(bar_addr(sb, B_XFULL));
         commit_to(bar_addr(sb, B_INVE));
