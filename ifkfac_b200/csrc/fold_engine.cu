@@ -35,27 +35,32 @@ namespace {
 constexpr int WB = 128;   // columns of a task
 constexpr int TPB = 256;  // 8 warps; warps w and w + 4 share TMEM lanes 32(w%4)..+31
 static_assert(TPB == panel::PT2, "the persistent fold runs the panel with all its threads");
-constexpr int MAXW = 384; // waves per launch
-// Ticket order: wave d = t + CBW * cb (then by fold and t).  Any positive
-// weights give a topological order of the dependencies; weighting the column
-// block more hands out the tasks that have many panels to apply (right-hand
-// blocks) before the tasks of later sub-tiles that could only wait.
-#ifndef IFK_FOLD_CBW
-#define IFK_FOLD_CBW 2
-#endif
-constexpr int CBW = IFK_FOLD_CBW;
+constexpr int MAXW = 1536;  // waves per launch (the table of wave offsets in the launch parameters)
+// Ticket order: wave d = t + cbw * cb (then by fold and t).  Any positive
+// weights give a topological order of the dependencies.  The weight sets how
+// far a column block's tasks trail the block to their left: a task handed out
+// long before the panels it applies are published only waits, one handed out
+// late delays the panel chain.  The next block's panels come about three
+// sub-tile steps after a block's (the sub-tiles trail one another by a leaf,
+// a block by two panels plus applies); measured on the config-2 fold (8.6 ms
+// at weight 8 against 9.9 at 2, 9.3 at 3, 8.8 at 12 and 12.4 at 32), the weight
+// is CBW_TARGET, lowered per launch where the wave table would overflow.
+constexpr int CBW_TARGET = 8;
+// Sub-tiles per launch piece (callers split longer folds): the limit that weight
+// 2 and a 384-wave table gave, so workspaces keep their size.
+constexpr int PIECE_WAVES = 384, PIECE_CBW = 2;
 
 // The sub-tiles t of wave d for a fold of T sub-tiles and CB column blocks:
-// t = tlo, tlo + CBW, ... (cnt of them), column block (d - t) / CBW.
-__host__ __device__ __forceinline__ void wave_range(int d, int T, int CB, int* tlo, int* cnt) {
-  int lo = d - CBW * (CB - 1);
+// t = tlo, tlo + cbw, ... (cnt of them), column block (d - t) / cbw.
+__host__ __device__ __forceinline__ void wave_range(int d, int T, int CB, int cbw, int* tlo, int* cnt) {
+  int lo = d - cbw * (CB - 1);
   if (lo < 0) lo = 0;
-  lo += (d - lo) % CBW;
+  lo += (d - lo) % cbw;
   const int hi = d < T - 1 ? d : T - 1;
   *tlo = lo;
-  *cnt = hi >= lo ? (hi - lo) / CBW + 1 : 0;
+  *cnt = hi >= lo ? (hi - lo) / cbw + 1 : 0;
 }
-__host__ __device__ __forceinline__ int num_waves(int T, int CB) { return T + CBW * (CB - 1); }
+__host__ __device__ __forceinline__ int num_waves(int T, int CB, int cbw) { return T + cbw * (CB - 1); }
 using panel::LDP;
 using panel::PanelSmem;
 
@@ -172,6 +177,7 @@ struct PFBatch {
   PFold f[PFOLD_MAX_FOLDS];
   PSeg seg[PFOLD_MAX_BATCH_SEGS];
   int nf;
+  int cbw;  // ticket-order weight of the column block
   int nwaves;
   int ntasks;
   int* ctr;     // ticket counter
@@ -917,11 +923,11 @@ __device__ __forceinline__ void decode(const PFBatch& b, int tk, int* f, int* t,
   for (int q = 0; q < b.nf; ++q) {
     const PFold& F = b.f[q];
     int tlo, cnt;
-    wave_range(d, F.T, F.CB, &tlo, &cnt);
+    wave_range(d, F.T, F.CB, b.cbw, &tlo, &cnt);
     if (r < cnt) {
       *f = q;
-      *t = tlo + r * CBW;
-      *cb = (d - *t) / CBW;
+      *t = tlo + r * b.cbw;
+      *cb = (d - *t) / b.cbw;
       return;
     }
     r -= cnt;
@@ -1044,7 +1050,7 @@ int64_t pfold_subtiles(const PFoldDesc& d) {
   return t;
 }
 
-int64_t pfold_max_subtiles(int64_t n) { return (int64_t)MAXW - CBW * (cdiv(n, WB) - 1); }
+int64_t pfold_max_subtiles(int64_t n) { return (int64_t)PIECE_WAVES - PIECE_CBW * (cdiv(n, WB) - 1); }
 
 size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n) {
   size_t b = 256;
@@ -1066,7 +1072,7 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
   b.ctr = (int*)ws;
   b.abort_ = (int*)ws + 1;
   char* w = (char*)ws + 256;
-  int maxw = 0, nsegs_total = 0;
+  int tmax = 0, cbmax = 1, nsegs_total = 0;
   for (int q = 0; q < nf; ++q) {  // flags first, so one memset clears them all
     const PFoldDesc& D = d[q];
     const int64_t T = pfold_subtiles(D);
@@ -1109,9 +1115,19 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
     w += align256((size_t)F.T * F.CB * 4);
     F.pflag = (int*)w;
     w += align256((size_t)F.T * F.K * 4);
-    maxw = maxw > num_waves(F.T, F.CB) ? maxw : num_waves(F.T, F.CB);
+    tmax = tmax > F.T ? tmax : F.T;
+    cbmax = cbmax > F.CB ? cbmax : F.CB;
   }
   if (b.nf == 0) return IFK_OK;
+  // the largest weight up to CBW_TARGET whose waves fit the table (at least
+  // PIECE_CBW: every fold has at most pfold_max_subtiles sub-tiles)
+  b.cbw = cbmax > 1 ? (int)mn<int64_t>(CBW_TARGET, (MAXW - tmax) / (cbmax - 1)) : CBW_TARGET;
+  if (b.cbw < 1) return IFK_ERR_SHAPE;
+  int maxw = 0;
+  for (int g = 0; g < b.nf; ++g) {
+    const int nw = num_waves(b.f[g].T, b.f[g].CB, b.cbw);
+    maxw = maxw > nw ? maxw : nw;
+  }
   const size_t flag_bytes = (size_t)(w - (char*)ws);
   for (int g = 0; g < b.nf; ++g) {
     b.f[g].img = (uint8_t*)w;
@@ -1123,7 +1139,7 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s)
     b.wave_off[dd] = acc;
     for (int g = 0; g < b.nf; ++g) {
       int tlo, cnt;
-      wave_range(dd, b.f[g].T, b.f[g].CB, &tlo, &cnt);
+      wave_range(dd, b.f[g].T, b.f[g].CB, b.cbw, &tlo, &cnt);
       acc += cnt;
     }
   }
