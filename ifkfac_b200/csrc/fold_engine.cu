@@ -423,15 +423,15 @@ __device__ void refresh_a1(Ctx& c) {
     const int r = tid;
     const uint32_t base = c.tm + ((uint32_t)((warp & 3) * 32) << 16) + TM_D3 + h * WB;
 #pragma unroll 1
-    for (int q = 0; q < WB / 32; ++q) {
-      float v[32];
-      tc::tmem_ld32(base + q * 32, v);
+    for (int q = 0; q < WB / 64; ++q) {
+      float v[64];
+      tc::tmem_ld64(base + q * 64, v);
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < 8; ++g) {
         float e8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) e8[e] = v[g * 8 + e];
-        store8(c.sb + OFF_A1 + tc::cm_off<false>(q * 32 + g * 8, r, A1_MN, A1_K), e8);
+        store8(c.sb + OFF_A1 + tc::cm_off<false>(q * 64 + g * 8, r, A1_MN, A1_K), e8);
       }
     }
   }
@@ -824,13 +824,10 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       const int hh = tid >> 7;
       const int r = tid;
       const uint32_t base = c.tm + ((uint32_t)((warp & 3) * 32) << 16) + TM_D3 + hh * WB + q * NB;
-#pragma unroll 1
-      for (int g = 0; g < 2; ++g) {
-        float v[32];
-        tc::tmem_ld32(base + g * 32, v);
+      float v[NB];
+      tc::tmem_ld64(base, v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) S.P[(g * 32 + e) * panel::SP + r] = v[e];
-      }
+      for (int e = 0; e < NB; ++e) S.P[e * panel::SP + r] = v[e];
     }
     __syncthreads();
 #ifdef IFK_TRACE
