@@ -87,3 +87,22 @@ def test_segment_fold_argument_errors_before_any_gpu_work():
     wt = L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(1), seg(rows=1000),
                                             (ctypes.c_double * 1)(1.0))
     assert wt >= ws                                       # the damping rows add sub-tiles
+
+
+def test_fold_workspace_stops_at_one_launch_piece():
+    """A fold taller than one persistent launch runs as several launches over one
+    workspace, so its workspace stops growing at the piece size: 384 - 2 (CB - 1)
+    sub-tiles of 256 rows, 322 at n = 4096 (CB = 32 column blocks).  Chunks of
+    2048 rows keep the fp32 path's share fixed."""
+    L = _lib.lib()
+    n = 4096
+    a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
+
+    def ws(nchunks):
+        segs = (_lib.Segment * nchunks)(*[_lib.Segment(0x1000, n, 2048, None, 0, n, 0, 0)
+                                          for _ in range(nchunks)])
+        return L.ifk_tsqr_fold_segments_workspace(1, a64(n), (ctypes.c_int * 1)(nchunks), segs, None)
+
+    piece = 322 // 8  # whole chunks of 8 sub-tiles below the piece size
+    assert ws(piece) < ws(piece + 1) == ws(piece + 2) == ws(200)
+    assert ws(1) < ws(2) < ws(piece)
