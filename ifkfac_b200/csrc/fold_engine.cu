@@ -3,12 +3,13 @@
 // The fold R <- qr([R; X]).R is cut into tasks COL(f, t, cb): fold f, row
 // sub-tile t (SUB = 256 rows) and column block cb (WB = 128 columns, i.e. two
 // panels of NB = 64).  One CTA per SM takes tickets from a global counter in
-// wave order (t + cb), which is a topological order of the dependencies:
+// wave order (t + cbw * cb), which is a topological order of the dependencies:
 //   COL(f, t, cb) applies panel k < 2cb of sub-tile t once that panel is
 //   published by COL(f, t, k/2) and COL(f, t-1, cb) has applied its own panel
 //   k (the R rows of panel k in block cb are then final for sub-tile t-1: a
-//   progress counter per task), and factors its own panels as COL(f, t-1, cb)
-//   finishes the same R rows.  Sub-tile t so trails sub-tile t-1 by one step.
+//   progress counter per task), and factors each 16-column leaf of its own
+//   panels as COL(f, t-1, cb) finishes the same rows of the R diagonal block.
+//   Sub-tile t so trails sub-tile t-1 by one leaf.
 // A task only waits for lower tickets, which were handed to CTAs already
 // running, so the schedule cannot deadlock; every wait is bounded anyway and
 // reports IFK_ERR_TIMEOUT.
@@ -457,7 +458,7 @@ __device__ __forceinline__ void img_wait(Ctx& c, int b) {
 // Where apply_panel takes its images and R rows, and its lookahead to the next panel.
 struct ApplyOpts {
   int buf = 0;                      // image buffer holding the panel's Y / T images
-  bool rpre = false;                // the panel's R rows were staged in OFF_RN by this thread
+  bool rpre = false;                // the panel's R rows were staged in OFF_RN during the previous apply
   // Lookahead to the next panel (none when next_flag is null), checked by
   // thread 0 while GEMM1 runs: its images are loaded into the other buffer if
   // it is published, and its R rows (k0_next, nbk_next) are staged while
@@ -536,7 +537,7 @@ __device__ __forceinline__ void apply_panel(Ctx& c, const PFold& F, int64_t k0, 
       *c.s_ready = 0;
     }
   }
-  // this thread's 32 R entries, read once while GEMM1 runs (staged by this thread
+  // this thread's 32 R entries, read once while GEMM1 runs (staged by the CTA
   // during the previous apply, or from global memory)
   const bool rcol = col < wc && !(skip_half0 && col < NB);
   float rr[32];
