@@ -10,36 +10,30 @@
 // blocks of one factor) lives in a fixed file-scope device array sized for
 // factors of order up to IFK_NOALLOC_MAX_N.  Every GPU that loads the library
 // holds that array until the process exits.
-#include <mutex>
-
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
 
 namespace {
 
 constexpr int64_t kMaxN = IFK_NOALLOC_MAX_N;
-constexpr size_t kScratchBytes = 2ull * 2ull * (size_t)((kMaxN + 127) / 128) * 128 * 128;  // 2 MiB
+constexpr size_t kScratchBytes = 2ull << 20;  // trsm_tc_workspace(IFK_NOALLOC_MAX_N), checked per call
 
 // Shared by every call on a device; it keeps the last call's contents.
 static __device__ __align__(256) unsigned char g_natgrad_scratch[kScratchBytes];
 
-// Device address of g_natgrad_scratch per device, looked up once with that
-// device current.  In host code the symbol itself is only a host-side handle,
-// never a device address, so kernels are always given the looked-up pointer.
-std::mutex g_mu;
-void* g_addr[128] = {};
-
+// Device address of g_natgrad_scratch in the current context.  In host code the
+// symbol itself is only a host-side handle, never a device address, so kernels
+// are always given the address looked up here, with the calling device
+// current.  It is looked up on every call (cheap once the module is loaded)
+// rather than cached per device, so a context destroyed and created again
+// (cudaDeviceReset) never leaves a stale address behind.  The first call on a
+// device loads the module there; make it before any stream capture.
 int scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return IFK_ERR_CUDA;
-  if (dev < 0 || dev >= 128) return IFK_ERR_DEVICE;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_natgrad_scratch) != cudaSuccess || !p) return IFK_ERR_CUDA;
-    g_addr[dev] = p;
-  }
-  *out = g_addr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_natgrad_scratch) != cudaSuccess || !p) return IFK_ERR_CUDA;
+  *out = p;
   return IFK_OK;
 }
 
@@ -53,6 +47,8 @@ extern "C" int ifk_natgrad_noalloc(const float* grad_W, int64_t ld_g, const void
   if (n_out <= 0 || n_in <= 0 || ld_g < n_in || ld_nat < n_in || ld_rx < n_in || ld_rg < n_out)
     return IFK_ERR_SHAPE;
   if (n_out > kMaxN || n_in > kMaxN) return IFK_ERR_LIMIT;
+  // the scratch layout of the per-block-row solves must fit the fixed array
+  if (ifk::trsm_tc_workspace(n_out > n_in ? n_out : n_in) > kScratchBytes) return IFK_ERR_LIMIT;
   if (r_dtype != IFK_F32 && r_dtype != IFK_BF16) return IFK_ERR_DTYPE;
   if (prec != IFK_PREC_AUTO && prec != IFK_PREC_FP32 && prec != IFK_PREC_BF16) return IFK_ERR_ARG;
   if (prec == IFK_PREC_AUTO) prec = r_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;

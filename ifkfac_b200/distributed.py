@@ -102,8 +102,10 @@ def merge_running(factor: triangular.RunningFactor,
 
 class DistributedIFKFAC:
     """Data-parallel IFKFAC over a process group: the reference optimizer's
-    semantics on the rows of every rank, with the work split the survey's
-    multi-GPU plan gives.
+    semantics on the rows of every rank: the TSQR is sharded by batch rows, the
+    local factors are combined by the merge tree of the reference's ``tsqr``
+    (``ifkfac/triangular.py:150-227``), and whole layers are dealt to ranks for
+    their solves.
 
     * Each rank's hooks fold that rank's rows (batch-sharded streaming TSQR).
     * At a refresh every layer's running factors are merged across ranks by the

@@ -9,8 +9,11 @@
  *
  * Conventions
  *  - All matrices are device pointers, row-major, with an explicit leading
- *    dimension in elements.  The caller owns every buffer; the library never
- *    allocates device memory on these paths and never frees caller memory.
+ *    dimension in elements.  The caller owns every buffer and passes the
+ *    scratch each call needs as a workspace; the library never allocates
+ *    device memory on these paths and never frees caller memory.  One
+ *    exception: ifk_natgrad_noalloc takes no workspace and uses a fixed 2 MiB
+ *    device array inside the library (present on every GPU that loads it).
  *  - R factors are n x n fp32 (or bf16 where stated), upper triangular, with a
  *    non-negative diagonal (the reference's positive-diagonal convention,
  *    ifkfac/triangular.py:230-239).  A running factor that has seen fewer
@@ -22,8 +25,10 @@
  *    out wait) are written to a caller-provided device int, which stays 0 on
  *    success.
  *  - Calls are reentrant: no hidden global state other than the per-device
- *    kernel attributes set on first use.  Calls that share a workspace must be
- *    ordered on one stream.
+ *    kernel attributes set on first use, and the fixed scratch array of
+ *    ifk_natgrad_noalloc (shared by all of its calls, which must therefore be
+ *    ordered by the caller).  Calls that share a workspace must be ordered on
+ *    one stream.
  *  - Precision: IFK_PREC_BF16 runs the GEMM-shaped work on tcgen05 tensor
  *    cores with bf16 operands and fp32 accumulation (fp32 panels, norms,
  *    divides and storage); IFK_PREC_FP32 runs everything in fp32 on the CUDA
