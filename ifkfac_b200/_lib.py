@@ -21,6 +21,7 @@ NOALLOC_MAX_N = 4096
 F32, BF16 = 0, 1
 PREC_AUTO, PREC_FP32, PREC_BF16 = 0, 1, 2
 FOLD_TRAPEZOIDAL_CHUNK = 1
+FOLD_DEBUG_WITHHOLD = 256  # tests of the failure path only
 
 _i64, _sz, _vp, _int, _dbl = ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int, ctypes.c_double
 
@@ -37,6 +38,8 @@ SIGNATURES = {
                                      _vp, _sz, _vp]),
     "ifk_tsqr_fold_segments_workspace": (_sz, [_int, _vp, _vp, _vp, _vp]),
     "ifk_tsqr_fold_segments": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _int, _vp, _vp, _sz, _vp]),
+    "ifk_rtree_merge_workspace": (_sz, [_int, _i64]),
+    "ifk_rtree_merge": (_int, [_int, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "ifk_finalize_workspace": (_sz, [_i64]),
     "ifk_finalize_batched_workspace": (_sz, [_int, _vp]),
     "ifk_finalize_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _dbl, _vp, _vp, _int, _int, _vp,

@@ -184,6 +184,8 @@ struct PFBatch {
   int* ctr;     // ticket counter
   int* abort_;  // set when a wait gave up: every CTA stops
   int* status;  // caller's status word (may be null)
+  uint32_t wait_limit;  // polls of a cross-CTA wait before it gives up
+  int withhold;         // test only: the first panel of fold 0 is never published
   int wave_off[MAXW + 1];
 };
 static_assert(sizeof(PFBatch) <= 32000, "launch parameters of one persistent fold launch (limit 32764 bytes)");
@@ -225,10 +227,11 @@ __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t b
 }
 // Wait for this thread's bulk stores, then release *flag to other CTAs (the
 // proxy fence orders the copy engine's writes before the release store).
-__device__ __forceinline__ void bulk_publish(int* flag) {
+// release == false (the test-only withheld panel) waits for the stores alone.
+__device__ __forceinline__ void bulk_publish(int* flag, bool release = true) {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   asm volatile("fence.proxy.async.global;" ::: "memory");
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
+  if (release) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -244,7 +247,7 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 __device__ __forceinline__ bool cta_wait_ge(const int* flag, int target, const PFBatch& b, int* s_ok) {
   if (threadIdx.x == 0) {
     int ok = 0;
-    for (uint32_t it = 0; it < (1u << 24); ++it) {
+    for (uint32_t it = 0; it < b.wait_limit; ++it) {
       if (ld_acquire(flag) >= target) {
         ok = 1;
         break;
@@ -803,6 +806,9 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(6, TR_NOW());
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
   int* pending_img = nullptr;  // flag of panel images whose bulk store is in flight
+  // test only (IFK_FOLD_DEBUG_WITHHOLD): panel 0 of fold 0's first sub-tile is never
+  // published, so every wait on it runs out and the launch reports IFK_ERR_TIMEOUT
+  const bool withheld0 = b.withhold && f == 0 && t == 0 && cb == 0;
 #pragma unroll 1
   for (int q = 0; q < 2; ++q) {
     const int kk = 2 * cb + q;
@@ -846,7 +852,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 #endif
     TR_ADD(12, 1);
     if (pending_img) {  // the first panel's bulk store must be done before its images are overwritten
-      if (tid == 0) bulk_publish(pending_img);
+      if (tid == 0) bulk_publish(pending_img, !withheld0);
       pending_img = nullptr;
       __syncthreads();
     }
@@ -880,7 +886,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       pending_img = F.pflag + (size_t)t * F.K + kk;
     } else {
       __syncthreads();
-      if (tid == 0) bulk_publish(F.pflag + (size_t)t * F.K + kk);
+      if (tid == 0) bulk_publish(F.pflag + (size_t)t * F.K + kk, !(withheld0 && q == 0));
     }
     TR_ADD(13, TR_NOW() - p1);
     if (q == 0) {
@@ -900,7 +906,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     }
   }
   if (pending_img) {
-    if (tid == 0) bulk_publish(pending_img);
+    if (tid == 0) bulk_publish(pending_img, !withheld0);
     __syncthreads();
   }
   tc::fence_before();
@@ -1060,13 +1066,17 @@ size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n) {
   return b;
 }
 
-int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s) {
+int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s, int debug) {
   const int sms = num_sms();
   if (sms <= 0) return IFK_ERR_CUDA;
   if (nf > PFOLD_MAX_FOLDS) return IFK_ERR_SHAPE;
   PFBatch b;
   b.nf = 0;
   b.status = status;
+  // a cross-CTA wait polls about every 0.1 us: 2^24 polls are a few seconds, the
+  // test-only short limit (IFK_FOLD_DEBUG_WITHHOLD) a few milliseconds
+  b.wait_limit = (debug & PFOLD_DEBUG_WITHHOLD) ? (1u << 14) : (1u << 24);
+  b.withhold = (debug & PFOLD_DEBUG_WITHHOLD) ? 1 : 0;
   b.ctr = (int*)ws;
   b.abort_ = (int*)ws + 1;
   char* w = (char*)ws + 256;

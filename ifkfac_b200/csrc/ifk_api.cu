@@ -79,7 +79,7 @@ int plan_pieces(const PFoldDesc& D, const PFoldSeg* segs, int nseg, std::vector<
 // takes its segments from segs[f] (nsegs[f] of them) when segs is given, else
 // from in[f].seg.
 int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStream_t s,
-                   const PFoldSeg* const* segs = nullptr, const int* nsegs = nullptr) {
+                   const PFoldSeg* const* segs = nullptr, const int* nsegs = nullptr, int debug = 0) {
   for (int base = 0; base < nf; base += PFOLD_MAX_FOLDS) {
     const int cnt = std::min(PFOLD_MAX_FOLDS, nf - base);
     std::vector<std::vector<PFoldDesc>> pieces(cnt);
@@ -98,7 +98,7 @@ int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStrea
         if (i >= pieces[q].size()) continue;
         const PFoldDesc& P = pieces[q][i];
         if (!d.empty() && nseg + P.nseg > PFOLD_MAX_BATCH_SEGS) {
-          const int rc = pfold_run((int)d.size(), d.data(), ws, status, s);
+          const int rc = pfold_run((int)d.size(), d.data(), ws, status, s, debug);
           if (rc != IFK_OK) return rc;
           d.clear();
           nseg = 0;
@@ -107,7 +107,7 @@ int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStrea
         nseg += P.nseg;
       }
       if (!d.empty()) {
-        const int rc = pfold_run((int)d.size(), d.data(), ws, status, s);
+        const int rc = pfold_run((int)d.size(), d.data(), ws, status, s, debug);
         if (rc != IFK_OK) return rc;
       }
     }
@@ -160,16 +160,18 @@ int ifk_tsqr_fold(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int6
   if (n <= 0 || rows < 0 || rows_R < 0 || rows_R > n || ldR < n || (rows > 0 && ld_chunk < n))
     return IFK_ERR_SHAPE;
   if (!dtype_ok(chunk_dtype)) return IFK_ERR_DTYPE;
-  if (!prec_ok(prec) || (flags & ~IFK_FOLD_TRAPEZOIDAL_CHUNK)) return IFK_ERR_ARG;
+  if (!prec_ok(prec) || (flags & ~(IFK_FOLD_TRAPEZOIDAL_CHUNK | IFK_FOLD_DEBUG_WITHHOLD))) return IFK_ERR_ARG;
   if (rows == 0) return IFK_OK;
   if (!workspace || !aligned(workspace) || workspace_bytes < fold_ws(rows, n))
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
+  if ((flags & IFK_FOLD_DEBUG_WITHHOLD) && prec != IFK_PREC_BF16) return IFK_ERR_ARG;
   if (prec == IFK_PREC_BF16) {
     PFoldDesc d = pfold_desc(R, ldR, n, rows_R);
     pfold_add(d, chunk, ld_chunk, rows, chunk_dtype == IFK_BF16 ? 1 : 0, 0.f,
               (flags & IFK_FOLD_TRAPEZOIDAL_CHUNK) ? 1 : 0);
-    return run_persistent(1, &d, workspace, d_status, S(stream));
+    return run_persistent(1, &d, workspace, d_status, S(stream), nullptr, nullptr,
+                          (flags & IFK_FOLD_DEBUG_WITHHOLD) ? PFOLD_DEBUG_WITHHOLD : 0);
   }
   FoldArgs a;
   a.R = R;
@@ -400,6 +402,68 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
       if (rc != IFK_OK) return rc;
     }
   }
+  return IFK_OK;
+}
+
+// ---- R-tree merge of factors held by one process ----------------------------
+
+size_t ifk_rtree_merge_workspace(int nfactors, int64_t n) {
+  if (nfactors <= 0 || n <= 0) return 0;
+  // the widest round merges nfactors / 2 pairs, each a fold of up to n rows
+  return std::max<size_t>((size_t)(nfactors / 2) * fold_ws(n, n), ALIGN);
+}
+
+int ifk_rtree_merge(int nfactors, float* const* R, const int64_t* ldR, const int64_t* rows, int64_t n, int prec,
+                    int64_t* rows_out, int* d_status, void* workspace, size_t workspace_bytes,
+                    ifk_stream_t stream) {
+  if (nfactors <= 0 || !R || !ldR || !rows || !rows_out) return IFK_ERR_ARG;
+  if (!prec_ok(prec) || prec == IFK_PREC_AUTO) return IFK_ERR_ARG;
+  if (n <= 0) return IFK_ERR_SHAPE;
+  for (int i = 0; i < nfactors; ++i) {
+    if (!R[i]) return IFK_ERR_ARG;
+    if (ldR[i] < n || rows[i] < 0 || rows[i] > n) return IFK_ERR_SHAPE;
+  }
+  if (nfactors > 1 && (!workspace || !aligned(workspace) ||
+                       workspace_bytes < ifk_rtree_merge_workspace(nfactors, n)))
+    return IFK_ERR_WORKSPACE;
+  // items of the current round: (factor index, meaningful rows)
+  std::vector<std::pair<int, int64_t>> items;
+  for (int i = 0; i < nfactors; ++i) items.emplace_back(i, rows[i]);
+  while (items.size() > 1) {
+    std::vector<std::pair<int, int64_t>> next;
+    std::vector<float*> ra;
+    std::vector<const void*> rb;
+    std::vector<int64_t> lda, ldb, rows_a, rows_b, nn;
+    for (size_t i = 0; i < items.size(); i += 2) {
+      if (i + 1 == items.size()) {  // odd one out: carried forward
+        next.push_back(items[i]);
+        continue;
+      }
+      const auto a = items[i], b = items[i + 1];
+      next.emplace_back(a.first, std::min<int64_t>(n, a.second + b.second));
+      if (b.second == 0) continue;
+      ra.push_back(R[a.first]);
+      lda.push_back(ldR[a.first]);
+      rows_a.push_back(a.second);
+      rb.push_back(R[b.first]);
+      ldb.push_back(ldR[b.first]);
+      // bf16 mode: rows past a factor's count stay zero (the fold's rank bound), so
+      // only the meaningful rows are folded; fp32 mode folds the whole factor, where
+      // a zero pivot can leave content below that count
+      rows_b.push_back(prec == IFK_PREC_BF16 ? b.second : n);
+      nn.push_back(n);
+    }
+    if (!ra.empty()) {
+      // the merges of one round share one launch (each a trapezoidal-chunk fold)
+      const int rc = ifk_tsqr_fold_batched((int)ra.size(), ra.data(), lda.data(), rows_a.data(), rb.data(),
+                                           ldb.data(), rows_b.data(), nn.data(), IFK_F32, prec,
+                                           IFK_FOLD_TRAPEZOIDAL_CHUNK, d_status, workspace, workspace_bytes,
+                                           stream);
+      if (rc != IFK_OK) return rc;
+    }
+    items.swap(next);
+  }
+  *rows_out = items[0].second;
   return IFK_OK;
 }
 

@@ -87,8 +87,11 @@ int64_t pfold_subtiles(const PFoldDesc& d);
 int64_t pfold_max_subtiles(int64_t n);
 // workspace of one launch over folds of the given sub-tile counts and widths
 size_t pfold_workspace(int nf, const int64_t* subtiles, const int64_t* n);
-// one launch; every fold must have at most pfold_max_subtiles sub-tiles
-int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s);
+// one launch; every fold must have at most pfold_max_subtiles sub-tiles.  debug:
+// PFOLD_DEBUG_WITHHOLD (tests only) withholds the first panel of the first fold and
+// shortens the cross-CTA waits, so the launch ends with IFK_ERR_TIMEOUT.
+constexpr int PFOLD_DEBUG_WITHHOLD = 1;
+int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s, int debug = 0);
 
 // chunk (bf16 or fp32, rows x n) -> X fp32.  With ridx, row i is chunk row ridx[i]
 // (an index outside [0, src_rows) gives a zero row and IFK_ERR_ARG in *status);

@@ -2,30 +2,36 @@
 
 Each rank folds its own share of the rows into a local running factor (the
 hooks or :class:`ifkfac_b200.triangular.RunningFactor`).  :func:`rtree_merge`
-then combines the local factors into the factor of all rows:
+then combines the local factors into the factor of all rows, in the merge
+order of the reference's ``tsqr`` tree (``ifkfac/triangular.py:207-220``:
+round by round, adjacent pairs in rank order, the odd one carried forward):
 
-1. one ``all_gather`` of the local n x n factors (fp32, missing rows zero, into
-   one stacked buffer) and one of their row counts;
-2. the binary merge tree of the reference's ``tsqr``
-   (``ifkfac/triangular.py:207-220``): round by round, adjacent pairs in rank
-   order are merged, the odd one out is carried forward.  A merge folds the
-   second factor's rows into the first as a trapezoidal chunk
-   (``ifk_tsqr_fold`` with ``IFK_FOLD_TRAPEZOIDAL_CHUNK``, the structured
-   [R_i; R_j] QR), which keeps the diagonal non-negative like the reference's
-   sign normalisation.
+1. one small ``all_gather`` of the ranks' row counts, so that every rank knows
+   the row count of every subtree;
+2. ceil(log2 world) rounds of pairwise exchange: in the round of stride s, rank
+   i (i mod 2s == 0) receives the factor of rank i + s and merges it into its
+   own, and rank i + s leaves the tree.  The merges of one round run on
+   different ranks at the same time.  A merge folds the second factor's rows
+   into the first as a trapezoidal chunk (``ifk_tsqr_fold`` with
+   ``IFK_FOLD_TRAPEZOIDAL_CHUNK``, the structured [R_i; R_j] QR), which keeps
+   the diagonal non-negative like the reference's sign normalisation;
+3. a broadcast of rank 0's merged factor.
 
-Every rank runs the same tree over the same gathered inputs with the same
-kernels, so every rank ends with the same factor.  The total row count (for the
+So every rank ends with the same factor.  The total row count (for the
 1 / sqrt(p) scaling of ``get_factors``) is the sum over ranks.
+:func:`tree_merge` runs the same tree on factors that one process holds.
 """
 from __future__ import annotations
 
+import logging
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
 from . import triangular
+
+logger = logging.getLogger(__name__)
 
 # merge(R_a, rows_a, R_b, rows_b) -> rows of the merged factor, written into R_a
 Merge = Callable[[torch.Tensor, int, torch.Tensor, int], int]
@@ -37,11 +43,39 @@ def fold_merge(R_a: torch.Tensor, rows_a: int, R_b: torch.Tensor, rows_b: int, p
     is folded whole: exactly dependent columns (zero pivots) can leave some of
     its content below row rows_b.  The merged factor has min(n, rows_a + rows_b)
     meaningful rows."""
+    from . import _lib
     n = R_a.shape[1]
     if min(rows_b, n) == 0:
         return rows_a
-    triangular.fold_(R_a, rows_a, R_b, prec=prec, trapezoidal_chunk=True)
+    # bf16 mode keeps the rows past a factor's count zero (the fold's rank bound),
+    # so only the meaningful rows are folded
+    chunk = R_b[:min(rows_b, n)] if prec == _lib.PREC_BF16 else R_b
+    triangular.fold_(R_a, rows_a, chunk, prec=prec, trapezoidal_chunk=True)
     return min(n, rows_a + rows_b)
+
+
+def tree_merge_device(factors: Sequence[torch.Tensor], rows: Sequence[int], prec: int) -> int:
+    """The tree of :func:`tree_merge` on factors one process holds, by the library's
+    ``ifk_rtree_merge`` (the merges of each round in one launch); the result is in
+    ``factors[0]``.  Returns its meaningful rows."""
+    import ctypes
+    from . import _lib
+    L = _lib.lib()
+    k = len(factors)
+    if k != len(rows) or k == 0:
+        raise ValueError("tree_merge_device needs one row count per factor")
+    n = factors[0].shape[1]
+    for f in factors:
+        if f.dtype != torch.float32 or f.shape != (n, n) or f.stride(1) != 1 or not f.is_cuda:
+            raise ValueError("factors must be n x n row-major float32 CUDA tensors")
+    ws = torch.empty(max(int(L.ifk_rtree_merge_workspace(k, n)), 256), dtype=torch.uint8, device=factors[0].device)
+    out = ctypes.c_int64(0)
+    _lib.check(L.ifk_rtree_merge(
+        k, (ctypes.c_void_p * k)(*[f.data_ptr() for f in factors]),
+        (ctypes.c_int64 * k)(*[f.stride(0) for f in factors]), (ctypes.c_int64 * k)(*[int(r) for r in rows]),
+        n, prec, ctypes.byref(out), None, ws.data_ptr(), ws.numel(),
+        torch.cuda.current_stream().cuda_stream), "ifk_rtree_merge")
+    return int(out.value)
 
 
 def tree_merge(factors: Sequence[torch.Tensor], rows: Sequence[int],
@@ -63,35 +97,71 @@ def tree_merge(factors: Sequence[torch.Tensor], rows: Sequence[int],
     return items[0]
 
 
-def gather_factors(R: torch.Tensor, rows: int, rows_seen: int,
-                   group: Optional[dist.ProcessGroup] = None
-                   ) -> Tuple[List[torch.Tensor], List[int], List[int]]:
-    """All ranks' factors (views of one gathered tensor), meaningful row counts
-    and total row counts, in rank order."""
-    world = dist.get_world_size(group)
-    n = R.shape[1]
-    counts = torch.tensor([int(rows), int(rows_seen)], dtype=torch.int64, device=R.device)
-    all_counts = torch.empty(world, 2, dtype=torch.int64, device=R.device)
-    dist.all_gather(list(all_counts.unbind(0)), counts, group=group)
-    stacked = torch.empty(world, n, n, dtype=R.dtype, device=R.device)
-    factors = list(stacked.unbind(0))
-    dist.all_gather(factors, R.contiguous(), group=group)
-    c = all_counts.cpu().tolist()
-    return factors, [r for r, _ in c], [s for _, s in c]
+def _global_rank(group, r: int) -> int:
+    return dist.get_global_rank(group, r) if group is not None else r
 
 
 def rtree_merge(R: torch.Tensor, rows: int, rows_seen: int,
                 group: Optional[dist.ProcessGroup] = None,
                 merge: Merge = fold_merge) -> Tuple[int, int]:
     """Replace the local factor ``R`` (n x n fp32, ``rows`` meaningful rows,
-    built from ``rows_seen`` data rows) by the factor of every rank's rows.
-    Returns (meaningful rows, total data rows), identical on every rank."""
+    built from ``rows_seen`` data rows) by the factor of every rank's rows, by
+    pairwise merges in ceil(log2 world) rounds and a broadcast (the tree of
+    ``ifkfac/triangular.py:207-220``).  Returns (meaningful rows, total data
+    rows), identical on every rank.  If a collective fails (a rank that never
+    posts its factor makes its partner's receive time out), the error
+    propagates and ``R`` is left as it was: the merges run on a copy."""
     if R.dim() != 2 or R.shape[0] != R.shape[1]:
         raise ValueError("rtree_merge expects an n x n factor buffer")
-    factors, rows_all, seen_all = gather_factors(R, rows, rows_seen, group)
-    merged, merged_rows = tree_merge(factors, rows_all, merge)
-    R.copy_(merged)
-    return merged_rows, sum(seen_all)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = R.shape[1]
+    counts = torch.tensor([int(rows), int(rows_seen)], dtype=torch.int64, device=R.device)
+    all_counts = torch.empty(world, 2, dtype=torch.int64, device=R.device)
+    dist.all_gather(list(all_counts.unbind(0)), counts, group=group)
+    c = all_counts.cpu().tolist()
+    rows_all, seen_all = [r for r, _ in c], [x for _, x in c]
+    total_rows, total_seen = min(n, sum(rows_all)), sum(seen_all)
+    if world == 1:
+        return total_rows, total_seen
+    work = R.clone()
+    cur = min(n, rows_all[rank])
+    other = None
+    s = 1
+    while s < world:
+        if rank % (2 * s) == 0:
+            partner = rank + s
+            if partner < world:
+                rb = min(n, sum(rows_all[partner:partner + s]))
+                if rb > 0:
+                    if other is None:
+                        other = torch.empty_like(work)
+                    dist.recv(other, src=_global_rank(group, partner), group=group)
+                    cur = merge(work, cur, other, rb)
+        else:
+            # rank % 2s == s: hand the subtree's factor to rank - s and leave the tree
+            if cur > 0:
+                dist.send(work, dst=_global_rank(group, rank - s), group=group)
+            break
+        s *= 2
+    dist.broadcast(work, src=_global_rank(group, 0), group=group)
+    R.copy_(work)
+    return total_rows, total_seen
+
+
+def merge_or_skip(R: torch.Tensor, rows: int, rows_seen: int,
+                  group: Optional[dist.ProcessGroup] = None,
+                  merge: Merge = fold_merge) -> Optional[Tuple[int, int]]:
+    """:func:`rtree_merge`, or None with a warning when a collective of the merge
+    failed (a peer never posted its factor and the process group's timeout ran
+    out, or the peer is gone).  ``R`` is then unchanged, so the caller can keep
+    its running factor and skip the factor update, as the reference does when a
+    refresh cannot be computed (``ifkfac/ifkfac.py:207-223``)."""
+    try:
+        return rtree_merge(R, rows, rows_seen, group, merge)
+    except (RuntimeError, dist.DistError) as e:  # timeouts and lost peers surface as these
+        logger.warning("IFKFAC: R-tree merge failed (%s); factor update skipped", e)
+        return None
 
 
 def merge_running(factor: triangular.RunningFactor,
@@ -121,8 +191,14 @@ class DistributedIFKFAC:
       the merged R_G is scaled by ``delta_scale`` (default 1 / world; pass 1.0
       when each rank's loss is already normalised by the global batch).
     * Layer l's natural gradient and update run on rank ``l mod world`` only (its
-      momentum buffer lives there); the owner then broadcasts the layer's
-      parameters to the other ranks.
+      momentum buffer lives there); each owner then broadcasts the parameters of
+      all its layers to the other ranks in one flat buffer (one broadcast per
+      rank and step, not one per parameter).
+    * If a collective of the refresh fails (a rank never posts its factor and the
+      process group's timeout runs out), the factor update is skipped with a
+      warning and the previous factors stay in use, the reference's handling of a
+      refresh that cannot be computed (``ifkfac/ifkfac.py:207-223``); the running
+      factors are cleared, since some may already hold a merged state.
 
     Construct it on every rank with the same model and arguments; ``step()`` is a
     collective."""
@@ -144,7 +220,8 @@ class DistributedIFKFAC:
     def zero_grad(self, set_to_none: bool = True) -> None:
         self.opt.zero_grad(set_to_none=set_to_none)
 
-    def _merge_factors(self) -> None:
+    def _merge_factors(self) -> bool:
+        """R-tree merge of every factor; False (after a warning) when a collective failed."""
         h = self.opt.hooks
         if h.deferred:
             h._drain_deferred()
@@ -165,12 +242,16 @@ class DistributedIFKFAC:
                 f = table[m]
                 if f is None:
                     f = table[m] = Factor(n, dev, h.precision)
-                rows, total = rtree_merge(f.R, f.rows_R, f.rows_seen, self.group,
-                                          merge=lambda a, ra, b, rb, p=f.prec: fold_merge(a, ra, b, rb, p))
+                got = merge_or_skip(f.R, f.rows_R, f.rows_seen, self.group,
+                                    merge=lambda a, ra, b, rb, p=f.prec: fold_merge(a, ra, b, rb, p))
+                if got is None:
+                    return False
+                rows, total = got
                 f.rows_R, f.rows_seen = rows, total
                 nrows[m] = total
                 if ti == 1 and self.delta_scale != 1.0:
                     f.R.mul_(self.delta_scale)  # R^T R scales with the square of the rows
+        return True
 
     def _average_gradients(self, params) -> None:
         grads = [p.grad for p in params if p.grad is not None]
@@ -199,8 +280,7 @@ class DistributedIFKFAC:
         if self.average_gradients:
             self._average_gradients([p for m in layers for p in m.parameters()])
         if should_refresh(opt._step_count, opt.factor_update_freq):
-            self._merge_factors()
-            opt._update_factors()
+            refresh_or_skip(self._merge_factors, opt._update_factors, opt.hooks.clear)
         todo = []
         for m in layers:
             lr, wd, mom = opt._get_module_hp(m)
@@ -209,9 +289,44 @@ class DistributedIFKFAC:
         nats = opt._batched_natgrads([m for m, _, _, _ in todo])
         for m, lr, wd, mom in todo:
             opt._apply_preconditioner(m, lr, wd, mom, nats.get(m))
-        # the owners' updated parameters go to every rank
-        for m in layers:
-            for p in m.parameters():
-                dist.broadcast(p.data, src=dist.get_global_rank(self.group, self.owner[m])
-                               if self.group is not None else self.owner[m], group=self.group)
+        # the owners' updated parameters go to every rank: one flat buffer per owner
+        for o in range(self.world):
+            params = [p for m in layers if self.owner[m] == o for p in m.parameters()]
+            broadcast_flat(params, _global_rank(self.group, o), o == self.rank, self.group)
         return loss
+
+
+def refresh_or_skip(merge, update, clear) -> bool:
+    """The refresh of :class:`DistributedIFKFAC`: ``merge()`` (the R-tree of every
+    factor, False when a collective failed), then ``update()`` (finalize, finite
+    check, cast).  On a failed merge the update is skipped and ``clear()`` drops the
+    running factors, which may hold a partly merged state; the factors already in
+    use stay (the reference skips a refresh it cannot compute,
+    ``ifkfac/ifkfac.py:207-223``).  Returns whether the factors were updated."""
+    if merge():
+        update()
+        return True
+    clear()
+    return False
+
+
+def broadcast_flat(params: Sequence[torch.Tensor], src: int, is_src: bool,
+                   group: Optional[dist.ProcessGroup] = None) -> None:
+    """Broadcast a list of tensors from global rank ``src`` as one flat buffer per
+    dtype (one collective each instead of one per tensor); the receivers copy their
+    slices back."""
+    by_dtype = {}
+    for p in params:
+        by_dtype.setdefault(p.dtype, []).append(p)
+    for dt, ps in by_dtype.items():
+        if is_src:
+            flat = torch.cat([p.data.reshape(-1) for p in ps])
+        else:
+            flat = torch.empty(sum(p.numel() for p in ps), dtype=dt, device=ps[0].device)
+        dist.broadcast(flat, src=src, group=group)
+        if not is_src:
+            off = 0
+            for p in ps:
+                k = p.numel()
+                p.data.copy_(flat[off:off + k].view_as(p.data))
+                off += k

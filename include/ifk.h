@@ -70,6 +70,12 @@ extern "C" {
 
 /* ---- fold flags ------------------------------------------------------- */
 #define IFK_FOLD_TRAPEZOIDAL_CHUNK 1  /* chunk row i is zero left of column i (an R factor) */
+/* Tests of the failure path only (ifk_tsqr_fold, IFK_PREC_BF16): the first
+ * panel of the fold is never published and the cross-CTA waits give up after
+ * a few milliseconds instead of seconds, so every task that needs that panel
+ * times out; the call then leaves IFK_ERR_TIMEOUT in *d_status, R is not a
+ * valid factor, and the device stays usable for the next call. */
+#define IFK_FOLD_DEBUG_WITHHOLD 256
 
 typedef void* ifk_stream_t;  /* a cudaStream_t */
 
@@ -193,6 +199,28 @@ IFK_API int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* l
                                    const ifk_segment* segs, int chunk_dtype,
                                    const double* ident_tail, int prec, int* d_status,
                                    void* workspace, size_t workspace_bytes, ifk_stream_t stream);
+
+/* ---- R-tree merge --------------------------------------------------------- */
+
+/* Workspace bytes for ifk_rtree_merge of nfactors factors of order n. */
+IFK_API size_t ifk_rtree_merge_workspace(int nfactors, int64_t n);
+
+/*
+ * Merge nfactors running factors held by this process (R[i]: n x n fp32,
+ * leading dimension ldR[i], rows[i] meaningful rows; for instance the local
+ * factors of all data-parallel ranks after a gather) into R[0], in the order
+ * of the reference's tile/tree TSQR (ifkfac/triangular.py:207-220): round by
+ * round, adjacent pairs [R_a; R_b] are merged into R_a (a fold of R_b as a
+ * trapezoidal chunk, positive diagonal) and the odd one out is carried
+ * forward.  The merges of one round share one persistent launch.  prec is
+ * IFK_PREC_FP32 or IFK_PREC_BF16.  *rows_out (host) receives the merged
+ * factor's meaningful rows, min(n, sum of rows).  The other R[i] are left in
+ * intermediate states.  Replaces the merge tree of tsqr (the batched leaf
+ * QRs before it are ifk_tsqr_fold_batched).
+ */
+IFK_API int ifk_rtree_merge(int nfactors, float* const* R, const int64_t* ldR, const int64_t* rows,
+                            int64_t n, int prec, int64_t* rows_out, int* d_status,
+                            void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
 /* ---- damping fold ------------------------------------------------------ */
 

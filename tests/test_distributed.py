@@ -20,7 +20,7 @@ N = 24
 
 def _rows_for(rank):
     # rank 1 holds fewer rows than columns (trapezoid), rank 2 (if any) none
-    return {0: 40, 1: 13, 2: 0, 3: 30}[rank]
+    return {0: 40, 1: 13, 2: 0, 3: 30, 4: 7}[rank]
 
 
 def _data(rank):
@@ -69,7 +69,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 5])
 def test_rtree_merge_gloo_matches_tsqr(tmp_path, world):
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     Rs = [np.load(tmp_path / f"r{r}.npy") for r in range(world)]
@@ -123,3 +123,75 @@ def test_fold_merge_on_device_matches_oracle_tsqr():
     ref = ora.positive_diagonal_R(ora._qr_r(np.concatenate(blocks, 0)))
     err = np.linalg.norm(out.cpu().numpy().astype(np.float64) - ref) / np.linalg.norm(ref)
     assert nrows == n and err < 1e-5, err
+
+
+def _silent_rank_worker(rank, world, port, outdir):
+    """Rank 1 never posts its factor (it does not enter the merge); the others must
+    give up within the process group's timeout and keep their local factor."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=3))
+    done = os.path.join(outdir, "done")
+    if rank == 1:
+        # stay alive, silent, until the others have finished (no collective at all)
+        import time
+        t0 = time.time()
+        while len([f for f in os.listdir(outdir) if f.startswith("res")]) < world - 1 and time.time() - t0 < 60:
+            time.sleep(0.1)
+        open(done, "w").close()
+        os._exit(0)
+    X = _data(rank)
+    R = torch.from_numpy(_local_factor(X))
+    before = R.clone()
+    import time
+    t0 = time.time()
+    got = D.merge_or_skip(R, min(N, X.shape[0]), X.shape[0], merge=_oracle_merge)
+    dt = time.time() - t0
+    np.save(os.path.join(outdir, f"res{rank}.npy"),
+            np.array([got is None, bool(torch.equal(R, before)), dt]))
+    import time as _t
+    t1 = _t.time()
+    while not os.path.exists(done) and _t.time() - t1 < 60:
+        _t.sleep(0.1)
+    os._exit(0)  # the group is broken: leave without a collective teardown
+
+
+def test_rank_that_never_posts_its_factor_times_out_on_the_host(tmp_path):
+    world = 3
+    mp.spawn(_silent_rank_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in (0, 2):
+        skipped, unchanged, secs = np.load(tmp_path / f"res{r}.npy")
+        assert skipped and unchanged, r
+        assert secs < 30, secs  # bounded by the 3 s timeout of each failing collective
+
+
+def test_refresh_is_skipped_when_the_merge_fails():
+    calls = []
+    ok = D.refresh_or_skip(lambda: False, lambda: calls.append("update"), lambda: calls.append("clear"))
+    assert not ok and calls == ["clear"]
+    calls.clear()
+    ok = D.refresh_or_skip(lambda: True, lambda: calls.append("update"), lambda: calls.append("clear"))
+    assert ok and calls == ["update"]
+
+
+def _bcast_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ps = [torch.full((3, 2), float(rank)), torch.full((5,), 10.0 + rank),
+              torch.full((2,), 20 + rank, dtype=torch.int64)]
+        D.broadcast_flat(ps, src=1, is_src=(rank == 1))
+        np.save(os.path.join(outdir, f"b{rank}.npy"),
+                np.concatenate([p.double().reshape(-1).numpy() for p in ps]))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_broadcast_flat_gloo(tmp_path):
+    mp.spawn(_bcast_worker, args=(3, _free_port(), str(tmp_path)), nprocs=3, join=True)
+    want = np.concatenate([np.full(6, 1.0), np.full(5, 11.0), np.full(2, 21.0)])
+    for r in range(3):
+        np.testing.assert_array_equal(np.load(tmp_path / f"b{r}.npy"), want)

@@ -170,13 +170,15 @@ def test_c2_fp32_mode_natgrad():
 
 
 def test_c5_width_factor_n8192():
-    """A factor of config 5's widest order (n = 8192, the down projection's input):
-    4 tiles of 2048 bf16 rows and the damping rows (lambda = 1e-3) in one launch,
-    32 trapezoidal damping sub-tiles, against the fp32 QR of the stacked rows."""
+    """A factor of config 5's widest order (n = 8192, the down projection's input) at
+    config 5's row count: 16 tiles of 2048 bf16 rows and the damping rows (lambda =
+    1e-3) in one launch, 32 trapezoidal damping sub-tiles.  Checked through the
+    size-independent property R^T R = X^T X / p + lambda I (Gram matrix of the same
+    bf16 values, fp32 GEMM on the host)."""
     import torch
     from ifkfac_b200 import _lib
     from ifkfac_b200.engine import Factor, fold_segments
-    n, p, lam = 8192, 8192, 1e-3
+    n, p, lam = 8192, 32768, 1e-3
     rng = np.random.default_rng(8192)
     X = _scaled(rng, p, n)
     dev = torch.device("cuda", 0)
@@ -186,13 +188,15 @@ def test_c5_width_factor_n8192():
                   ident_tail=[math.sqrt(lam * p)])
     torch.cuda.synchronize()
     assert int(f.status.item()) == 0
-    got = f.R.cpu().numpy() / math.sqrt(p)
-    aug = np.concatenate([X / np.float32(math.sqrt(p)), np.float32(math.sqrt(lam)) * np.eye(n, dtype=np.float32)])
-    want = O.positive_diagonal_R(O._qr_r(aug))
-    e = rel(got, want)
-    print(f"n=8192 damped factor: rel err {e:.3e}")
+    R = f.R.cpu() / math.sqrt(p)
+    del x, f
+    Xt = torch.from_numpy(X)
+    A = (Xt.t() @ Xt) / p + lam * torch.eye(n)
+    e = float(torch.linalg.norm(R.t() @ R - A) / torch.linalg.norm(A))
+    print(f"n=8192, p=32768 damped factor: rel err of R^T R {e:.3e}")
     assert e < 1e-2, e
-    assert np.all(np.diagonal(got) > 0)
+    assert bool((torch.diagonal(R) > 0).all())
+    assert bool((torch.tril(R, -1) == 0).all())
 
 
 def test_fold_longer_than_one_launch_piece():
