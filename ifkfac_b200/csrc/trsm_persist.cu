@@ -1,27 +1,40 @@
 // Persistent tensor-core triangular solve, op(A) X = B in place (bf16 A).
 //
-// Right-hand-side columns are independent, so each CTA owns NT = 32 columns of
-// B and solves every block row (NB2 = 128 rows) for them in one launch, with no
-// synchronisation between CTAs.  Block row j (left-looking):
-//   D   = sum_{s solved} op(A)_{j,s} X_s        tcgen05, bf16 operands, fp32 TMEM
-//   Y   = B_j - D                               fp32
-//   X_j = inv(op(A)_{j,j}) Y                    tcgen05, 3-term bf16 split
+// The solve is cut into tasks (j, c): block row j (NB2 = 128 rows, in solve
+// order) of column tile c (NC = 128 right-hand-side columns).  Left-looking:
+//   D    = sum_{s solved before j} op(A)_{j,s} X_{s,c}   tcgen05, bf16 operands, fp32 TMEM
+//   Y    = B_{j,c} - D                                    fp32
+//   X_jc = inv(op(A)_{j,j}) Y                             tcgen05, 3-term bf16 split
+// Columns are independent, so task (j, c) depends only on the tasks (s, c)
+// before it in its column tile.  One CTA per SM takes tasks from a global
+// ticket counter in level order (all tasks of block row 0, then of block row
+// 1, ...), a topological order of the dependencies: a task waits only for
+// tasks with lower tickets, which went to CTAs already running.  A finished
+// task publishes its solved block as a bf16 operand image in global memory and
+// raises a readiness flag; the tasks below it in the column tile bring that
+// image in by bulk copy.  128 columns per task (against 32 per CTA in a
+// column-owning layout) give each copied 32 KB tile of A four times the
+// tensor-core work, and every SM has tasks even when the right-hand side is
+// narrow.
 // Warp roles (192 threads):
-//   warps 0-3  epilogue: TMEM lanes 32w..32w+31 = rows of the block; Y, X_j, writes
-//   warp 4     producer: bulk copies (contiguous 32 KB / 8 KB images) of the
-//              packed op(A)_{j,s} tile, of this CTA's bf16 copy of X_s and of the
-//              inverses
-// Before the solve, pack_tiles_kernel writes every strictly upper 128 x 128
-// block of A once as the shared-memory image of the operand tile it becomes
-// (K-major for op = A, MN-major transposed for op = A^T), so every copy of the
-// K loop is one contiguous bulk transfer.
+//   warps 0-3  epilogue: TMEM lanes 32w..32w+31 = rows of the block; Y, X_jc,
+//              the writes of X (or of the fused momentum / lr update) and of
+//              the bf16 image, the readiness flag
+//   warp 4     producer: takes tickets, waits (bounded) for the flags of the
+//              blocks a task needs, and issues the bulk copies of the packed
+//              op(A)_{j,s} tile and of X_{s,c} (64 KB per stage, two stages),
+//              then of the two inverse tiles inv(op(A)_jj) hi / lo
 //   warp 5     MMA issue
-// A three-stage full/empty mbarrier ring feeds the K loop; D is double-buffered
-// in TMEM so the next block row's products start while this row's epilogue runs.
-// The inverses inv(A_jj) (fp32 column substitution, 3-term bf16 split) are
-// written by diag_inverse_layout_kernel directly in the operand layout.
-// Every wait is bounded: a role that gives up raises the CTA's abort word, the
-// others stop at their next wait, and the launch reports IFK_ERR_TIMEOUT.
+// D is double-buffered in TMEM, so the next task's products start while this
+// task's epilogue runs.  Before the solve, pack_tiles_kernel writes every
+// strictly upper 128 x 128 block of A once as the shared-memory image of the
+// operand tile it becomes (K-major for op = A, MN-major transposed for
+// op = A^T) and clears the readiness flags; diag_inverse_layout_kernel writes
+// the inverses of the diagonal blocks (fp32 column substitution, 3-term bf16
+// split) in the operand layout.
+// Every wait is bounded: a role that gives up raises the launch's abort word,
+// every role of every CTA stops at its next wait, and the launch reports
+// IFK_ERR_TIMEOUT.
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
 #include "tc.cuh"
