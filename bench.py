@@ -185,7 +185,7 @@ def run_step(lc, per_tile, tiles, x, d, g, w):
     for lo, hi in tiles:
         lc.fold(x[lo:hi], d[lo:hi])
     lc.refresh(DAMPING, consume=not per_tile)
-    lc.update(w, lc.natgrad(g), LR, MOM, 0.0, None)
+    lc.natgrad_update(g, w, LR, MOM)
 
 
 def time_components(lc, per_tile, tiles, X, D, gW, W):
@@ -211,6 +211,9 @@ def time_components(lc, per_tile, tiles, X, D, gW, W):
         for lo, hi in tiles:
             lc.fold(X[lo:hi], D[lo:hi])  # kept for the launch below: no device work
         comp["tsqr_fold_ms"] = timed(lambda: lc.refresh(DAMPING, consume=True))
+    # the step's natural gradient + update (one call; the last solve applies the update)
+    comp["trsm_update_ms"] = timed(lambda: lc.natgrad_update(gW, W, LR, MOM))
+    # the two halves as separate calls, for reference
     nat = [None]
 
     def nat_fn():
@@ -387,13 +390,12 @@ def run_ours(args, rank, world, local_rank):
                         lc.flush()
                 lc.refresh(DAMPING, consume=True)
             s0.wait_event(eg)
-            nat = lc.natgrad(gb)
+            if st["wdone"] is not None:
+                s0.wait_event(st["wdone"])  # the previous read-back of W has finished
+            lc.natgrad_update(gb, W, LR, MOM)
             fe = torch.cuda.Event()
             fe.record(s0)
             st["free"][st["k"] % 2] = fe
-            if st["wdone"] is not None:
-                s0.wait_event(st["wdone"])  # the previous read-back of W has finished
-            lc.update(W, nat, LR, MOM, 0.0, None)
             ue = torch.cuda.Event()
             ue.record(s0)
             dh.wait_event(ue)
@@ -465,6 +467,175 @@ def run_ours(args, rank, world, local_rank):
                            "peak_source": f"{pk['source']} bf16 burst"}
     if not args.no_cpu_baseline and world == 1:
         out["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(out), flush=True)
+
+
+def run_sharded(args, rank, world, local_rank):
+    """Config 2 on N GPUs with the path's own partition: the same single-layer operator
+    at every N (strong scaling).  The 16384 rows of X and delta are batch-sharded, p / N
+    per rank; every rank folds its rows into local factors (rank 0 with the damping rows
+    sqrt(lambda p) I as the last segment of the same launch); the local factors are
+    combined by the R-tree of the reference's tsqr (ifkfac/triangular.py:207-220):
+    ceil(log2 N) rounds of pairwise NCCL send / recv, both factors of a round merged in
+    one launch (trapezoidal-chunk folds); the owner of the layer (rank 0) finalises
+    (1 / sqrt(p), bf16 cast), runs the four solves with the fused momentum / lr update
+    and broadcasts W to every rank.  Timing: K eager steps between barriers, CUDA events,
+    max over ranks; the per-stage split is taken on every rank and gathered."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import LayerCurvature, fold_segments, _arr, _ws
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    L = _lib.lib()
+    _lib.check(L.ifk_device_check(), "ifk_device_check")
+    X, D, gW, W = make_inputs(dev, 1234)  # the same operator on every rank
+    rows = P_ROWS // world
+    lo = rank * rows
+    tiles = [(a, min(a + TILE, lo + rows)) for a in range(lo, lo + rows, TILE)]
+    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_BF16, torch.bfloat16, TILE, window=len(tiles))
+    fx, fg = lc.fx, lc.fg
+    other = [torch.empty(N_DIM, N_DIM, device=dev), torch.empty(N_DIM, N_DIM, device=dev)]
+    ws_m = _ws(L.ifk_tsqr_fold_batched_workspace(2, _arr(ctypes.c_int64, [N_DIM, N_DIM]),
+                                                  _arr(ctypes.c_int64, [N_DIM, N_DIM])), dev)
+    stream = lambda: torch.cuda.current_stream().cuda_stream
+    # rows of each rank's local factor (rank 0 holds the damping rows too)
+    local_rows = [min(N_DIM, rows + (N_DIM if r == 0 else 0)) for r in range(world)]
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def merge_into(rb):
+        n2 = _arr(ctypes.c_int64, [N_DIM, N_DIM])
+        _lib.check(L.ifk_tsqr_fold_batched(
+            2, _arr(ctypes.c_void_p, [fx.R.data_ptr(), fg.R.data_ptr()]), n2,
+            _arr(ctypes.c_int64, [fx.rows_R, fg.rows_R]),
+            _arr(ctypes.c_void_p, [other[0].data_ptr(), other[1].data_ptr()]), n2,
+            _arr(ctypes.c_int64, [rb, rb]), n2, _lib.F32, _lib.PREC_BF16, _lib.FOLD_TRAPEZOIDAL_CHUNK,
+            lc.status.data_ptr(), ws_m.data_ptr(), ws_m.numel(), stream()), "ifk_tsqr_fold_batched")
+        fx.rows_R = fg.rows_R = min(N_DIM, fx.rows_R + rb)
+
+    def step(marks=None):
+        mark = (lambda: marks.append(ev()) or marks[-1].record()) if marks is not None else (lambda: None)
+        mark()
+        lc.clear()
+        segs = ([X[a:b] for a, b in tiles], [D[a:b] for a, b in tiles])
+        tails = [math.sqrt(DAMPING * P_ROWS)] * 2 if rank == 0 else None
+        lc.ws_pair = fold_segments((fx, fg), segs, lc.ws_pair, ident_tail=tails)
+        fx.consumed = fg.consumed = False  # merged below, then finalised; cleared next step
+        mark()
+        s = 1
+        while s < world:
+            if rank % (2 * s) == 0:
+                partner = rank + s
+                if partner < world:
+                    rb = min(N_DIM, sum(local_rows[partner:partner + s]))
+                    for w in dist.batch_isend_irecv([dist.P2POp(dist.irecv, other[0], partner),
+                                                     dist.P2POp(dist.irecv, other[1], partner)]):
+                        w.wait()
+                    merge_into(rb)
+            else:
+                for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, fx.R, rank - s),
+                                                 dist.P2POp(dist.isend, fg.R, rank - s)]):
+                    w.wait()
+                break
+            s *= 2
+        mark()
+        if rank == 0:
+            _lib.check(L.ifk_finalize_batched(
+                2, _arr(ctypes.c_void_p, [fx.R.data_ptr(), fg.R.data_ptr()]), _arr(ctypes.c_int64, [N_DIM] * 2),
+                _arr(ctypes.c_int64, [fx.rows_R, fg.rows_R]), _arr(ctypes.c_int64, [N_DIM] * 2),
+                _arr(ctypes.c_double, [float(P_ROWS)] * 2), 0.0,
+                _arr(ctypes.c_void_p, [lc.RX.data_ptr(), lc.RG.data_ptr()]), _arr(ctypes.c_int64, [N_DIM] * 2),
+                _lib.BF16, _lib.PREC_BF16, lc.status.data_ptr(), lc.ws_fin.data_ptr(), lc.ws_fin.numel(),
+                stream()), "ifk_finalize_batched")
+            lc.natgrad_update(gW, W, LR, MOM)
+        mark()
+        dist.broadcast(W, src=0)
+        mark()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # per-stage split of one step on every rank (eager, events on the launching stream)
+    marks = []
+    dist.barrier()
+    step(marks)
+    torch.cuda.synchronize()
+    names = ["local_fold", "rtree_merge", "finalize_solve_update", "broadcast_W"]
+    mine = torch.tensor([marks[i].elapsed_time(marks[i + 1]) for i in range(len(names))], device=dev)
+    allst = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allst, mine)
+    # timed region
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    with ClockSampler(local_rank) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        e1.synchronize()
+    dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end: each rank's rows (and rank 0's grad_W) from pinned host memory every
+    # step, W read back to the host by rank 0
+    hX = X[lo:lo + rows].cpu().pin_memory()
+    hD = D[lo:lo + rows].cpu().pin_memory()
+    hG = gW.cpu().pin_memory()
+    hW = torch.empty_like(W, device="cpu").pin_memory()
+
+    def e2e_step():
+        X[lo:lo + rows].copy_(hX, non_blocking=True)
+        D[lo:lo + rows].copy_(hD, non_blocking=True)
+        if rank == 0:
+            gW.copy_(hG, non_blocking=True)
+        step()
+        if rank == 0:
+            hW.copy_(W, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    k2 = max(2, min(args.steps, 10))
+    a, b = ev(), ev()
+    a.record()
+    for _ in range(k2):
+        e2e_step()
+    b.record()
+    b.synchronize()
+    e2e_ms = a.elapsed_time(b) / k2
+    t = torch.tensor([e2e_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    if rank != 0:
+        return
+    flops = algorithmic_flops()
+    pk = peaks()
+    stages = {nm: [float(x[i]) for x in allst] for i, nm in enumerate(names)}
+    out = {
+        "metric": METRIC, "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "n": N_DIM, "p": P_ROWS, "tile_rows": TILE, "damping": DAMPING,
+                   "lr": LR, "momentum": MOM, "use_true_bf16": True,
+                   "parallelism": (f"rows batch-sharded over {world} GPUs ({rows} each), R-tree over NCCL "
+                                   "send/recv, solves + update on the layer's owner, W broadcast"),
+                   "l2": "inputs larger than L2 (X + delta bf16 = 268 MB read per step)", "cuda_graph": False},
+        "tflops": flops["total"] / (ms * 1e-3) / 1e12,
+        "tflops_frac_of_measured_bf16": flops["total"] / (ms * 1e-3) / 1e12 / pk["bf16"],
+        "stages_ms_per_rank": stages,
+        "clocks": clk.summary(),
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s",
+                "h2d_bytes_per_step": X.numel() * 2 + D.numel() * 2 + gW.numel() * 4,
+                "d2h_bytes_per_step": W.numel() * 4, "ms_per_step": e2e_ms,
+                "note": "each rank copies its rows of X and delta (rank 0 also grad_W) from pinned host memory "
+                        "every step; rank 0 reads W back"},
+    }
     print(json.dumps(out), flush=True)
 
 
@@ -1124,6 +1295,10 @@ def main():
     ap.add_argument("--e2e-groups", default="1",
                     help="one-launch schedule, e2e: fold launches the row tiles are split into: a count of "
                          "equal groups, or comma-separated tile counts of consecutive groups (e.g. 1,7)")
+    ap.add_argument("--partition", choices=["rows", "layers"], default="rows",
+                    help="N > 1, config 2: 'rows' (default) solves the same operator on N GPUs, rows "
+                         "batch-sharded and merged by the R-tree; 'layers' gives every rank a layer of its own "
+                         "(independent operators, no collective)")
     ap.add_argument("--no-other-schedule", action="store_true",
                     help="skip the secondary timing of the other schedule")
     ap.add_argument("--profile", action="store_true",
@@ -1152,7 +1327,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if world > 1 and args.partition == "rows":
+            run_sharded(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch

@@ -50,6 +50,9 @@ SIGNATURES = {
     "ifk_natgrad_workspace": (_sz, [_i64, _i64]),
     "ifk_natgrad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
                            _vp, _sz, _vp]),
+    "ifk_natgrad_update_workspace": (_sz, [_i64, _i64]),
+    "ifk_natgrad_update": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp, _i64, _i64, _dbl, _dbl, _dbl,
+                                  _int, _int, _vp, _vp, _sz, _vp]),
     "ifk_posterior_sample_workspace": (_sz, [_i64, _i64]),
     "ifk_posterior_sample": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _int, _vp,
                                     _vp, _sz, _vp]),

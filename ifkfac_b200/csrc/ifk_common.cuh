@@ -71,6 +71,24 @@ __device__ __forceinline__ void st4(float* p, float4 v, int valid) {
   if (valid > 2) p[2] = v.z;
 }
 
+// One element of the momentum / lr update on fp32 master weights
+// (ifkfac/ifkfac.py:394-413; a clip factor, when any, is already applied to g):
+//   buf = mom * buf + g (buf read as zero when buf_new), g = buf;  W *= decay;  W -= lr * g.
+struct UpdCoef {
+  float lr, mom, decay;
+  int use_mom, use_decay, buf_new;
+};
+// The rounding steps are spelled out (fused multiply-adds, no compiler
+// contraction), so every kernel that applies the update gives the same bits.
+__device__ __forceinline__ float upd_elem(float w, float& b, float g, const UpdCoef& p) {
+  if (p.use_mom) {
+    b = __fmaf_rn(p.buf_new ? 0.f : b, p.mom, g);
+    g = b;
+  }
+  if (p.use_decay) w = __fmul_rn(w, p.decay);
+  return __fmaf_rn(-p.lr, g, w);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

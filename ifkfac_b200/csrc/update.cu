@@ -35,14 +35,15 @@ struct UpdParams {
 };
 
 __device__ __forceinline__ float upd_one(float w, float* bufp, float g, const UpdParams& p, float gs) {
-  g *= gs;
-  if (p.use_mom) {
-    const float b = (p.buf_new ? 0.f : *bufp) * p.mom + g;
-    *bufp = b;
-    g = b;
-  }
-  if (p.use_decay) w = w * p.decay;
-  return w - p.lr * g;
+  // the element arithmetic is shared with the fused epilogue of the last solve
+  UpdCoef c;
+  c.lr = p.lr;
+  c.mom = p.mom;
+  c.decay = p.decay;
+  c.use_mom = p.use_mom;
+  c.use_decay = p.use_decay;
+  c.buf_new = p.buf_new;
+  return upd_elem(w, *bufp, __fmul_rn(g, gs), c);
 }
 
 __global__ void update_kernel(float* W, float* buf, const float* nat, int64_t count, UpdParams p,

@@ -345,6 +345,33 @@ class LayerCurvature:
             _stream()), "ifk_natgrad")
         return self.nat
 
+    def natgrad_update(self, grad_W: torch.Tensor, W: torch.Tensor, lr: float, momentum: float,
+                       weight_decay: float = 0.0) -> None:
+        """The natural gradient and the update without clipping in one library call
+        (ifk_natgrad_update).  Same result as :meth:`natgrad` followed by
+        :meth:`update` with grad_clip None."""
+        if grad_W.dtype != torch.float32 or grad_W.stride(1) != 1:
+            grad_W = grad_W.float().contiguous()
+        if not (W.is_contiguous() and W.dtype == torch.float32 and W.shape == (self.n_out, self.n_in)):
+            raise ValueError("W must be a contiguous n_out x n_in float32 tensor")
+        L = _lib.lib()
+        p = self.prec
+        if p == _lib.PREC_AUTO:
+            p = _lib.PREC_BF16 if self.factor_dtype == torch.bfloat16 else _lib.PREC_FP32
+        new_buf = False
+        if momentum > 0 and self.buf is None:
+            self.buf = torch.empty(self.n_out, self.n_in, dtype=torch.float32, device=self.device)
+            new_buf = True
+        need = L.ifk_natgrad_update_workspace(self.n_out, self.n_in)
+        if getattr(self, "ws_ngu", None) is None or self.ws_ngu.numel() < need:
+            self.ws_ngu = _ws(need, self.device)
+        check(L.ifk_natgrad_update(
+            grad_W.data_ptr(), grad_W.stride(0), self.RX.data_ptr(), self.n_in, self.RG.data_ptr(), self.n_out,
+            _DT[self.factor_dtype], W.data_ptr(), self.buf.data_ptr() if momentum > 0 else None, self.n_out,
+            self.n_in, float(lr), float(momentum), float(weight_decay), 1 if new_buf else 0, p,
+            self.status.data_ptr(), self.ws_ngu.data_ptr(), self.ws_ngu.numel(), _stream()),
+            "ifk_natgrad_update")
+
     def update(self, W: torch.Tensor, nat: torch.Tensor, lr: float, momentum: float,
                weight_decay: float, grad_clip: Optional[float]) -> None:
         """Epilogue of ifkfac/ifkfac.py:394-413 on fp32 master weights, in place."""

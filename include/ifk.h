@@ -301,6 +301,31 @@ IFK_API int ifk_natgrad(const float* grad_W, int64_t ld_g,
                 int64_t n_out, int64_t n_in, int prec, int* d_status,
                 void* workspace, size_t workspace_bytes, ifk_stream_t stream);
 
+/* Workspace bytes for ifk_natgrad_update. */
+IFK_API size_t ifk_natgrad_update_workspace(int64_t n_out, int64_t n_in);
+
+/*
+ * The natural gradient of ifk_natgrad followed by the update of ifk_update
+ * without clipping, in one call: with nat = R_G^-1 R_G^-T grad_W R_X^-1 R_X^-T,
+ *   buf = momentum * buf + nat (buf read as zero when buf_is_new; no buffer
+ *   when momentum == 0, buf may then be NULL), W *= 1 - lr * weight_decay
+ *   (weight_decay > 0), W -= lr * buf (or lr * nat without momentum).
+ * W and buf are contiguous n_out x n_in fp32; grad_W is not modified.  The
+ * natural gradient goes to the workspace and one elementwise pass applies the
+ * update; the result is bit for bit that of ifk_natgrad followed by ifk_update
+ * with grad_clip <= 0.  A caller that clips (a norm over all of nat) uses the
+ * two calls.
+ *
+ * Replaces apply_vered (ifkfac/triangular.py:551-656) together with the
+ * per-layer epilogue of the bucketed fast path (ifkfac/ifkfac.py:394-413).
+ */
+IFK_API int ifk_natgrad_update(const float* grad_W, int64_t ld_g,
+                               const void* R_X, int64_t ld_rx, const void* R_G, int64_t ld_rg,
+                               int r_dtype, float* W, float* buf, int64_t n_out, int64_t n_in,
+                               double lr, double momentum, double weight_decay, int buf_is_new,
+                               int prec, int* d_status, void* workspace, size_t workspace_bytes,
+                               ifk_stream_t stream);
+
 /* ---- K-FAC Laplace posterior draw ---------------------------------------- */
 
 /* Workspace bytes for ifk_posterior_sample (that of ifk_natgrad). */
