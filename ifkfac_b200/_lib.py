@@ -71,11 +71,20 @@ SIGNATURES = {
 PER_SEGMENT_DTYPE = -1  # chunk_dtype of ifk_tsqr_fold_segments: each segment's own
 
 
+class Conv2d(ctypes.Structure):
+    """``ifk_conv2d`` of include/ifk.h: im2col geometry of an NCHW image segment."""
+    _fields_ = [("batch", ctypes.c_int64), ("channels", ctypes.c_int64), ("height", ctypes.c_int64),
+                ("width", ctypes.c_int64), ("kernel_h", ctypes.c_int32), ("kernel_w", ctypes.c_int32),
+                ("stride_h", ctypes.c_int32), ("stride_w", ctypes.c_int32), ("pad_h", ctypes.c_int32),
+                ("pad_w", ctypes.c_int32), ("dilation_h", ctypes.c_int32), ("dilation_w", ctypes.c_int32)]
+
+
 class Segment(ctypes.Structure):
     """``ifk_segment`` of include/ifk.h: rows of a chunk for ifk_tsqr_fold_segments."""
     _fields_ = [("chunk", ctypes.c_void_p), ("ld", ctypes.c_int64), ("rows", ctypes.c_int64),
                 ("row_index", ctypes.c_void_p), ("src_rows", ctypes.c_int64), ("cols", ctypes.c_int64),
-                ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("conv", ctypes.POINTER(Conv2d))]
 
 
 class IFKError(RuntimeError):

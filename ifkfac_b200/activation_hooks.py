@@ -54,15 +54,20 @@ def prepare_x(x: torch.Tensor, module: nn.Module, max_conv_rows: int, max_seq_ro
               augment_bias: bool, transform=None):
     """Activation rows of one forward call (ifkfac/activation_hooks.py:519-548).
 
-    The rows are returned as :class:`Rows`: the 3-D reshape is a view, and the
-    random row subsample and the bias column are read in place by the fold
-    kernels instead of being copied.  With a chunk transform the rows are
+    The rows are returned as :class:`Rows`: the 3-D reshape is a view; the
+    random row subsample, the bias column and a Conv2d input's im2col rows are
+    read in place by the fold kernels instead of being copied.  With a chunk transform the rows are
     materialised and the transform's output (a tensor) is returned."""
     idx = None
     if isinstance(module, nn.Conv2d):
-        x = unfold_conv_input(x, module)
-        if max_conv_rows > 0 and x.shape[0] > max_conv_rows:
-            idx = torch.randperm(x.shape[0], device=x.device)[:max_conv_rows]
+        # im2col rows read in place by the fold (no F.unfold copy); the same rows and
+        # the same random subsample as the reference's unfold + randperm
+        rows = Rows.conv2d(x, module)
+        if max_conv_rows > 0 and rows.rows > max_conv_rows:
+            rows = Rows.conv2d(x, module, torch.randperm(rows.rows, device=x.device)[:max_conv_rows])
+        if transform is not None:
+            return transform(rows.materialize())
+        return rows
     elif x.ndim > 2:
         x = x.reshape(-1, x.shape[-1])
         if max_seq_rows > 0 and x.shape[0] > max_seq_rows:

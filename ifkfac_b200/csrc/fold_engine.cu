@@ -24,6 +24,8 @@
 // fp32 master, publishes their Y / T images and R diagonal blocks, applies the
 // first to the second half of the block, and marks itself done.  X is read
 // from the caller's chunk once; there is no working copy in global memory.
+#include <cstring>
+
 #include "ifk_common.cuh"
 #include "ifk_internal.h"
 #include "panel.cuh"
@@ -100,7 +102,9 @@ constexpr uint32_t A2_MN = 128, A2_K = (WB / 8) * 128;  // 128, 2048
 constexpr uint32_t B2_MN = 128, B2_K = (NB / 8) * 128;  // 128, 1024
 constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
 
-enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2 };
+// Element kinds of a segment: fp32 / bf16 rows, the identity, or an NCHW image read
+// through im2col (XK_CONV + 2 * geometry slot + (bf16 ? 1 : 0)).
+enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2, XK_CONV = 8 };
 
 #ifdef IFK_TRACE
 // Diagnostic build only: per-task timestamps (globaltimer, ns), 24 int64 per task.
@@ -152,7 +156,7 @@ __device__ unsigned long long g_apply_phase[16];
 // fold before it.
 struct PSeg {
   const void* X;
-  int64_t ldX;
+  int64_t ldX;          // im2col segments: the first image row (X is an NCHW image)
   int64_t rows, row_off;
   const int64_t* ridx;  // row i of the segment is row ridx[i] of X (null: row i)
   int64_t src_rows;     // rows of X (bound for ridx)
@@ -186,6 +190,7 @@ struct PFBatch {
   int* status;  // caller's status word (may be null)
   uint32_t wait_limit;  // polls of a cross-CTA wait before it gives up
   int withhold;         // test only: the first panel of fold 0 is never published
+  ConvGeo conv[PFOLD_MAX_CONV];  // geometry of the im2col segments
   int wave_off[MAXW + 1];
 };
 static_assert(sizeof(PFBatch) <= 32000, "launch parameters of one persistent fold launch (limit 32764 bytes)");
@@ -309,13 +314,14 @@ struct FoldLeafHook {
 // row ridx[gi] of X; an index outside X gives a zero row and IFK_ERR_ARG.
 // Columns past X's own (cols) read 1 (the bias column) then 0.
 __device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj, int valid, float (&v)[32],
-                                           int* status) {
+                                           int* status, const ConvGeo* conv) {
   if (F.xkind == XK_IDENT) {
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = (e < valid && gi == gj + e) ? F.ident : 0.f;
     return;
   }
-  int64_t si = gi;
+  // an im2col segment without row indices starts at image row ldX (its launch piece)
+  int64_t si = F.xkind >= XK_CONV ? gi + F.ldX : gi;
   if (F.ridx) {
     si = F.ridx[gi];
     if (si < 0 || si >= F.src_rows) {
@@ -327,7 +333,21 @@ __device__ __forceinline__ void load_row32(const PSeg& F, int64_t gi, int64_t gj
   }
   const int64_t vm64 = F.cols - gj;  // columns of this group held by X
   const int vm = vm64 < valid ? (vm64 > 0 ? (int)vm64 : 0) : valid;
-  if (F.xkind == XK_BF16) {
+  if (F.xkind >= XK_CONV) {
+    // im2col row si of the NCHW image: gathered element by element (zero padding)
+    const ConvGeo& g = conv[(F.xkind - XK_CONV) >> 1];
+    const bool bf = ((F.xkind - XK_CONV) & 1) != 0;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      float x = 0.f;
+      if (e < vm) {
+        const int64_t off = conv_offset(g, si, gj + e);
+        if (off >= 0)
+          x = bf ? __bfloat162float(((const __nv_bfloat16*)F.X)[off]) : ((const float*)F.X)[off];
+      }
+      v[e] = x;
+    }
+  } else if (F.xkind == XK_BF16) {
     const __nv_bfloat16* p = (const __nv_bfloat16*)F.X + si * F.ldX + gj;
     const bool vec = vm >= 32 && ((((uintptr_t)p) & 15) == 0);
     if (vec) {
@@ -690,7 +710,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     for (int q = 0; q < WB / 32; ++q) {
       float v[32];
       if (r < h) {
-        load_row32(G, row0 + r, cs + q * 32, wc - q * 32, v, b.status);
+        load_row32(G, row0 + r, cs + q * 32, wc - q * 32, v, b.status, b.conv);
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0.f;
@@ -1064,7 +1084,8 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s,
   b.ctr = (int*)ws;
   b.abort_ = (int*)ws + 1;
   char* w = (char*)ws + 256;
-  int tmax = 0, cbmax = 1, nsegs_total = 0;
+  int tmax = 0, cbmax = 1, nsegs_total = 0, nconv = 0;
+  const ConvGeo* convsrc[PFOLD_MAX_CONV] = {};
   for (int q = 0; q < nf; ++q) {  // flags first, so one memset clears them all
     const PFoldDesc& D = d[q];
     const int64_t T = pfold_subtiles(D);
@@ -1098,6 +1119,18 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s,
       P.cols = E.cols < 0 ? D.n : E.cols;
       P.t0 = t0;
       P.xkind = E.xkind;
+      if (E.conv) {  // an im2col segment: its geometry goes to the launch's table
+        int slot = -1;
+        for (int q2 = 0; q2 < nconv; ++q2)
+          if (memcmp(convsrc[q2], E.conv, sizeof(ConvGeo)) == 0) slot = q2;
+        if (slot < 0) {
+          if (nconv == PFOLD_MAX_CONV) return IFK_ERR_SHAPE;  // callers split
+          slot = nconv;
+          convsrc[nconv] = E.conv;
+          b.conv[nconv++] = *E.conv;
+        }
+        P.xkind = XK_CONV + 2 * slot + (E.xkind == XK_BF16 ? 1 : 0);
+      }
       P.tri = E.tri;
       P.ident = E.ident;
       t0 += (int)cdiv(E.rows, SUB);

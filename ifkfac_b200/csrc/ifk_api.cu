@@ -2,6 +2,7 @@
 // Host-side validation happens before anything is queued on the stream.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 #include "ifk_common.cuh"
@@ -62,6 +63,7 @@ int plan_pieces(const PFoldDesc& D, const PFoldSeg* segs, int nseg, std::vector<
       PFoldSeg piece = E;
       piece.rows = take;
       if (E.ridx) piece.ridx = E.ridx + off;  // gathered rows: the index array advances
+      else if (E.conv) piece.ldX = E.ldX + off;  // im2col rows: the first image row advances
       else if (E.xkind != 2) piece.X = (const char*)E.X + off * E.ldX * elem_bytes(E.xkind);
       cur.seg[cur.nseg++] = piece;
       cur_sub += take_sub;
@@ -94,14 +96,35 @@ int run_persistent(int nf, const PFoldDesc* in, void* ws, int* status, cudaStrea
     for (size_t i = 0; i < most; ++i) {
       std::vector<PFoldDesc> d;
       int nseg = 0;
+      std::vector<ConvGeo> geos;  // distinct im2col geometries of the launch being built
+      auto new_geos = [&](const PFoldDesc& P) {
+        int add = 0;
+        for (int g = 0; g < P.nseg; ++g) {
+          if (!P.seg[g].conv) continue;
+          bool seen = false;
+          for (const ConvGeo& c : geos) seen = seen || memcmp(&c, P.seg[g].conv, sizeof(ConvGeo)) == 0;
+          for (int h = 0; h < g && !seen; ++h)
+            seen = P.seg[h].conv && memcmp(P.seg[h].conv, P.seg[g].conv, sizeof(ConvGeo)) == 0;
+          add += seen ? 0 : 1;
+        }
+        return add;
+      };
       for (int q = 0; q < cnt; ++q) {
         if (i >= pieces[q].size()) continue;
         const PFoldDesc& P = pieces[q][i];
-        if (!d.empty() && nseg + P.nseg > PFOLD_MAX_BATCH_SEGS) {
+        if (!d.empty() && (nseg + P.nseg > PFOLD_MAX_BATCH_SEGS ||
+                           (int)geos.size() + new_geos(P) > PFOLD_MAX_CONV)) {
           const int rc = pfold_run((int)d.size(), d.data(), ws, status, s, debug);
           if (rc != IFK_OK) return rc;
           d.clear();
+          geos.clear();
           nseg = 0;
+        }
+        for (int g = 0; g < P.nseg; ++g) {
+          if (!P.seg[g].conv) continue;
+          bool seen = false;
+          for (const ConvGeo& c : geos) seen = seen || memcmp(&c, P.seg[g].conv, sizeof(ConvGeo)) == 0;
+          if (!seen) geos.push_back(*P.seg[g].conv);
         }
         d.push_back(P);
         nseg += P.nseg;
@@ -263,7 +286,7 @@ int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ldR, const
 static int fold_fp32(float* R, int64_t ldR, int64_t rows_R, const void* chunk, int64_t ld_chunk,
                      int64_t rows, int64_t n, int chunk_dtype, int tri, float ident, int prec,
                      int* d_status, void* workspace, cudaStream_t s, const int64_t* ridx = nullptr,
-                     int64_t src_rows = 0, int64_t cols = -1) {
+                     int64_t src_rows = 0, int64_t cols = -1, const ConvGeo* conv = nullptr) {
   FoldArgs a;
   a.R = R;
   a.ldR = ldR;
@@ -278,10 +301,37 @@ static int fold_fp32(float* R, int64_t ldR, int64_t rows_R, const void* chunk, i
   a.tri = tri;
   a.err = d_status;
   const int rc = chunk ? copy_chunk(a.X, a.ldX, chunk, ld_chunk, rows, n, chunk_dtype, s, ridx, src_rows, cols,
-                                    d_status)
+                                    d_status, conv)
                        : fill_scaled_identity(a.X, a.ldX, n, ident, s);
   if (rc != IFK_OK) return rc;
   return fold_run(a, prec, s);
+}
+
+// im2col geometry of a segment (checked), or false when it is not a valid one
+static bool conv_geo(const ifk_segment& E, ConvGeo* g) {
+  const ifk_conv2d* c = E.conv;
+  if (c->batch <= 0 || c->channels <= 0 || c->height <= 0 || c->width <= 0 || c->kernel_h <= 0 ||
+      c->kernel_w <= 0 || c->stride_h <= 0 || c->stride_w <= 0 || c->pad_h < 0 || c->pad_w < 0 ||
+      c->dilation_h <= 0 || c->dilation_w <= 0)
+    return false;
+  const int64_t ho = (c->height + 2 * c->pad_h - c->dilation_h * (c->kernel_h - 1) - 1) / c->stride_h + 1;
+  const int64_t wo = (c->width + 2 * c->pad_w - c->dilation_w * (c->kernel_w - 1) - 1) / c->stride_w + 1;
+  if (ho <= 0 || wo <= 0 || ho > (1 << 30) || wo > (1 << 30)) return false;
+  g->B = c->batch;
+  g->C = c->channels;
+  g->H = c->height;
+  g->W = c->width;
+  g->kh = c->kernel_h;
+  g->kw = c->kernel_w;
+  g->sh = c->stride_h;
+  g->sw = c->stride_w;
+  g->ph = c->pad_h;
+  g->pw = c->pad_w;
+  g->dh = c->dilation_h;
+  g->dw = c->dilation_w;
+  g->Ho = (int)ho;
+  g->Wo = (int)wo;
+  return true;
 }
 
 static int64_t seg_base(int f, const int* nseg) {
@@ -332,8 +382,16 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
       if (E.rows == 0) continue;
       if (!E.chunk) return IFK_ERR_ARG;
       if (E.cols != n[f] && E.cols != n[f] - 1) return IFK_ERR_SHAPE;
-      if (E.cols < 1 || E.ld < E.cols) return IFK_ERR_SHAPE;
-      if (E.row_index && E.src_rows <= 0) return IFK_ERR_SHAPE;
+      if (E.conv) {
+        // an NCHW image read through im2col: C kh kw columns, B Ho Wo image rows
+        ConvGeo g;
+        if (!conv_geo(E, &g)) return IFK_ERR_SHAPE;
+        if (E.cols != g.C * g.kh * g.kw || E.src_rows != g.B * g.Ho * g.Wo) return IFK_ERR_SHAPE;
+        if (!E.row_index && E.rows > E.src_rows) return IFK_ERR_SHAPE;
+      } else {
+        if (E.cols < 1 || E.ld < E.cols) return IFK_ERR_SHAPE;
+        if (E.row_index && E.src_rows <= 0) return IFK_ERR_SHAPE;
+      }
       if (per_seg && !dtype_ok(E.dtype)) return IFK_ERR_DTYPE;
       any = true;
     }
@@ -345,6 +403,12 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
     return IFK_ERR_WORKSPACE;
   if (prec == IFK_PREC_AUTO) prec = chunk_dtype == IFK_BF16 ? IFK_PREC_BF16 : IFK_PREC_FP32;
   cudaStream_t s = S(stream);
+  // im2col geometries, one per segment that has one (stable storage for the launcher)
+  int64_t nsegs = 0;
+  for (int f = 0; f < nfolds; ++f) nsegs += nseg[f];
+  std::vector<ConvGeo> geo((size_t)nsegs);
+  for (int64_t i = 0; i < nsegs; ++i)
+    if (segs[i].conv && segs[i].rows > 0) conv_geo(segs[i], &geo[(size_t)i]);
   if (prec == IFK_PREC_BF16) {
     std::vector<PFoldDesc> d((size_t)nfolds);
     std::vector<std::vector<PFoldSeg>> sg((size_t)nfolds);
@@ -358,7 +422,7 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
         if (E.rows <= 0) continue;
         PFoldSeg P;
         P.X = E.chunk;
-        P.ldX = E.ld;
+        P.ldX = E.conv ? 0 : E.ld;  // im2col segments: the first image row
         P.rows = E.rows;
         P.xkind = (per_seg ? E.dtype : chunk_dtype) == IFK_BF16 ? 1 : 0;
         P.ident = 0.f;
@@ -366,6 +430,7 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
         P.ridx = E.row_index;
         P.src_rows = E.src_rows;
         P.cols = E.cols;
+        P.conv = E.conv ? &geo[(size_t)(base + g)] : nullptr;
         sg[f].push_back(P);
       }
       if (ident_tail && ident_tail[f] > 0) {
@@ -392,7 +457,8 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
       const ifk_segment& E = segs[base + g];
       if (E.rows == 0) continue;
       const int rc = fold_fp32(R[f], ldR[f], rr, E.chunk, E.ld, E.rows, n[f], per_seg ? E.dtype : chunk_dtype, 0, 0.f,
-                               prec, d_status, workspace, s, E.row_index, E.src_rows, E.cols);
+                               prec, d_status, workspace, s, E.row_index, E.src_rows, E.cols,
+                               E.conv ? &geo[(size_t)(base + g)] : nullptr);
       if (rc != IFK_OK) return rc;
       rr = std::min<int64_t>(n[f], rr + E.rows);
     }

@@ -45,6 +45,28 @@ constexpr int MAX_SEGS = 12;
 // segments between them (the launch parameters hold both tables).
 constexpr int PFOLD_MAX_FOLDS = 64;
 constexpr int PFOLD_MAX_BATCH_SEGS = 256;
+constexpr int PFOLD_MAX_CONV = 8;  // im2col segments per launch (their geometry is in the launch parameters)
+// im2col geometry of a contiguous N x C x H x W tensor (the rows of F.unfold,
+// transposed): row b * Ho * Wo + oh * Wo + ow, column (c * kh + ki) * kw + kj holds
+// x[b, c, oh * sh - ph + ki * dh, ow * sw - pw + kj * dw], zero outside the image.
+struct ConvGeo {
+  int64_t B, C, H, W;
+  int kh, kw, sh, sw, ph, pw, dh, dw, Ho, Wo;
+};
+// Value of im2col row si, column col (si < B * Ho * Wo, col < C * kh * kw): its
+// offset in x, or -1 for the zero padding.
+__host__ __device__ inline int64_t conv_offset(const ConvGeo& g, int64_t si, int64_t col) {
+  const int64_t L = (int64_t)g.Ho * g.Wo;
+  const int64_t b = si / L, l = si - b * L;
+  const int oh = (int)(l / g.Wo), ow = (int)(l - (int64_t)oh * g.Wo);
+  const int kk = g.kh * g.kw;
+  const int64_t c = col / kk;
+  const int rr = (int)(col - c * kk), ki = rr / g.kw, kj = rr - ki * g.kw;
+  const int y = oh * g.sh - g.ph + ki * g.dh, x = ow * g.sw - g.pw + kj * g.dw;
+  if (y < 0 || y >= g.H || x < 0 || x >= g.W) return -1;
+  return ((b * g.C + c) * g.H + y) * g.W + x;
+}
+
 struct PFoldSeg {
   const void* X;
   int64_t ldX;
@@ -55,6 +77,7 @@ struct PFoldSeg {
   const int64_t* ridx = nullptr;  // device row indices into X (rows of them), or null: rows 0 .. rows-1
   int64_t src_rows = 0;           // rows of X (bound for ridx)
   int64_t cols = -1;              // columns of X read (n, or n - 1 with a column of ones after them); < 0: n
+  const ConvGeo* conv = nullptr;  // X is an NCHW image read through im2col (host pointer; src_rows = B Ho Wo)
 };
 struct PFoldDesc {
   float* R;
@@ -98,7 +121,7 @@ int pfold_run(int nf, const PFoldDesc* d, void* ws, int* status, cudaStream_t s,
 // with cols = n - 1, column n - 1 is ones.
 int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows,
                int64_t n, int dtype, cudaStream_t s, const int64_t* ridx = nullptr, int64_t src_rows = 0,
-               int64_t cols = -1, int* status = nullptr);
+               int64_t cols = -1, int* status = nullptr, const ConvGeo* conv = nullptr);
 // X = sqrt(damping) I (n x n)
 int fill_scaled_identity(float* X, int64_t ldX, int64_t n, float v, cudaStream_t s);
 // Rout = upper(Rin) * scale (n x n fp32)

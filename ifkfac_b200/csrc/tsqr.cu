@@ -257,6 +257,32 @@ __global__ void copy_chunk_kernel(float* X, int64_t ldX, const Tin* src, int64_t
   }
 }
 
+// im2col rows of an NCHW image (ConvGeo), optionally gathered by ridx
+template <typename Tin>
+__global__ void copy_conv_kernel(float* X, int64_t ldX, const Tin* src, ConvGeo g, int64_t rows, int64_t n,
+                                 const int64_t* ridx, int64_t src_rows, int64_t cols, int* status) {
+  const int64_t total = rows * n;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / n, j = idx % n;
+    int64_t si = i;
+    if (ridx) {
+      si = ridx[i];
+      if (si < 0 || si >= src_rows) {
+        if (status && j == 0) atomicExch(status, IFK_ERR_ARG);
+        X[i * ldX + j] = 0.f;
+        continue;
+      }
+    }
+    float v = 1.f;
+    if (j < cols) {
+      const int64_t off = conv_offset(g, si, j);
+      v = off >= 0 ? ld_elem(src, off) : 0.f;
+    }
+    X[i * ldX + j] = v;
+  }
+}
+
 __global__ void fill_identity_kernel(float* X, int64_t ldX, int64_t n, float v) {
   const int64_t total = n * n;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -326,9 +352,20 @@ size_t xw_bytes(int64_t rows, int64_t n) { return (size_t)rows * xw_ld(n) * size
 size_t fold_tbuf_bytes(int64_t rows) { return (size_t)cdiv(rows, SUB) * NB * NB * sizeof(float); }
 
 int copy_chunk(float* X, int64_t ldX, const void* chunk, int64_t ld_chunk, int64_t rows, int64_t n,
-               int dtype, cudaStream_t s, const int64_t* ridx, int64_t src_rows, int64_t cols, int* status) {
+               int dtype, cudaStream_t s, const int64_t* ridx, int64_t src_rows, int64_t cols, int* status,
+               const ConvGeo* conv) {
   if (rows == 0) return IFK_OK;
   if (cols < 0) cols = n;
+  if (conv) {
+    if (dtype == IFK_BF16)
+      copy_conv_kernel<<<grid_for(rows * n), 256, 0, s>>>(X, ldX, (const __nv_bfloat16*)chunk, *conv, rows, n, ridx,
+                                                          src_rows, cols, status);
+    else
+      copy_conv_kernel<<<grid_for(rows * n), 256, 0, s>>>(X, ldX, (const float*)chunk, *conv, rows, n, ridx,
+                                                          src_rows, cols, status);
+    IFK_CUDA_TRY(cudaGetLastError());
+    return IFK_OK;
+  }
   if (dtype == IFK_BF16)
     copy_chunk_kernel<<<grid_for(rows * n), 256, 0, s>>>(
         X, ldX, (const __nv_bfloat16*)chunk, ld_chunk, rows, n, ridx, src_rows, cols, status);

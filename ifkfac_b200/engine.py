@@ -118,7 +118,11 @@ class Rows:
     """Rows of a 2-D device tensor for a fold, read in place by the fold kernels:
     ``x[index]`` (``index`` an int64 device tensor, or None for every row), with a
     column of ones appended when ``ones`` (the augmented-bias column).  The
-    reference's hooks copy both (``ifkfac/activation_hooks.py:531-543``)."""
+    reference's hooks copy both (``ifkfac/activation_hooks.py:531-543``).
+
+    :meth:`conv2d` gives the im2col rows of a Conv2d input (an NCHW tensor) the
+    same way: the fold gathers each element from the image, so the
+    ``F.unfold`` matrix of ``ifkfac/activation_hooks.py:489-499`` is never formed."""
 
     def __init__(self, x: torch.Tensor, index: Optional[torch.Tensor] = None, ones: bool = False):
         if x.dim() != 2:
@@ -132,13 +136,47 @@ class Rows:
             if index.dim() != 1:
                 raise ValueError("Rows index must be 1-D")
         self.x, self.index, self.ones = x, index, bool(ones)
+        self.geo = None  # im2col geometry (conv2d rows)
+
+    @classmethod
+    def conv2d(cls, x: torch.Tensor, module, index: Optional[torch.Tensor] = None) -> "Rows":
+        """im2col rows (B * Ho * Wo, C * kh * kw) of the NCHW input ``x`` of the Conv2d
+        ``module`` (F.unfold's order), optionally the rows ``index`` of them."""
+        if x.dim() != 4:
+            raise ValueError(f"a Conv2d input is N x C x H x W, got shape {tuple(x.shape)}")
+        if x.dtype not in _DT:
+            x = x.float()
+        x = x.contiguous()
+        r = cls.__new__(cls)
+        pair = lambda v: (v, v) if isinstance(v, int) else tuple(v)
+        (kh, kw), (sh, sw), (ph, pw), (dh, dw) = (pair(module.kernel_size), pair(module.stride),
+                                                  pair(module.padding), pair(module.dilation))
+        if isinstance(module.padding, str):
+            raise ValueError("string padding is not supported by the im2col rows")
+        B, C, H, W = x.shape
+        Ho = (H + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+        Wo = (W + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+        r.x = x
+        r.index = index.to(device=x.device, dtype=torch.int64).contiguous() if index is not None else None
+        r.ones = False
+        r.geo = dict(B=B, C=C, H=H, W=W, kh=kh, kw=kw, sh=sh, sw=sw, ph=ph, pw=pw, dh=dh, dw=dw, Ho=Ho, Wo=Wo)
+        r._module = module
+        return r
+
+    @property
+    def src_rows(self) -> int:
+        if self.geo is not None:
+            return self.geo["B"] * self.geo["Ho"] * self.geo["Wo"]
+        return int(self.x.shape[0])
 
     @property
     def rows(self) -> int:
-        return int(self.index.numel()) if self.index is not None else int(self.x.shape[0])
+        return int(self.index.numel()) if self.index is not None else self.src_rows
 
     @property
     def cols(self) -> int:
+        if self.geo is not None:
+            return self.geo["C"] * self.geo["kh"] * self.geo["kw"]
         return int(self.x.shape[1]) + (1 if self.ones else 0)
 
     @property
@@ -149,8 +187,19 @@ class Rows:
     def device(self) -> torch.device:
         return self.x.device
 
+    def conv_struct(self):
+        g = self.geo
+        return _lib.Conv2d(g["B"], g["C"], g["H"], g["W"], g["kh"], g["kw"], g["sh"], g["sw"],
+                           g["ph"], g["pw"], g["dh"], g["dw"])
+
     def materialize(self) -> torch.Tensor:
         """The rows as a tensor of their own (what the reference's hooks build)."""
+        if self.geo is not None:
+            g = self.geo
+            y = torch.nn.functional.unfold(self.x, kernel_size=(g["kh"], g["kw"]), dilation=(g["dh"], g["dw"]),
+                                           padding=(g["ph"], g["pw"]), stride=(g["sh"], g["sw"]))
+            y = y.permute(0, 2, 1).reshape(-1, self.cols)
+            return y[self.index] if self.index is not None else y
         y = self.x[self.index] if self.index is not None else self.x
         if self.ones:
             y = torch.cat([y, torch.ones(y.shape[0], 1, device=y.device, dtype=y.dtype)], dim=1)
@@ -195,10 +244,17 @@ def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence], ws: t
     nf = len(factors)
     flat = [r for cs in segs for r in cs]
     arr = (_lib.Segment * max(len(flat), 1))()
+    keep = []  # im2col geometries, alive for the call
     for i, r in enumerate(flat):
-        arr[i] = _lib.Segment(r.x.data_ptr(), r.x.stride(0), r.rows,
-                              r.index.data_ptr() if r.index is not None else None, r.x.shape[0], r.x.shape[1],
-                              _DT[r.dtype], 0)
+        if r.geo is not None:
+            geo = r.conv_struct()
+            keep.append(geo)
+            arr[i] = _lib.Segment(r.x.data_ptr(), 0, r.rows, r.index.data_ptr() if r.index is not None else None,
+                                  r.src_rows, r.cols, _DT[r.dtype], 0, ctypes.pointer(geo))
+        else:
+            arr[i] = _lib.Segment(r.x.data_ptr(), r.x.stride(0), r.rows,
+                                  r.index.data_ptr() if r.index is not None else None, r.x.shape[0], r.x.shape[1],
+                                  _DT[r.dtype], 0, None)
     ns = _arr(ctypes.c_int64, [f.n for f in factors])
     nseg = _arr(ctypes.c_int, [len(cs) for cs in segs])
     tail = _arr(ctypes.c_double, [float(v) for v in ident_tail]) if ident_tail is not None else None

@@ -152,6 +152,7 @@ IFK_API int ifk_tsqr_fold_batched(int nfolds, float* const* R, const int64_t* ld
  * status word.  dtype (IFK_F32 or IFK_BF16) is the chunk's element type when
  * the call's chunk_dtype is IFK_PER_SEGMENT_DTYPE, and is ignored otherwise.
  */
+typedef struct ifk_conv2d ifk_conv2d;
 typedef struct ifk_segment {
   const void* chunk;
   int64_t ld;
@@ -161,7 +162,27 @@ typedef struct ifk_segment {
   int64_t cols;
   int32_t dtype;
   int32_t reserved;
+  const ifk_conv2d* conv;  /* NULL, or the chunk is an image read through im2col (below) */
 } ifk_segment;
+
+/*
+ * An ifk_segment whose `conv` is set reads its rows from a contiguous
+ * N x C x H x W image `chunk` through im2col, the rows of the reference's
+ * F.unfold (ifkfac/activation_hooks.py:489-499): image row
+ * b * Ho * Wo + oh * Wo + ow, column (c * kernel_h + ki) * kernel_w + kj, holds
+ * chunk[b, c, oh * stride_h - pad_h + ki * dilation_h,
+ *       ow * stride_w - pad_w + kj * dilation_w] (zero outside the image), with
+ * Ho, Wo the output size of the convolution.  cols must be C * kernel_h *
+ * kernel_w and src_rows N * Ho * Wo; row_index (optional) picks image rows, the
+ * conv-row subsample of :522-530; `ld` is ignored.  The fold reads the elements
+ * in place: the im2col matrix is never formed.  The geometry is read during
+ * the call (host memory).
+ */
+struct ifk_conv2d {
+  int64_t batch, channels, height, width;
+  int32_t kernel_h, kernel_w, stride_h, stride_w;
+  int32_t pad_h, pad_w, dilation_h, dilation_w;
+};
 
 /* chunk_dtype of ifk_tsqr_fold_segments: each segment gives its own (needs an
  * explicit IFK_PREC_FP32 or IFK_PREC_BF16). */

@@ -54,10 +54,33 @@ def test_segment_struct_matches_header():
     """ctypes mirror of ifk_segment: the field order and offsets of include/ifk.h."""
     import re
     body = re.search(r"typedef struct ifk_segment \{(.*?)\} ifk_segment;", open(_lib.HEADER).read(), re.S).group(1)
-    fields = re.findall(r"(\w+);", body)
+    fields = re.findall(r"(\w+);", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
     assert fields == [f for f, _ in _lib.Segment._fields_]
-    assert ctypes.sizeof(_lib.Segment) == 56
-    assert _lib.Segment.cols.offset == 40 and _lib.Segment.dtype.offset == 48
+    assert ctypes.sizeof(_lib.Segment) == 64
+    assert _lib.Segment.cols.offset == 40 and _lib.Segment.dtype.offset == 48 and _lib.Segment.conv.offset == 56
+    body = re.search(r"struct ifk_conv2d \{(.*?)\};", open(_lib.HEADER).read(), re.S).group(1)
+    names = [n for grp in re.findall(r"int\d+_t ([\w, ]+);", body) for n in grp.replace(" ", "").split(",")]
+    assert names == [f for f, _ in _lib.Conv2d._fields_]
+    assert ctypes.sizeof(_lib.Conv2d) == 64
+
+
+def test_conv_segment_geometry_errors_before_any_gpu_work():
+    """im2col segments: the columns must be C kh kw and the source rows N Ho Wo."""
+    L = _lib.lib()
+    a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
+    geo = _lib.Conv2d(2, 3, 8, 8, 3, 3, 1, 1, 1, 1, 1, 1)  # Ho = Wo = 8
+    n = 27
+
+    def call(cols=27, src=2 * 64, rows=100, g=geo):
+        segs = (_lib.Segment * 1)(_lib.Segment(0x1000, 0, rows, None, src, cols, 0, 0, ctypes.pointer(g)))
+        return L.ifk_tsqr_fold_segments(1, (ctypes.c_void_p * 1)(0x2000), a64(n), a64(0), a64(n),
+                                        (ctypes.c_int * 1)(1), segs, _lib.BF16, None, _lib.PREC_BF16, None,
+                                        None, 0, None)
+    assert call() == _lib.ERR_WORKSPACE  # valid geometry: only the missing workspace is refused
+    assert call(cols=26) == _lib.ERR_SHAPE
+    assert call(src=2 * 63) == _lib.ERR_SHAPE
+    assert call(rows=2 * 64 + 1) == _lib.ERR_SHAPE  # more rows than the image has
+    assert call(g=_lib.Conv2d(2, 3, 8, 8, 3, 3, 0, 1, 1, 1, 1, 1)) == _lib.ERR_SHAPE  # zero stride
 
 
 def test_segment_fold_argument_errors_before_any_gpu_work():
