@@ -224,6 +224,53 @@ def time_components(lc, per_tile, tiles, X, D, gW, W):
     return comp
 
 
+def time_fp32_mode(dev, X, D, gW, W, tiles):
+    """The same operator in the fp32 mode (IFK_PREC_FP32, the reference's
+    use_true_bf16=False path at its 1e-5 bound): fp32 rows, one fold launch per tile
+    (fp32 Householder panels, fp32 trailing updates on the CUDA cores), the damping
+    fold, fp32 factors, fp32 solves and the update.  Eager, CUDA events, one GPU."""
+    import torch
+    from ifkfac_b200 import _lib
+    from ifkfac_b200.engine import LayerCurvature
+    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_FP32, torch.float32, TILE, window=1)
+    Xf, Df, Wf = X.float(), D.float(), W.clone()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def step(comp=None):
+        marks = [ev() for _ in range(4)]
+        marks[0].record()
+        lc.clear()
+        for lo, hi in tiles:
+            lc.fold(Xf[lo:hi], Df[lo:hi])
+        marks[1].record()
+        lc.refresh(DAMPING)
+        marks[2].record()
+        lc.natgrad_update(gW, Wf, LR, MOM)
+        marks[3].record()
+        if comp is not None:
+            marks[3].synchronize()
+            comp.update(tsqr_ms=marks[0].elapsed_time(marks[1]), fold_ms=marks[1].elapsed_time(marks[2]),
+                        trsm_update_ms=marks[2].elapsed_time(marks[3]))
+
+    step()
+    torch.cuda.synchronize()
+    comp = {}
+    step(comp)
+    k = 3
+    a, b = ev(), ev()
+    a.record()
+    for _ in range(k):
+        step()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / k
+    out = {"ms_per_step": ms, "value": 1000.0 / ms, "unit": "steps/s", "dtype": "f32",
+           "timing": "eager, CUDA events, one GPU", "components_ms": comp}
+    del lc, Xf, Df, Wf
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     from ifkfac_b200 import _lib
@@ -326,6 +373,11 @@ def run_ours(args, rank, world, local_rank):
                  "value": 1000.0 / oms, "unit": "steps/s", "timing": "eager, CUDA events, one GPU",
                  "components_ms": time_components(lco, not per_tile, tiles, X, D, gW, Wo)}
         del lco, Wo
+
+    # ---- secondary: the fp32 mode (use_true_bf16=False) on the same operator ----
+    fp32 = None
+    if rank == 0 and not args.no_fp32_mode:
+        fp32 = time_fp32_mode(dev, X, D, gW, W, tiles)
 
     # ---- end to end through the public API: pinned host inputs in, weights out ----
     e2e = None
@@ -445,6 +497,7 @@ def run_ours(args, rank, world, local_rank):
         "components_ms": comp,
         "schedule": args.schedule,
         "other_schedule": other,
+        "fp32_mode": fp32,
         "gpu_launches": (n_ours * args.steps) if n_ours is not None else None,
         "gpu_launches_detail": {"libifk_per_step": n_ours, "torch_per_step": n_other, "source": launch_src},
         "clocks": clk.summary(),
@@ -1299,6 +1352,8 @@ def main():
                     help="N > 1, config 2: 'rows' (default) solves the same operator on N GPUs, rows "
                          "batch-sharded and merged by the R-tree; 'layers' gives every rank a layer of its own "
                          "(independent operators, no collective)")
+    ap.add_argument("--no-fp32-mode", action="store_true",
+                    help="skip the secondary timing of the fp32 mode (use_true_bf16=False)")
     ap.add_argument("--no-other-schedule", action="store_true",
                     help="skip the secondary timing of the other schedule")
     ap.add_argument("--profile", action="store_true",

@@ -553,6 +553,8 @@ int ifk_finalize(const float* R_in, int64_t ldR, int64_t rows_R, int64_t n, doub
   const int64_t ldF = xw_ld(n);
   float* Rf = (float*)workspace;
   void* fws = (char*)workspace + align_up((size_t)n * ldF * sizeof(float));
+  if (damping == 0)  // nothing to fold: scale, cast and check in one pass
+    return finish_factor(R_out, ld_out, out_dtype, R_in, ldR, n, d_status, s, (float)std::sqrt(rows_total));
   int rc = scale_upper(Rf, ldF, R_in, ldR, n, (float)std::sqrt(rows_total), s);
   if (rc != IFK_OK) return rc;
   if (damping > 0 && prec == IFK_PREC_BF16) {
@@ -616,6 +618,17 @@ static int finalize_many(int nfactors, const float* const* R_in, const int64_t* 
     const int cnt = std::min(MAX_FOLDS, nfactors - base);
     char* ws = (char*)workspace;
     float* Rf[MAX_FOLDS];
+    if (damping == 0) {
+      // nothing to fold: each factor is scaled, cast and checked in one pass
+      for (int q = 0; q < cnt; ++q) {
+        const int f = base + q;
+        int* st = f_status ? f_status[f] : d_status;
+        const int rc = finish_factor(R_out[f], ld_out[f], out_dtype, R_in[f], ldR[f], n[f], st, s,
+                                     (float)std::sqrt(rows_total[f]));
+        if (rc != IFK_OK) return rc;
+      }
+      continue;
+    }
     for (int q = 0; q < cnt; ++q) {
       const int f = base + q;
       Rf[q] = (float*)ws;

@@ -130,9 +130,10 @@ int scale_upper(float* Rout, int64_t ldo, const float* Rin, int64_t ldi, int64_t
 // Run the fold waves.  prec: IFK_PREC_FP32 or IFK_PREC_BF16.
 int fold_run(const FoldArgs& a, int prec, cudaStream_t s);
 int fold_run_batch(const FoldBatch& b, int prec, cudaStream_t s);
-// Cast an n x n fp32 factor to the output type and flag non-finite entries.
+// Cast an n x n fp32 factor to the output type and flag non-finite entries; with
+// scale > 0 the output is upper(R) / scale (scale_upper and the cast in one pass).
 int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t ldR, int64_t n,
-                  int* d_status, cudaStream_t s);
+                  int* d_status, cudaStream_t s, float scale = 0.f);
 
 // In-place triangular solve op(A) X = B on a strided view of B (n x N).
 // A is an n x n upper-triangular factor (fp32 or bf16); trans != 0 solves

@@ -30,8 +30,8 @@
 // strictly upper 128 x 128 block of A once as the shared-memory image of the
 // operand tile it becomes (K-major for op = A, MN-major transposed for
 // op = A^T) and clears the readiness flags; diag_inverse_layout_kernel writes
-// the inverses of the diagonal blocks (fp32 column substitution, 3-term bf16
-// split) in the operand layout.
+// the inverses of the diagonal blocks (fp32 column substitution, four threads
+// per column, 3-term bf16 split) in the operand layout.
 // Every wait is bounded: a role that gives up raises the launch's abort word,
 // every role of every CTA stops at its next wait, and the launch reports
 // IFK_ERR_TIMEOUT.
@@ -237,39 +237,41 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(const __grid_constant__
 // m in [hi K, lo K, hi MN, lo MN] order (SZ_A each) at inv_m + b * 4 * SZ_A.
 // One launch covers every block of a list of matrices.  Ragged last block:
 // identity pad.
-__global__ void __launch_bounds__(NB2) diag_inverse_layout_kernel(const __grid_constant__ InvBatch ib) {
+constexpr int INV_TPB = 4 * NB2;  // four threads per column of the inverse
+__global__ void __launch_bounds__(INV_TPB) diag_inverse_layout_kernel(const __grid_constant__ InvBatch ib) {
   extern __shared__ float dsm[];
   float (*U)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm);
   float (*Xs)[NB2 + 1] = reinterpret_cast<float (*)[NB2 + 1]>(dsm + NB2 * (NB2 + 1));
   const int mat = find_problem(ib.blk0, ib.nm, (int)blockIdx.x);
   const __nv_bfloat16* A = ib.A[mat];
   const int64_t ldA_ = ib.ld[mat], n = ib.n[mat];
-  const int b = (int)blockIdx.x - ib.blk0[mat], q = threadIdx.x;
+  const int b = (int)blockIdx.x - ib.blk0[mat], t = threadIdx.x;
   const int64_t b0 = (int64_t)b * NB2;
   const int nb = (int)mn<int64_t>(NB2, n - b0);
-  for (int idx = q; idx < NB2 * NB2; idx += NB2) {
+  for (int idx = t; idx < NB2 * NB2; idx += INV_TPB) {
     const int r = idx / NB2, l = idx % NB2;
     float v = (r == l) ? 1.f : 0.f;
     if (r < nb && l < nb) v = (l >= r) ? __bfloat162float(A[(b0 + r) * ldA_ + b0 + l]) : 0.f;
     U[r][l] = v;
   }
   __syncthreads();
-  // column q of U^-1 by back substitution; four partial sums break the FMA chain
-  for (int r = NB2 - 1; r >= 0; --r) {
-    float s0 = (r == q) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int l = r + 1;
-    for (; l + 3 < NB2; l += 4) {
-      s0 -= U[r][l] * Xs[l][q];
-      s1 -= U[r][l + 1] * Xs[l + 1][q];
-      s2 -= U[r][l + 2] * Xs[l + 2][q];
-      s3 -= U[r][l + 3] * Xs[l + 3][q];
+  // Column q of U^-1 by back substitution.  The four lanes of a column (one warp
+  // quad) each sum a residue class of the row's products, and two shuffles add
+  // the partial sums: the dependency from row r to row r - 1 stays inside the warp.
+  {
+    const int q = t >> 2, part = t & 3;
+    for (int r = NB2 - 1; r >= 0; --r) {
+      float acc = (part == 0 && r == q) ? 1.f : 0.f;
+      for (int l = r + 1 + part; l < NB2; l += 4) acc -= U[r][l] * Xs[l][q];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0) Xs[r][q] = acc / U[r][r];
+      __syncwarp();
     }
-    for (; l < NB2; ++l) s0 -= U[r][l] * Xs[l][q];
-    Xs[r][q] = ((s0 + s1) + (s2 + s3)) / U[r][r];
   }
   __syncthreads();
   uint8_t* o = ib.inv[mat] + (size_t)b * 4 * SZ_A;
-  for (int it = q; it < NB2 * (NB2 / 8); it += NB2) {
+  for (int it = t; it < NB2 * (NB2 / 8); it += INV_TPB) {
     // K-major: 8 consecutive k = l of row m; MN-major (transpose): 8 consecutive mn = l of k = m
     const int m = it >> 4, l8 = it & 15;
     float hi[8], lo[8];
@@ -788,7 +790,7 @@ int trsm_persist_prepare_many(int nm, const __nv_bfloat16* const* A, const int64
     }
     ib.blk0[ib.nm] = acc;
     if (acc == 0) continue;
-    diag_inverse_layout_kernel<<<(unsigned)acc, NB2, INV_SMEM, s>>>(ib);
+    diag_inverse_layout_kernel<<<(unsigned)acc, INV_TPB, INV_SMEM, s>>>(ib);
     IFK_CUDA_TRY(cudaGetLastError());
   }
   return IFK_OK;

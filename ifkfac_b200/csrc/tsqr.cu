@@ -292,33 +292,96 @@ __global__ void fill_identity_kernel(float* X, int64_t ldX, int64_t n, float v) 
   }
 }
 
+// Row-per-block elementwise passes over an n x n factor: blockIdx.y (and further
+// rows by stride) picks the row, the threads take its columns 4 at a time.
+__device__ __forceinline__ bool aligned16(const void* p, int64_t ld, int bytes) {
+  return ((uintptr_t)p % 16) == 0 && (ld * bytes) % 16 == 0;
+}
+
 __global__ void scale_upper_kernel(float* Ro, int64_t ldo, const float* Ri, int64_t ldi, int64_t n,
                                    float scale) {
-  const int64_t total = n * n;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = idx / n, j = idx % n;
-    Ro[i * ldo + j] = (j >= i) ? Ri[i * ldi + j] / scale : 0.f;
+  const bool vec = aligned16(Ro, ldo, 4) && aligned16(Ri, ldi, 4);
+  for (int64_t i = blockIdx.y; i < n; i += gridDim.y) {
+    const float* src = Ri + i * ldi;
+    float* dst = Ro + i * ldo;
+    for (int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; j0 < n;
+         j0 += (int64_t)gridDim.x * blockDim.x * 4) {
+      if (vec && j0 + 4 <= n) {
+        const float4 v = *reinterpret_cast<const float4*>(src + j0);
+        float4 o;
+        o.x = j0 >= i ? v.x / scale : 0.f;
+        o.y = j0 + 1 >= i ? v.y / scale : 0.f;
+        o.z = j0 + 2 >= i ? v.z / scale : 0.f;
+        o.w = j0 + 3 >= i ? v.w / scale : 0.f;
+        *reinterpret_cast<float4*>(dst + j0) = o;
+      } else {
+        for (int64_t j = j0; j < j0 + 4 && j < n; ++j) dst[j] = (j >= i) ? src[j] / scale : 0.f;
+      }
+    }
   }
 }
 
+// out = upper(R) / scale (scale 1: a copy) in out's element type; any non-finite
+// value sets IFK_ERR_NONFINITE.  With scale != 1 this is the damping-free finalize
+// in one pass: the same division and cast as scale_upper followed by the cast.
 template <typename Tout>
 __global__ void finish_factor_kernel(Tout* out, int64_t ldo, const float* R, int64_t ldR, int64_t n,
-                                     int* status) {
-  const int64_t total = n * n;
+                                     int* status, float scale, int apply_scale) {
   bool bad = false;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = idx / n, j = idx % n;
-    const float v = R[i * ldR + j];
-    bad |= !isfinite(v);
-    if constexpr (sizeof(Tout) == 2) {
-      out[i * ldo + j] = __float2bfloat16_rn(v);
-    } else {
-      if ((const void*)out != (const void*)R || ldo != ldR) out[i * ldo + j] = v;
+  const bool vec = aligned16(R, ldR, 4) && aligned16(out, ldo, sizeof(Tout) == 2 ? 2 : 4) &&
+                   (sizeof(Tout) == 4 || ((uintptr_t)out % 8) == 0);
+  for (int64_t i = blockIdx.y; i < n; i += gridDim.y) {
+    const float* src = R + i * ldR;
+    Tout* dst = out + i * ldo;
+    for (int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; j0 < n;
+         j0 += (int64_t)gridDim.x * blockDim.x * 4) {
+      float v[4];
+      const bool full = vec && j0 + 4 <= n;
+      if (full) {
+        const float4 x = *reinterpret_cast<const float4*>(src + j0);
+        v[0] = x.x;
+        v[1] = x.y;
+        v[2] = x.z;
+        v[3] = x.w;
+      } else {
+        for (int e = 0; e < 4; ++e) v[e] = j0 + e < n ? src[j0 + e] : 0.f;
+      }
+      if (apply_scale) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = (j0 + e >= i) ? v[e] / scale : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) bad |= (j0 + e < n) && !isfinite(v[e]);
+      if constexpr (sizeof(Tout) == 2) {
+        if (full) {
+          __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+          uint2 u;
+          u.x = *reinterpret_cast<uint32_t*>(&a);
+          u.y = *reinterpret_cast<uint32_t*>(&b);
+          *reinterpret_cast<uint2*>(dst + j0) = u;
+        } else {
+          for (int e = 0; e < 4; ++e)
+            if (j0 + e < n) dst[j0 + e] = __float2bfloat16_rn(v[e]);
+        }
+      } else {
+        if (apply_scale || (const void*)out != (const void*)R || ldo != ldR) {
+          if (full) {
+            *reinterpret_cast<float4*>(dst + j0) = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+            for (int e = 0; e < 4; ++e)
+              if (j0 + e < n) dst[j0 + e] = v[e];
+          }
+        }
+      }
     }
   }
   if (bad && status) atomicExch(status, IFK_ERR_NONFINITE);
+}
+
+dim3 rows_grid(int64_t n) {
+  const int64_t x = cdiv(cdiv(n, 4), 256);
+  const int64_t y = n < 2048 ? n : 2048;
+  return dim3((unsigned)(x < 1 ? 1 : x), (unsigned)(y < 1 ? 1 : y));
 }
 
 int grid_for(int64_t total) {
@@ -384,18 +447,18 @@ int fill_scaled_identity(float* X, int64_t ldX, int64_t n, float v, cudaStream_t
 
 int scale_upper(float* Rout, int64_t ldo, const float* Rin, int64_t ldi, int64_t n, float scale,
                 cudaStream_t s) {
-  scale_upper_kernel<<<grid_for(n * n), 256, 0, s>>>(Rout, ldo, Rin, ldi, n, scale);
+  scale_upper_kernel<<<rows_grid(n), 256, 0, s>>>(Rout, ldo, Rin, ldi, n, scale);
   IFK_CUDA_TRY(cudaGetLastError());
   return IFK_OK;
 }
 
 int finish_factor(void* out, int64_t ldo, int out_dtype, const float* R, int64_t ldR, int64_t n,
-                  int* d_status, cudaStream_t s) {
+                  int* d_status, cudaStream_t s, float scale) {
+  const int apply = scale > 0.f ? 1 : 0;
   if (out_dtype == IFK_BF16)
-    finish_factor_kernel<<<grid_for(n * n), 256, 0, s>>>((__nv_bfloat16*)out, ldo, R, ldR, n,
-                                                         d_status);
+    finish_factor_kernel<<<rows_grid(n), 256, 0, s>>>((__nv_bfloat16*)out, ldo, R, ldR, n, d_status, scale, apply);
   else
-    finish_factor_kernel<<<grid_for(n * n), 256, 0, s>>>((float*)out, ldo, R, ldR, n, d_status);
+    finish_factor_kernel<<<rows_grid(n), 256, 0, s>>>((float*)out, ldo, R, ldR, n, d_status, scale, apply);
   IFK_CUDA_TRY(cudaGetLastError());
   return IFK_OK;
 }
