@@ -120,6 +120,10 @@ __device__ __forceinline__ long long gtime() {
 #define TR_SET(i, v) tr[i] = (v)
 #define TR_ADD(i, v) tr[i] += (v)
 #define TR_NOW() gtime()
+__device__ long long g_wait_ns[1024];
+#define WT_BEGIN const long long wt0_ = gtime();
+#define WT_END g_wait_ns[blockIdx.x & 1023] += gtime() - wt0_;
+#define TR_WAIT() g_wait_ns[blockIdx.x & 1023]
 #define TR_FLUSH()                                                     \
   if (threadIdx.x == 0) {                                              \
     const int slot = atomicAdd(&g_trace_n, 1);                         \
@@ -132,6 +136,9 @@ __device__ __forceinline__ long long gtime() {
 #define TR_ADD(i, v)
 #define TR_NOW() 0
 #define TR_FLUSH()
+#define WT_BEGIN
+#define WT_END
+#define TR_WAIT() 0
 #endif
 
 #ifdef IFK_TRACE
@@ -235,6 +242,7 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 // Thread 0 waits for *flag >= target (bounded); the CTA learns the outcome through smem.
 __device__ __forceinline__ bool cta_wait_ge(const int* flag, int target, const PFBatch& b, int* s_ok) {
   if (threadIdx.x == 0) {
+    WT_BEGIN
     int ok = 0;
     for (uint32_t it = 0; it < b.wait_limit; ++it) {
       if (ld_acquire(flag) >= target) {
@@ -249,6 +257,7 @@ __device__ __forceinline__ bool cta_wait_ge(const int* flag, int target, const P
       if (b.status) atomicExch(b.status, IFK_ERR_TIMEOUT);
     }
     *s_ok = ok;
+    WT_END
   }
   __syncthreads();
   const bool ok = *(volatile int*)s_ok != 0;
@@ -671,6 +680,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(1, t);
   TR_SET(2, cb);
   TR_SET(3, TR_NOW());
+  TR_SET(20, TR_WAIT());
   const int tid = threadIdx.x, warp = tid >> 5;
   int si = 0;  // segment of sub-tile t
   const PSeg* SG = b.seg + F.seg0;
@@ -764,7 +774,6 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       if (t > 0 && !cta_wait_ge(prev_prog, k + 1, b, s_ok)) return;
     }
     AP_MARK(9);
-    TR_SET(21, TR_NOW());
     TR_ADD(9, TR_NOW() - w0);
     TR_ADD(10, 1);
     if (tid == LA && !(c.ipend & (1 << buf))) {
@@ -808,6 +817,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   //   skipped by every earlier sub-tile too, or by every later one, so its stages
   //   pass at once.
   TR_SET(6, TR_NOW());
+  TR_SET(21, TR_WAIT());
   PanelSmem& S = *reinterpret_cast<PanelSmem*>(c.sm);
   int* pending_img = nullptr;  // flag of panel images whose bulk store is in flight
   // test only (IFK_FOLD_DEBUG_WITHHOLD): panel 0 of fold 0's first sub-tile is never
@@ -916,6 +926,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   tc::fence_before();
   cta_publish_value(prog, stage_done(F.K));
   TR_SET(7, TR_NOW());
+  TR_SET(22, TR_WAIT());
   TR_FLUSH();
 }
 
