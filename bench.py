@@ -1016,21 +1016,30 @@ def run_c1(args, rank, world, local_rank):
 
 
 def run_c5(args, rank, world, local_rank):
-    """BASELINE config 5 on one GPU: a Llama-1B-shaped decoder (16 blocks, d 2048, 32 query
-    and 8 key/value heads, SwiGLU MLP 8192, vocab 128256 with the head tied to the
-    embedding, RMSNorm; no rotary embedding, which does not change a K-FAC shape),
-    random init, bf16 autocast, batch 4 x 2048 tokens, uniform random token ids.  K-FAC on
-    the 112 Linear layers of the blocks (q, k, v, o, gate, up, down), use_true_bf16,
-    damping 1e-3, factor_update_freq 20, the reference's default 2048 rows per layer and
-    step (max_seq_rows None), batched_qr.  Config 5 as stated runs p = 32768 rows on 8
-    GPUs; this is its one-GPU, default-rows form.  A step is forward + backward + IFKFAC.step."""
+    """a Llama-1B-shaped decoder (16 blocks, d 2048, 32 query and 8
+    key/value heads, SwiGLU MLP 8192, vocab 128256 with the head tied to the embedding,
+    RMSNorm; no rotary embedding, which does not change a K-FAC shape), random init,
+    bf16 autocast, sequences of 2048 uniform random token ids.  K-FAC on the 112 Linear
+    layers of the blocks (q, k, v, o, gate, up, down), use_true_bf16, damping 1e-3,
+    factor_update_freq 20, the reference's default 2048 rows per layer and step
+    (max_seq_rows None), batched_qr.  A step is forward + backward + the optimizer step.
+
+    Data-parallel over the ranks (config 5 as stated: batch 16 = 32768 tokens on 8
+    GPUs, i.e. 2 sequences per GPU): each rank runs ``--c5-batch`` sequences of its
+    own (weak scaling), and with more than one rank the optimizer is
+    DistributedIFKFAC: the TSQR batch-sharded (each rank folds its own rows), the
+    factors reduced to their layer's owner by the R-tree every 20 steps, gradients
+    averaged, layers round-robined for the solves and the updated weights broadcast."""
     import torch
+    import torch.distributed as dist
     import torch.nn as nn
     import torch.nn.functional as F
     from ifkfac_b200.ifkfac import IFKFAC
+    from ifkfac_b200.distributed import DistributedIFKFAC
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    d, nh, nkv, ff, vocab, nblk, seq, batch = 2048, 32, 8, 8192, 128256, 16, 2048, 4
+    d, nh, nkv, ff, vocab, nblk, seq = 2048, 32, 8, 8192, 128256, 16, 2048
+    batch = args.c5_batch
     hd = d // nh
 
     class Block(nn.Module):
@@ -1068,13 +1077,13 @@ def run_c5(args, rank, world, local_rank):
                 x = b(x)
             return F.linear(self.norm(x), self.tok.weight)  # tied head: not a K-FAC layer
 
-    torch.manual_seed(0)
+    torch.manual_seed(0)  # the same initial weights on every rank
     model = Llama().to(dev)
-    g = torch.Generator(device=dev).manual_seed(0)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)  # each rank its own batch shard
     idx = torch.randint(0, vocab, (batch, seq + 1), generator=g, device=dev)
     x, y = idx[:, :-1], idx[:, 1:]
-    opt = IFKFAC(model, lr=1e-4, damping=1e-3, factor_update_freq=20, momentum=0.9, use_true_bf16=True,
-                 batched_qr=True)
+    kw = dict(lr=1e-4, damping=1e-3, factor_update_freq=20, momentum=0.9, use_true_bf16=True, batched_qr=True)
+    opt = DistributedIFKFAC(model, **kw) if world > 1 else IFKFAC(model, **kw)
 
     def one():
         opt.zero_grad()
@@ -1085,10 +1094,16 @@ def run_c5(args, rank, world, local_rank):
         opt.step()
         return loss
 
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
     steps = max(20, (args.steps + 19) // 20 * 20)
-    for _ in range(max(args.warmup, 20)):  # past the first refresh
+    warm = max(args.warmup, 20)
+    for _ in range(warm):  # past the first refresh
         one()
     torch.cuda.synchronize()
+    barrier()
     with ClockSampler(local_rank) as clk:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -1096,21 +1111,32 @@ def run_c5(args, rank, world, local_rank):
             loss = one()
         b.record()
         b.synchronize()
+    barrier()
     ms = a.elapsed_time(b) / steps
-    ksum = kernel_summary(one, 20) if args.kernel_summary else None
-    out = {"metric": "preconditioned steps/sec (training step: forward + backward + IFKFAC.step)",
-           "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 20),
-           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic",
-           "config": {"workload": "C5 Llama-1B-shaped decoder on one GPU, 16 x (q, k, v, o, gate, up, down) "
-                                  "under K-FAC, 4 x 2048 tokens, 2048 rows per layer and step, bf16 autocast, "
-                                  "use_true_bf16, damping 1e-3, factor_update_freq 20, batched_qr",
-                      "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
-                      "timing": "eager, CUDA events around the step loop (host work included)"},
-           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9, "clocks": clk.summary(),
-           "kernel_summary": ksum}
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ksum = kernel_summary(one, 20) if args.kernel_summary and world == 1 else None
+    peak = torch.cuda.max_memory_allocated(dev) / 1e9
+    if rank == 0:
+        tokens = world * batch * seq
+        out = {"metric": "training tokens/s (forward + backward + IFKFAC.step, K-FAC on 112 layers)",
+               "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+               "warmup": warm, "ms_per_step": ms, "steps_per_s": 1000.0 / ms, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": "C5 Llama-1B-shaped decoder, 16 x (q, k, v, o, gate, up, down) under "
+                                      "K-FAC, 2048 rows per layer and step, bf16 autocast, use_true_bf16, "
+                                      "damping 1e-3, factor_update_freq 20, batched_qr",
+                          "sequences_per_gpu": batch, "seq_len": seq, "global_batch": world * batch,
+                          "parallelism": ("single GPU" if world == 1 else
+                                          f"data parallel over {world} GPUs: TSQR batch-sharded, R-tree to the "
+                                          "layer owners every 20 steps, layers round-robined for the solves"),
+                          "layers_under_kfac": len(opt.hooks.linear_layers), "final_loss": float(loss.item()),
+                          "timing": "eager, CUDA events around the step loop (host work included), max over ranks"},
+               "peak_mem_gb": peak, "clocks": clk.summary(), "kernel_summary": ksum}
+        print(json.dumps(out), flush=True)
     opt.cleanup()
-    print(json.dumps(out), flush=True)
 
 
 def run_laplace(args, rank, world, local_rank):
@@ -1334,8 +1360,11 @@ def main():
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "laplace"], default="c2",
                     help="c1: the reference's CPU-runnable MLP; c2: the single-layer operator (the headline); "
                          "c3: the 8-layer MLP training step; "
-                         "c4: the GPT-2-small-shaped decoder training step; c5: the Llama-1B-shaped one on one GPU; "
+                         "c4: the GPT-2-small-shaped decoder training step; c5: the Llama-1B-shaped one, data parallel "
+                         "over the ranks; "
                          "laplace: K-FAC Laplace draws")
+    ap.add_argument("--c5-batch", type=int, default=2,
+                    help="c5: sequences of 2048 tokens per GPU (config 5: 16 on 8 GPUs, i.e. 2 per GPU)")
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
@@ -1370,9 +1399,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)  # rank 0 only; other ranks exit without work
         return
-    if args.config in ("c1", "c3", "c4", "c5", "laplace"):
+    if args.config in ("c1", "c3", "c4", "laplace"):
         if rank == 0:
-            runs = {"c1": run_c1, "c3": run_c3, "c4": run_c4, "c5": run_c5, "laplace": run_laplace}
+            runs = {"c1": run_c1, "c3": run_c3, "c4": run_c4, "laplace": run_laplace}
             runs[args.config](args, rank, world, local_rank)
         return
     if world > 1:
@@ -1382,7 +1411,9 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        if world > 1 and args.partition == "rows":
+        if args.config == "c5":
+            run_c5(args, rank, world, local_rank)
+        elif world > 1 and args.partition == "rows":
             run_sharded(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)

@@ -164,6 +164,146 @@ def merge_or_skip(R: torch.Tensor, rows: int, rows_seen: int,
         return None
 
 
+# merge_many([(R_a, rows_a, R_b, rows_b, prec), ...]): each R_b's rows folded into
+# its R_a, in place (R_b holds only the rows that are sent: rows_b of them in bf16
+# mode, the whole factor in fp32 mode)
+MergeMany = Callable[[Sequence[Tuple[torch.Tensor, int, torch.Tensor, int, int]]], None]
+
+
+def fold_merge_many(jobs: Sequence[Tuple[torch.Tensor, int, torch.Tensor, int, int]]) -> None:
+    """The merges of one round of :func:`rtree_reduce_many` on the device: the
+    trapezoidal folds of each precision in one ``ifk_tsqr_fold_batched`` call
+    (the library runs up to 64 of them per persistent launch)."""
+    import ctypes
+    from . import _lib
+    from .engine import _arr, _stream
+    L = _lib.lib()
+    by_prec = {}
+    for j in jobs:
+        if j[2].shape[0] > 0:
+            by_prec.setdefault(j[4], []).append(j)
+    for prec, js in by_prec.items():
+        k = len(js)
+        ns = [ra.shape[1] for ra, _, _, _, _ in js]
+        rows = [rb.shape[0] for _, _, rb, _, _ in js]
+        dev = js[0][0].device
+        need = int(L.ifk_tsqr_fold_batched_workspace(k, _arr(ctypes.c_int64, rows), _arr(ctypes.c_int64, ns)))
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check(L.ifk_tsqr_fold_batched(
+            k, _arr(ctypes.c_void_p, [ra.data_ptr() for ra, _, _, _, _ in js]),
+            _arr(ctypes.c_int64, [ra.stride(0) for ra, _, _, _, _ in js]),
+            _arr(ctypes.c_int64, [min(na, ra.shape[1]) for ra, na, _, _, _ in js]),
+            _arr(ctypes.c_void_p, [rb.data_ptr() for _, _, rb, _, _ in js]),
+            _arr(ctypes.c_int64, [rb.stride(0) for _, _, rb, _, _ in js]), _arr(ctypes.c_int64, rows),
+            _arr(ctypes.c_int64, ns), _lib.F32, prec, _lib.FOLD_TRAPEZOIDAL_CHUNK, status.data_ptr(),
+            ws.data_ptr(), ws.numel(), _stream()), "ifk_tsqr_fold_batched")
+
+
+def rtree_reduce_many(items: Sequence[Tuple[torch.Tensor, int, int, int]], owners: Sequence[int],
+                      group: Optional[dist.ProcessGroup] = None, merge_many: MergeMany = fold_merge_many,
+                      bucket_bytes: int = 1 << 30) -> List[Tuple[int, int]]:
+    """The R-tree of :func:`rtree_merge` for many factors at once, each reduced to
+    its owner rank instead of to rank 0 and broadcast.
+
+    ``items[f] = (R, rows, rows_seen, prec)``: this rank's local factor f (n x n
+    fp32, ``rows`` meaningful rows, built from ``rows_seen`` data rows; ``prec``
+    the fold precision, ``_lib.PREC_*``).  Factor f is merged over the ranks
+    relabelled from ``owners[f]`` (relative rank (rank - owner) mod world), in the
+    order of the reference's ``tsqr`` tree over the relative ranks
+    (``ifkfac/triangular.py:207-220``: adjacent pairs, odd one carried forward),
+    so that the factor of all rows ends in ``items[f][0]`` on the owner.  Other
+    ranks' buffers hold partial merges or their local factor afterwards.
+
+    One ``all_gather`` of every factor's counts; then per round of the tree, the
+    exchanges of all factors go in buckets of at most ``bucket_bytes`` (a bucket
+    is a run of consecutive factors, the same on every rank, so every pair of
+    ranks posts its sends and receives in the same order) as one
+    ``batch_isend_irecv`` each, and the bucket's merges as one batched fold.  In
+    bf16 mode only the meaningful rows of a factor are sent (the fold keeps the
+    rows past a factor's count zero); fp32 mode sends the whole factor, which is
+    folded whole like :func:`fold_merge` does.
+
+    Returns (meaningful rows, total data rows) of every merged factor, the same on
+    every rank.  A failed collective raises; the buffers may then hold partial
+    merges, so the caller drops them (``DistributedIFKFAC`` clears its running
+    factors)."""
+    from . import _lib
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    nf = len(items)
+    if len(owners) != nf:
+        raise ValueError("rtree_reduce_many needs one owner per factor")
+    for R, _, _, _ in items:
+        if R.dim() != 2 or R.shape[0] != R.shape[1] or not R.is_contiguous():
+            raise ValueError("rtree_reduce_many expects contiguous n x n factor buffers")
+    if nf == 0:
+        return []
+    dev = items[0][0].device
+    ns = [R.shape[1] for R, _, _, _ in items]
+    counts = torch.tensor([[min(n, int(r)), int(s)] for n, (_, r, s, _) in zip(ns, items)],
+                          dtype=torch.int64, device=dev)
+    allc = torch.empty(world, nf, 2, dtype=torch.int64, device=dev)
+    dist.all_gather(list(allc.unbind(0)), counts, group=group)
+    c = allc.cpu().tolist()  # c[rank][factor] = [rows, rows_seen]
+    results = [(min(ns[f], sum(c[q][f][0] for q in range(world))), sum(c[q][f][1] for q in range(world)))
+               for f in range(nf)]
+    if world == 1:
+        return results
+    cur = [min(ns[f], c[rank][f][0]) for f in range(nf)]
+    active = [True] * nf
+    # buckets: runs of consecutive factors of at most bucket_bytes (the same on every rank)
+    buckets, lo, acc = [], 0, 0
+    for f in range(nf):
+        b = ns[f] * ns[f] * 4
+        if f > lo and acc + b > bucket_bytes:
+            buckets.append((lo, f))
+            lo, acc = f, 0
+        acc += b
+    buckets.append((lo, nf))
+    s = 1
+    while s < world:
+        plan = [None] * nf  # ('recv', partner, rows_b) or ('send', dst)
+        for f in range(nf):
+            if not active[f]:
+                continue
+            rel = (rank - owners[f]) % world
+            if rel % (2 * s) == 0:
+                prel = rel + s
+                if prel < world:
+                    rb = min(ns[f], sum(c[(owners[f] + q) % world][f][0] for q in range(prel, min(world, prel + s))))
+                    if rb > 0:
+                        plan[f] = ("recv", (owners[f] + prel) % world, rb)
+            else:  # rel mod 2s == s: hand the subtree's factor on and leave the tree
+                active[f] = False
+                if cur[f] > 0:
+                    plan[f] = ("send", (owners[f] + rel - s) % world)
+        for lo, hi in buckets:
+            ops, jobs = [], []
+            for f in range(lo, hi):
+                p = plan[f]
+                if p is None:
+                    continue
+                R, _, _, prec = items[f]
+                if p[0] == "recv":
+                    nrows = p[2] if prec == _lib.PREC_BF16 else ns[f]
+                    buf = torch.empty(nrows, ns[f], dtype=R.dtype, device=dev)
+                    ops.append(dist.P2POp(dist.irecv, buf, _global_rank(group, p[1]), group))
+                    jobs.append((f, buf, p[2]))
+                else:
+                    nrows = cur[f] if prec == _lib.PREC_BF16 else ns[f]
+                    ops.append(dist.P2POp(dist.isend, R[:nrows], _global_rank(group, p[1]), group))
+            if ops:
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()
+            if jobs:
+                merge_many([(items[f][0], cur[f], buf, rb, items[f][3]) for f, buf, rb in jobs])
+                for f, _, rb in jobs:
+                    cur[f] = min(ns[f], cur[f] + rb)
+        s *= 2
+    return results
+
+
 def merge_running(factor: triangular.RunningFactor,
                   group: Optional[dist.ProcessGroup] = None) -> None:
     """rtree_merge on a RunningFactor, in place (R, rows_R and rows_seen)."""
@@ -178,10 +318,13 @@ class DistributedIFKFAC:
     their solves.
 
     * Each rank's hooks fold that rank's rows (batch-sharded streaming TSQR).
-    * At a refresh every layer's running factors are merged across ranks by the
-      R-tree (:func:`rtree_merge`, the merge order of ``ifkfac/triangular.py:207-220``),
-      so every rank finalizes the factors of all rows (and the row counts of all
-      ranks scale them).
+    * At a refresh every layer's running factors are reduced across ranks to the
+      layer's owner by the R-tree (:func:`rtree_reduce_many`: the merge order of
+      ``ifkfac/triangular.py:207-220`` over ranks relabelled from the owner; the
+      exchanges of all factors of a round batched in buckets of ``bucket_bytes``,
+      their merges in batched folds), and the owner finalizes them (the row counts
+      of all ranks scale them).  Other ranks keep no factors of that layer: it is
+      solved on its owner only.
     * Gradients of the preconditioned layers are averaged across ranks (one
       ``all_reduce`` of a flat buffer) unless ``average_gradients=False`` (the
       caller already averages, e.g. under DDP).
@@ -204,10 +347,12 @@ class DistributedIFKFAC:
     collective."""
 
     def __init__(self, model, *args, group: Optional[dist.ProcessGroup] = None,
-                 average_gradients: bool = True, delta_scale: Optional[float] = None, **kwargs):
+                 average_gradients: bool = True, delta_scale: Optional[float] = None,
+                 bucket_bytes: int = 1 << 30, **kwargs):
         from .ifkfac import IFKFAC
         self.opt = IFKFAC(model, *args, **kwargs)
         self.group = group
+        self.bucket_bytes = int(bucket_bytes)
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.average_gradients = average_gradients
@@ -234,6 +379,7 @@ class DistributedIFKFAC:
         dist.all_gather(list(allw.unbind(0)), mine, group=self.group)
         width = allw.max(0).values.cpu().tolist()
         from .engine import Factor
+        entries = []  # (layer, 0 for X / 1 for delta, factor, row-count table)
         for li, m in enumerate(layers):
             for ti, (table, nrows) in enumerate(((h._fx, h._n_rows_X), (h._fg, h._n_rows_G))):
                 n = int(width[li][ti])
@@ -242,15 +388,23 @@ class DistributedIFKFAC:
                 f = table[m]
                 if f is None:
                     f = table[m] = Factor(n, dev, h.precision)
-                got = merge_or_skip(f.R, f.rows_R, f.rows_seen, self.group,
-                                    merge=lambda a, ra, b, rb, p=f.prec: fold_merge(a, ra, b, rb, p))
-                if got is None:
-                    return False
-                rows, total = got
-                f.rows_R, f.rows_seen = rows, total
-                nrows[m] = total
-                if ti == 1 and self.delta_scale != 1.0:
-                    f.R.mul_(self.delta_scale)  # R^T R scales with the square of the rows
+                entries.append((m, ti, f, nrows))
+        try:
+            got = rtree_reduce_many([(f.R, f.rows_R, f.rows_seen, f.prec) for _, _, f, _ in entries],
+                                    [self.owner[m] for m, _, _, _ in entries], self.group,
+                                    bucket_bytes=self.bucket_bytes)
+        except (RuntimeError, dist.DistError) as e:  # timeouts and lost peers surface as these
+            logger.warning("IFKFAC: R-tree merge failed (%s); factor update skipped", e)
+            return False
+        for (m, ti, f, nrows), (rows, total) in zip(entries, got):
+            if self.owner[m] != self.rank:
+                # not this rank's layer: its factors are finalised by the owner only
+                f.rows_seen = 0
+                continue
+            f.rows_R, f.rows_seen = rows, total
+            nrows[m] = total
+            if ti == 1 and self.delta_scale != 1.0:
+                f.R.mul_(self.delta_scale)  # R^T R scales with the square of the rows
         return True
 
     def _average_gradients(self, params) -> None:

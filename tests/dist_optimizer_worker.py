@@ -1,6 +1,7 @@
 """Worker of tests/test_gpu_distributed_optimizer.py, run under torch.distributed.run
 with one rank per GPU: DistributedIFKFAC on batch shards against IFKFAC on the
-full batch in one process (rank 0), and the ranks' parameters against each other.
+full batch in one process (on every rank: each owner checks its layers' factors),
+and the ranks' parameters against each other.
 Prints one JSON line on rank 0."""
 import datetime
 import json
@@ -46,22 +47,28 @@ def main():
     every = [torch.empty_like(flat) for _ in range(world)]
     dist.all_gather(every, flat)
     same = all(torch.equal(every[0], e) for e in every)
+    # the single-process reference on every rank; each rank checks the factors of its own layers
+    ref = make_model(dev)
+    opt = IFKFAC(ref, **kw)
+    for _ in range(steps):
+        opt.zero_grad()
+        F.cross_entropy(ref(X), Y).backward()
+        opt.step()
+    torch.cuda.synchronize()
+    mine = [(m, r) for m, r in zip(dopt.hooks.linear_layers, opt.hooks.linear_layers) if dopt.owner[m] == rank]
+    ferr = max([float((dopt._factors[m][i].float() - opt._factors[r][i].float()).norm()
+                      / opt._factors[r][i].float().norm()) for m, r in mine for i in (0, 1)] + [0.0])
+    held = sorted(m_i for m_i, m in enumerate(dopt.hooks.linear_layers) if m in dopt._factors)
+    owned = sorted(m_i for m_i, m in enumerate(dopt.hooks.linear_layers) if dopt.owner[m] == rank)
+    t = torch.tensor([ferr, float(held != owned)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
     if rank == 0:
-        ref = make_model(dev)
-        opt = IFKFAC(ref, **kw)
-        for _ in range(steps):
-            opt.zero_grad()
-            F.cross_entropy(ref(X), Y).backward()
-            opt.step()
-        torch.cuda.synchronize()
         werr = max(float((a - b).norm() / b.norm()) for a, b in zip(model.parameters(), ref.parameters()))
-        ferr = max(float((dopt._factors[m][i].float() - opt._factors[r][i].float()).norm()
-                         / opt._factors[r][i].float().norm())
-                   for m, r in zip(dopt.hooks.linear_layers, opt.hooks.linear_layers) for i in (0, 1))
         owners = sorted(set(dopt.owner.values()))
-        print(json.dumps({"same_on_ranks": same, "weight_rel_err": werr, "factor_rel_err": ferr,
-                          "owners": owners, "world": world}), flush=True)
-        opt.cleanup()
+        print(json.dumps({"same_on_ranks": same, "weight_rel_err": werr, "factor_rel_err": float(t[0]),
+                          "factors_on_owners_only": float(t[1]) == 0.0, "owners": owners, "world": world}),
+              flush=True)
+    opt.cleanup()
     dopt.cleanup()
     dist.barrier()
     dist.destroy_process_group()

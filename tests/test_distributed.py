@@ -125,6 +125,67 @@ def test_fold_merge_on_device_matches_oracle_tsqr():
     assert nrows == n and err < 1e-5, err
 
 
+def _factor_data(rank, f, n):
+    rng = np.random.default_rng(1000 + 17 * f + rank)
+    s = np.exp(rng.uniform(0, np.log(100.0), n))
+    return rng.standard_normal(((_rows_for(rank) + 5 * f) % 45, n)) * s
+
+
+def _oracle_merge_many(jobs):
+    for Ra, ra, Rb, rb, _ in jobs:
+        n = Ra.shape[1]
+        k = min(rb, n)
+        if k == 0:
+            continue
+        stacked = np.concatenate([Ra[:ra].numpy(), Rb[:k].numpy()], 0)
+        r = ora.positive_diagonal_R(ora._qr_r(stacked))
+        Ra.zero_()
+        Ra[: r.shape[0]] = torch.from_numpy(r)
+
+
+MANY_N = [24, 24, 10, 24, 16]
+
+
+def _reduce_many_worker(rank, world, port, outdir, prec):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        items = []
+        for f, n in enumerate(MANY_N):
+            X = _factor_data(rank, f, n)
+            R = np.zeros((n, n))
+            if X.shape[0]:
+                r = ora.positive_diagonal_R(ora._qr_r(X))
+                R[: r.shape[0]] = r
+            items.append((torch.from_numpy(R), min(n, X.shape[0]), X.shape[0], prec))
+        owners = [f % world for f in range(len(MANY_N))]
+        owners[-1] = world - 1
+        # small buckets: the exchanges of a round go in several batches
+        got = D.rtree_reduce_many(items, owners, merge_many=_oracle_merge_many, bucket_bytes=2 * 24 * 24 * 8)
+        for f, (R, _, _, _) in enumerate(items):
+            if owners[f] == rank:
+                np.save(os.path.join(outdir, f"m{f}.npy"), R.numpy())
+        np.save(os.path.join(outdir, f"g{rank}.npy"), np.array(got))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,prec", [(2, 1), (3, 2), (5, 2)])
+def test_rtree_reduce_many_gloo_reduces_every_factor_to_its_owner(tmp_path, world, prec):
+    # prec 2 (bf16 mode) sends only the meaningful rows of a factor, 1 (fp32 mode) the whole factor
+    mp.spawn(_reduce_many_worker, args=(world, _free_port(), str(tmp_path), prec), nprocs=world, join=True)
+    gots = [np.load(tmp_path / f"g{r}.npy") for r in range(world)]
+    for r in range(world):
+        np.testing.assert_array_equal(gots[r], gots[0])  # the same counts on every rank
+    for f, n in enumerate(MANY_N):
+        allX = np.concatenate([_factor_data(r, f, n) for r in range(world)], 0)
+        assert list(gots[0][f]) == [min(n, allX.shape[0]), allX.shape[0]]
+        ref = ora.positive_diagonal_R(ora._qr_r(allX))
+        got = np.load(tmp_path / f"m{f}.npy")
+        np.testing.assert_allclose(got[: ref.shape[0]], ref, rtol=0, atol=1e-9 * np.abs(ref).max())
+
+
 def _silent_rank_worker(rank, world, port, outdir):
     """Rank 1 never posts its factor (it does not enter the merge); the others must
     give up within the process group's timeout and keep their local factor."""

@@ -1,8 +1,9 @@
-"""DistributedIFKFAC on two GPUs (NCCL): batch-sharded TSQR merged by the R-tree at
-each refresh, gradients averaged, each layer's solves and update on its owner
-rank and broadcast.  Against IFKFAC on the full batch in one process: the same
-factors and trajectory up to the merge order of the rows (fp32 mode 1e-4; bf16
-mode within its 2e-2 bound), and bit-identical parameters on every rank.
+"""DistributedIFKFAC on two GPUs (NCCL): batch-sharded TSQR reduced by the R-tree to
+each layer's owner at each refresh, gradients averaged, each layer's solves and
+update on its owner rank and broadcast.  Against IFKFAC on the full batch in one
+process: the same factors (on the owners, the only ranks that hold them) and
+trajectory up to the merge order of the rows (fp32 mode 1e-4; bf16 mode within its
+2e-2 bound), and bit-identical parameters on every rank.
 Skipped with fewer than two GPUs."""
 import json
 import os
@@ -36,5 +37,5 @@ def test_distributed_optimizer_matches_single_process(prec, tol):
     assert r.returncode == 0, r.stderr[-3000:]
     line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
     out = json.loads(line)
-    assert out["same_on_ranks"] and out["owners"] == [0, 1]
+    assert out["same_on_ranks"] and out["owners"] == [0, 1] and out["factors_on_owners_only"]
     assert out["factor_rel_err"] < tol and out["weight_rel_err"] < tol, out
