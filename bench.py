@@ -1021,8 +1021,10 @@ def run_c5(args, rank, world, local_rank):
     RMSNorm; no rotary embedding, which does not change a K-FAC shape), random init,
     bf16 autocast, sequences of 2048 uniform random token ids.  K-FAC on the 112 Linear
     layers of the blocks (q, k, v, o, gate, up, down), use_true_bf16, damping 1e-3,
-    factor_update_freq 20, the reference's default 2048 rows per layer and step
-    (max_seq_rows None), batched_qr.  A step is forward + backward + the optimizer step.
+    factor_update_freq 20, batched_qr; every token's rows (max_seq_rows = 0: p = 32768
+    rows per layer and step on 8 GPUs, as config 5 states), or with ``--c5-rows 2048``
+    the reference's default cap of 2048 rows per layer and step (max_seq_rows None).
+    A step is forward + backward + the optimizer step.
 
     Data-parallel over the ranks (config 5 as stated: batch 16 = 32768 tokens on 8
     GPUs, i.e. 2 sequences per GPU): each rank runs ``--c5-batch`` sequences of its
@@ -1082,7 +1084,8 @@ def run_c5(args, rank, world, local_rank):
     g = torch.Generator(device=dev).manual_seed(1000 + rank)  # each rank its own batch shard
     idx = torch.randint(0, vocab, (batch, seq + 1), generator=g, device=dev)
     x, y = idx[:, :-1], idx[:, 1:]
-    kw = dict(lr=1e-4, damping=1e-3, factor_update_freq=20, momentum=0.9, use_true_bf16=True, batched_qr=True)
+    kw = dict(lr=1e-4, damping=1e-3, factor_update_freq=20, momentum=0.9, use_true_bf16=True, batched_qr=True,
+              max_seq_rows=0 if args.c5_rows == "all" else None)
     opt = DistributedIFKFAC(model, **kw) if world > 1 else IFKFAC(model, **kw)
 
     def one():
@@ -1126,8 +1129,10 @@ def run_c5(args, rank, world, local_rank):
                "warmup": warm, "ms_per_step": ms, "steps_per_s": 1000.0 / ms, "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                "config": {"workload": "C5 Llama-1B-shaped decoder, 16 x (q, k, v, o, gate, up, down) under "
-                                      "K-FAC, 2048 rows per layer and step, bf16 autocast, use_true_bf16, "
-                                      "damping 1e-3, factor_update_freq 20, batched_qr",
+                                      "K-FAC, " + ("every token's rows" if args.c5_rows == "all" else
+                                                   "2048 rows per layer, rank and step") +
+                                      ", bf16 autocast, use_true_bf16, damping 1e-3, factor_update_freq 20, batched_qr",
+                          "rows_per_layer_per_step": (world * batch * seq if args.c5_rows == "all" else world * 2048),
                           "sequences_per_gpu": batch, "seq_len": seq, "global_batch": world * batch,
                           "parallelism": ("single GPU" if world == 1 else
                                           f"data parallel over {world} GPUs: TSQR batch-sharded, R-tree to the "
@@ -1365,6 +1370,9 @@ def main():
                          "laplace: K-FAC Laplace draws")
     ap.add_argument("--c5-batch", type=int, default=2,
                     help="c5: sequences of 2048 tokens per GPU (config 5: 16 on 8 GPUs, i.e. 2 per GPU)")
+    ap.add_argument("--c5-rows", choices=["all", "2048"], default="all",
+                    help="c5: fold every token's rows (config 5: p = 32768 on 8 GPUs) or the reference's "
+                         "default cap of 2048 rows per layer and step")
     ap.add_argument("--c3-batched-qr", action="store_true",
                     help="c3: IFKFAC(batched_qr=True): the step's chunks of every layer folded together")
     ap.add_argument("--c3-per-layer-apply", action="store_true", help="c3: time only the per-layer apply")
