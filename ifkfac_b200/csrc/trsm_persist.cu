@@ -255,18 +255,24 @@ __global__ void __launch_bounds__(INV_TPB) diag_inverse_layout_kernel(const __gr
     U[r][l] = v;
   }
   __syncthreads();
-  // Column q of U^-1 by back substitution.  The four lanes of a column (one warp
-  // quad) each sum a residue class of the row's products, and two shuffles add
-  // the partial sums: the dependency from row r to row r - 1 stays inside the warp.
+  // Column q of U^-1 by column-oriented back substitution: the four lanes of a
+  // column (one warp quad) hold the residues of its rows l = 4k + part in
+  // registers; once x_r = res_r / U[r][r] is known (a shuffle from the lane of
+  // row r), every lane folds it into the residues of its rows above r.  A step
+  // is one shuffle, one divide and independent FMAs, so the chain from row r to
+  // row r - 1 is short; the U[l][r] reads of a warp hit four consecutive banks.
   {
-    const int q = t >> 2, part = t & 3;
+    const int q = t >> 2, part = t & 3, lane = t & 31;
+    float res[NB2 / 4];
+#pragma unroll
+    for (int k = 0; k < NB2 / 4; ++k) res[k] = (4 * k + part == q) ? 1.f : 0.f;
+#pragma unroll
     for (int r = NB2 - 1; r >= 0; --r) {
-      float acc = (part == 0 && r == q) ? 1.f : 0.f;
-      for (int l = r + 1 + part; l < NB2; l += 4) acc -= U[r][l] * Xs[l][q];
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (part == 0) Xs[r][q] = acc / U[r][r];
-      __syncwarp();
+      const float x = __shfl_sync(0xffffffffu, res[r >> 2], (lane & ~3) | (r & 3)) / U[r][r];
+      if (part == (r & 3)) Xs[r][q] = x;
+#pragma unroll
+      for (int k = 0; k <= (r >> 2); ++k)
+        if (4 * k + part < r) res[k] = fmaf(-U[4 * k + part][r], x, res[k]);
     }
   }
   __syncthreads();
