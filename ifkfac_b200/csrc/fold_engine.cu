@@ -107,8 +107,8 @@ constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
 enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2, XK_CONV = 8 };
 
 #ifdef IFK_TRACE
-// Diagnostic build only: per-task timestamps (globaltimer, ns), 24 int64 per task.
-constexpr int TRN = 24;
+// Diagnostic build only: per-task timestamps (globaltimer, ns), 26 int64 per task.
+constexpr int TRN = 26;
 __device__ long long g_trace[(1 << 14) * TRN];
 __device__ int g_trace_n;
 __device__ __forceinline__ long long gtime() {
@@ -124,6 +124,11 @@ __device__ long long g_wait_ns[1024];
 #define WT_BEGIN const long long wt0_ = gtime();
 #define WT_END g_wait_ns[blockIdx.x & 1023] += gtime() - wt0_;
 #define TR_WAIT() g_wait_ns[blockIdx.x & 1023]
+// nanoseconds thread 0 of each CTA spent in the leaf hooks of the own panels, waits excluded
+__device__ long long g_hook_ns[1024];
+#define HK_BEGIN const long long hk0_ = threadIdx.x == 0 ? gtime() - TR_WAIT() : 0;
+#define HK_END if (threadIdx.x == 0) g_hook_ns[blockIdx.x & 1023] += gtime() - TR_WAIT() - hk0_;
+#define TR_HOOK() g_hook_ns[blockIdx.x & 1023]
 #define TR_FLUSH()                                                     \
   if (threadIdx.x == 0) {                                              \
     const int slot = atomicAdd(&g_trace_n, 1);                         \
@@ -139,6 +144,9 @@ __device__ long long g_wait_ns[1024];
 #define WT_BEGIN
 #define WT_END
 #define TR_WAIT() 0
+#define HK_BEGIN
+#define HK_END
+#define TR_HOOK() 0
 #endif
 
 #ifdef IFK_TRACE
@@ -298,6 +306,7 @@ struct FoldLeafHook {
   int* s_ok;
   template <class SM>
   __device__ __forceinline__ bool before_leaf(SM& S, int s) {
+    HK_BEGIN
     if (prev_prog && !cta_wait_ge(prev_prog, stage0 + s, *b, s_ok)) return false;
     const int L0 = s * panel::LEAF;
     for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
@@ -305,16 +314,19 @@ struct FoldLeafHook {
       S.Rk[i * LDP + j] = (i < nbk && j < nbk && j >= i) ? R[(c0 + i) * ldR + c0 + j] : 0.f;
     }
     __syncthreads();
+    HK_END
     return true;
   }
   template <class SM>
   __device__ __forceinline__ void after_leaf(SM& S, int s) {
+    HK_BEGIN
     const int L0 = s * panel::LEAF;
     for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
       const int i = L0 + idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) R[(c0 + i) * ldR + c0 + j] = S.Rk[i * LDP + j];
     }
     cta_publish_value(prog, stage0 + s);
+    HK_END
   }
 };
 
@@ -681,6 +693,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   TR_SET(2, cb);
   TR_SET(3, TR_NOW());
   TR_SET(20, TR_WAIT());
+  TR_SET(24, TR_HOOK());
   const int tid = threadIdx.x, warp = tid >> 5;
   int si = 0;  // segment of sub-tile t
   const PSeg* SG = b.seg + F.seg0;
@@ -927,6 +940,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
   cta_publish_value(prog, stage_done(F.K));
   TR_SET(7, TR_NOW());
   TR_SET(22, TR_WAIT());
+  TR_SET(25, TR_HOOK());
   TR_FLUSH();
 }
 
