@@ -116,12 +116,32 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
   }
 }
 
-constexpr int LDW = WC + 1;
+// Shared-memory row strides of the fp32 trailing update: 16-byte aligned rows, so
+// that the tiles arrive by 16-byte cp.async copies and are read as float4.
+// Every read pattern of the update touches at most two distinct rows of Y and
+// Ts per warp (broadcasts) or one contiguous row of Xb / W, so the padding only
+// has to keep the rows aligned.
+constexpr int LDS = NB + 4;   // Y and Ts rows
+constexpr int LDWS = WC + 4;  // Xb and W rows
+static_assert(NB == 64 && WC == 64 && SUB == 256 && PT == 256, "the update's thread tiles");
+constexpr int UCH = 4;  // row chunks of the tiles' copies (GEMM1 starts on the first)
 constexpr size_t upd_smem_bytes() {
-  return sizeof(float) * ((size_t)SUB * LDP + (size_t)SUB * LDW + (size_t)NB * LDW + (size_t)NB * LDP);
+  return sizeof(float) * ((size_t)SUB * LDS + (size_t)SUB * LDWS + (size_t)NB * LDWS + (size_t)NB * LDS);
 }
 
-// fp32 trailing update of one (sub-tile, panel, column block) per block.
+// 16 bytes global -> shared, the bytes past `valid` floats zero-filled (valid 0..4)
+__device__ __forceinline__ void cp16(float* dst, const float* src, int valid, const float* dummy) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(valid > 0 ? src : dummy),
+               "r"(valid * 4)
+               : "memory");
+}
+
+// fp32 trailing update of one (sub-tile, panel, column block) per block:
+//   W = Y^T X_t[:, cols] + R[k rows, cols];  W2 = T^T W;  R[k rows, cols] -= W2;
+//   X_t[:, cols] -= Y W2.
+// The tiles come by cp.async in UCH row chunks, so the first GEMM starts while
+// the later chunks are in flight; all reads of shared memory are float4.
 __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int wave) {
   const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
@@ -131,111 +151,152 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
   const int64_t cs = (int64_t)blockIdx.y * WC;
   if (cs < c0 + NB || cs >= a.n) return;
 
-  extern __shared__ float sm[];
-  float* Y = sm;                 // SUB x LDP
-  float* Xb = Y + SUB * LDP;     // SUB x LDW
-  float* W = Xb + SUB * LDW;     // NB x LDW
-  float* Ts = W + NB * LDW;      // NB x LDP: Ts[i][l] = T[l][i]
+  extern __shared__ __align__(16) float sm[];
+  float* Y = sm;                 // SUB x LDS: the panel's Y
+  float* Xb = Y + SUB * LDS;     // SUB x LDWS: the sub-tile's columns cs ..
+  float* W = Xb + SUB * LDWS;    // NB x LDWS
+  float* Ts = W + NB * LDWS;     // NB x LDS: Ts[i][l] = T[l][i]
 
   const int tid = threadIdx.x;
   const int64_t row0 = (int64_t)t * SUB;
   const int h = (int)mn<int64_t>(SUB, a.rows - row0);
   const int nbk = (int)mn<int64_t>(NB, a.n - c0);
   const int wc = (int)mn<int64_t>(WC, a.n - cs);
-  const float* Tb = a.Tb + (size_t)t * NB * NB;
+  const float* Tb = a.Tb + (size_t)t * NB * NB;  // column-major: Tb[i*NB + l] = T[l][i]
 
-  for (int idx = tid; idx < SUB * NB; idx += PT) {
-    const int i = idx / NB, j = idx % NB;
-    Y[i * LDP + j] = (i < h && j < nbk) ? a.X[(row0 + i) * a.ldX + c0 + j] : 0.f;
+  // copies: Ts with the first chunk, then SUB / UCH rows of Y and Xb per group
+  for (int q = tid; q < NB * NB / 4; q += PT) {
+    const int i = q >> 4, l4 = (q & 15) * 4;
+    cp16(Ts + i * LDS + l4, Tb + i * NB + l4, 4, Tb);
   }
-  for (int idx = tid; idx < SUB * WC; idx += PT) {
-    const int i = idx / WC, j = idx % WC;
-    Xb[i * LDW + j] = (i < h && j < wc) ? a.X[(row0 + i) * a.ldX + cs + j] : 0.f;
+#pragma unroll
+  for (int ch = 0; ch < UCH; ++ch) {
+    for (int q = tid; q < (SUB / UCH) * (NB / 4); q += PT) {
+      const int i = ch * (SUB / UCH) + (q >> 4), j4 = (q & 15) * 4;
+      const int vy = i < h ? mx<int>(0, mn<int>(4, nbk - j4)) : 0;
+      const int vx = i < h ? mx<int>(0, mn<int>(4, wc - j4)) : 0;
+      const float* rowp = a.X + (row0 + i) * a.ldX;
+      cp16(Y + i * LDS + j4, rowp + c0 + j4, vy, a.X);
+      cp16(Xb + i * LDWS + j4, rowp + cs + j4, vx, a.X);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  for (int idx = tid; idx < NB * NB; idx += PT) {
-    const int i = idx / NB, l = idx % NB;  // Tb column-major: Tb[i*NB + l] = T[l][i]
-    Ts[i * LDP + l] = Tb[i * NB + l];
-  }
-  __syncthreads();
 
-  const int ty = tid / 16, tx = tid % 16;
+  const int ty = tid >> 4, tx = tid & 15;
+  // ---- W = Y^T Xb (+ R rows): thread (ty, tx) owns W[ty*4 .. +3][tx*4 .. +3] ----
   float acc[4][4];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
-  for (int kk = 0; kk < h; ++kk) {
-    float av[4], bv[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) av[r] = Y[kk * LDP + ty * 4 + r];
+  for (int ch = 0; ch < UCH; ++ch) {
+    if (ch == 0) asm volatile("cp.async.wait_group 3;" ::: "memory");
+    if (ch == 1) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    if (ch == 2) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    if (ch == 3) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const int k0 = ch * (SUB / UCH), k1 = mn<int>(h, k0 + SUB / UCH);
+#pragma unroll 4
+    for (int kk = k0; kk < k1; ++kk) {
+      const float4 av = *reinterpret_cast<const float4*>(Y + kk * LDS + ty * 4);
+      const float4 bv = *reinterpret_cast<const float4*>(Xb + kk * LDWS + tx * 4);
+      const float ar[4] = {av.x, av.y, av.z, av.w}, bq[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) bv[q] = Xb[kk * LDW + tx * 4 + q];
+      for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
+        for (int q = 0; q < 4; ++q) acc[r][q] = fmaf(ar[r], bq[q], acc[r][q]);
+    }
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < 4; ++r) {
+    const int i = ty * 4 + r;
+    float o[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int i = ty * 4 + r, c = tx * 4 + q;
+      const int c = tx * 4 + q;
       const float rv = (i < nbk && c < wc) ? a.R[(c0 + i) * a.ldR + cs + c] : 0.f;
-      W[i * LDW + c] = acc[r][q] + rv;
+      o[q] = acc[r][q] + rv;
     }
+    *reinterpret_cast<float4*>(W + i * LDWS + tx * 4) = make_float4(o[0], o[1], o[2], o[3]);
+  }
   __syncthreads();
-  // W2 = T^T W
+  // ---- W2 = T^T W; R rows -= W2 ----
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
-  for (int l = 0; l < NB; ++l) {
-    float av[4], bv[4];
+#pragma unroll 2
+  for (int l = 0; l < NB; l += 4) {
+    float4 bw[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) av[r] = Ts[(ty * 4 + r) * LDP + l];
+    for (int u = 0; u < 4; ++u) bw[u] = *reinterpret_cast<const float4*>(W + (l + u) * LDWS + tx * 4);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) bv[q] = W[l * LDW + tx * 4 + q];
+    for (int r = 0; r < 4; ++r) {
+      const float4 tv = *reinterpret_cast<const float4*>(Ts + (ty * 4 + r) * LDS + l);
+      const float tl[4] = {tv.x, tv.y, tv.z, tv.w};
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
+      for (int u = 0; u < 4; ++u) {
+        acc[r][0] = fmaf(tl[u], bw[u].x, acc[r][0]);
+        acc[r][1] = fmaf(tl[u], bw[u].y, acc[r][1]);
+        acc[r][2] = fmaf(tl[u], bw[u].z, acc[r][2]);
+        acc[r][3] = fmaf(tl[u], bw[u].w, acc[r][3]);
+      }
+    }
   }
-  __syncthreads();
+  __syncthreads();  // every thread has read W
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < 4; ++r) {
+    const int i = ty * 4 + r;
+    *reinterpret_cast<float4*>(W + i * LDWS + tx * 4) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int i = ty * 4 + r, c = tx * 4 + q;
-      W[i * LDW + c] = acc[r][q];
+      const int c = tx * 4 + q;
       if (i < nbk && c < wc) a.R[(c0 + i) * a.ldR + cs + c] -= acc[r][q];
     }
+  }
   __syncthreads();
-  // X_t[:, cols] -= Y W2 ; thread (ty, tx): rows ty*16.., cols tx*4..
+  // ---- X_t[:, cols] -= Y W2; thread (ty, tx): rows ty*16 .. +15, columns tx*4 .. +3 ----
   float acc2[16][4];
 #pragma unroll
   for (int r = 0; r < 16; ++r)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc2[r][q] = 0.f;
-  for (int l = 0; l < NB; ++l) {
-    float bv[4];
+#pragma unroll 1
+  for (int l = 0; l < NB; l += 4) {
+    float4 bw[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) bv[q] = W[l * LDW + tx * 4 + q];
+    for (int u = 0; u < 4; ++u) bw[u] = *reinterpret_cast<const float4*>(W + (l + u) * LDWS + tx * 4);
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      const float av = Y[(ty * 16 + r) * LDP + l];
+      const float4 yv = *reinterpret_cast<const float4*>(Y + (ty * 16 + r) * LDS + l);
+      const float yl[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc2[r][q] += av * bv[q];
+      for (int u = 0; u < 4; ++u) {
+        acc2[r][0] = fmaf(yl[u], bw[u].x, acc2[r][0]);
+        acc2[r][1] = fmaf(yl[u], bw[u].y, acc2[r][1]);
+        acc2[r][2] = fmaf(yl[u], bw[u].z, acc2[r][2]);
+        acc2[r][3] = fmaf(yl[u], bw[u].w, acc2[r][3]);
+      }
     }
   }
+  const bool full = tx * 4 + 4 <= wc;
 #pragma unroll
-  for (int r = 0; r < 16; ++r)
+  for (int r = 0; r < 16; ++r) {
+    const int i = ty * 16 + r;
+    if (i >= h) continue;
+    const float4 xv = *reinterpret_cast<const float4*>(Xb + i * LDWS + tx * 4);
+    const float o[4] = {xv.x - acc2[r][0], xv.y - acc2[r][1], xv.z - acc2[r][2], xv.w - acc2[r][3]};
+    float* dst = a.X + (row0 + i) * a.ldX + cs + tx * 4;
+    if (full) {
+      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = ty * 16 + r, c = tx * 4 + q;
-      if (i < h && c < wc) a.X[(row0 + i) * a.ldX + cs + c] = Xb[i * LDW + c] - acc2[r][q];
+      for (int q = 0; q < 4; ++q)
+        if (tx * 4 + q < wc) dst[q] = o[q];
     }
+  }
 }
-
 template <typename Tin>
 __global__ void copy_chunk_kernel(float* X, int64_t ldX, const Tin* src, int64_t lds, int64_t rows,
                                   int64_t n, const int64_t* ridx, int64_t src_rows, int64_t cols,
