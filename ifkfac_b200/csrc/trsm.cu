@@ -37,11 +37,15 @@ __global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ld
   const int nb = (int)mn<int64_t>(NS, n - b0);
   const int nc = (int)mn<int64_t>(NRHS, N - c0);
   for (int idx = tid; idx < NS * NS; idx += NRHS) {
-    const int i = idx / NS, j = idx % NS;
+    // A's contiguous index fastest across threads: j for op = A, i for op = A^T
+    const int i = trans ? idx % NS : idx / NS, j = trans ? idx / NS : idx % NS;
     Ad[i][j] = (i < nb && j < nb) ? opA(A, ldA, trans, b0 + i, b0 + j) : (i == j ? 1.f : 0.f);
   }
+  // B's contiguous index varies fastest across threads: the columns of a row-major
+  // view, the rows of a transposed one (rs == 1), so the tile loads coalesce
+  const bool tv = rs == 1 && cs != 1;
   for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
-    const int i = idx / NRHS, j = idx % NRHS;
+    const int i = tv ? idx % NS : idx / NRHS, j = tv ? idx / NS : idx % NRHS;
     Bs[i][j] = (i < nb && j < nc) ? B[(b0 + i) * rs + (c0 + j) * cs] : 0.f;
   }
   __syncthreads();
@@ -61,7 +65,7 @@ __global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ld
   }
   __syncthreads();
   for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
-    const int i = idx / NRHS, j = idx % NRHS;
+    const int i = tv ? idx % NS : idx / NRHS, j = tv ? idx / NS : idx % NRHS;
     if (i < nb && j < nc) B[(b0 + i) * rs + (c0 + j) * cs] = Bs[i][j];
   }
 }
@@ -83,22 +87,29 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
   const int ns = (int)mn<int64_t>(NS, n - s0);
   const int nc = (int)mn<int64_t>(NRHS, N - c0);
   for (int idx = tid; idx < NS * NS; idx += 256) {
-    const int i = idx / NS, l = idx % NS;
+    // A's contiguous index fastest across threads: l for op = A, i for op = A^T
+    const int i = trans ? idx % NS : idx / NS, l = trans ? idx / NS : idx % NS;
     As[i][l] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
   }
+  // B's contiguous index varies fastest across threads (see trsm_diag_kernel):
+  // the tile loads and the read-modify-writes of the result coalesce
+  const bool tv = rs == 1 && cs != 1;
   for (int idx = tid; idx < NS * NRHS; idx += 256) {
-    const int l = idx / NRHS, c = idx % NRHS;
+    const int l = tv ? idx % NS : idx / NRHS, c = tv ? idx / NS : idx % NRHS;
     Xs[l][c] = (l < ns && c < nc) ? B[(s0 + l) * rs + (c0 + c) * cs] : 0.f;
   }
   __syncthreads();
+  // thread tile: rows ri .. ri + 3, columns ci .. ci + 3 of the result, the
+  // contiguous one taken from the lane index
   const int ty = tid / 16, tx = tid % 16;
+  const int ri = (tv ? tx : ty) * 4, ci = (tv ? ty : tx) * 4;
   float acc[4][4] = {};
   for (int l = 0; l < NS; ++l) {
     float av[4], bv[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) av[r] = As[ty * 4 + r][l];
+    for (int r = 0; r < 4; ++r) av[r] = As[ri + r][l];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) bv[q] = Xs[l][tx * 4 + q];
+    for (int q = 0; q < 4; ++q) bv[q] = Xs[l][ci + q];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int i = ty * 4 + r, c = tx * 4 + q;
+      const int i = ri + r, c = ci + q;
       if (i < nj && c < nc) B[(j0 + i) * rs + (c0 + c) * cs] -= acc[r][q];
     }
 }
