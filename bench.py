@@ -228,7 +228,8 @@ def time_fp32_mode(dev, X, D, gW, W, tiles):
     """The same operator in the fp32 mode (IFK_PREC_FP32, the reference's
     use_true_bf16=False path at its 1e-5 bound): fp32 rows, one fold launch per tile
     (fp32 Householder panels, fp32 trailing updates on the CUDA cores), the damping
-    fold, fp32 factors, fp32 solves and the update.  Eager, CUDA events, one GPU."""
+    fold, fp32 factors, fp32 solves and the update.  Timed as a CUDA graph of the step
+    (CUDA events, one GPU); the component split is one eager step."""
     import torch
     from ifkfac_b200 import _lib
     from ifkfac_b200.engine import LayerCurvature
@@ -236,17 +237,18 @@ def time_fp32_mode(dev, X, D, gW, W, tiles):
     Xf, Df, Wf = X.float(), D.float(), W.clone()
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
-    def step(comp=None):
-        marks = [ev() for _ in range(4)]
-        marks[0].record()
+    def step(comp=None, marked=True):
+        marks = [ev() for _ in range(4)] if marked else None
+        mark = (lambda i: marks[i].record()) if marked else (lambda i: None)
+        mark(0)
         lc.clear()
         for lo, hi in tiles:
             lc.fold(Xf[lo:hi], Df[lo:hi])
-        marks[1].record()
+        mark(1)
         lc.refresh(DAMPING)
-        marks[2].record()
+        mark(2)
         lc.natgrad_update(gW, Wf, LR, MOM)
-        marks[3].record()
+        mark(3)
         if comp is not None:
             marks[3].synchronize()
             comp.update(tsqr_ms=marks[0].elapsed_time(marks[1]), fold_ms=marks[1].elapsed_time(marks[2]),
@@ -256,16 +258,37 @@ def time_fp32_mode(dev, X, D, gW, W, tiles):
     torch.cuda.synchronize()
     comp = {}
     step(comp)
+    # the step captured in a CUDA graph, like the headline's (its fp32 solves are
+    # many short launches); eager if the capture fails
+    graph, timing = None, "eager, CUDA events, one GPU"
+    try:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step(marked=False)
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(g, stream=s):
+            step(marked=False)
+        g.replay()
+        torch.cuda.synchronize()
+        graph, timing = g, "CUDA graph of the step, CUDA events, one GPU (components: one eager step)"
+    except Exception as e:  # noqa: BLE001 - reported in the line
+        timing = f"eager, CUDA events, one GPU (graph capture failed: {type(e).__name__})"
     k = 3
     a, b = ev(), ev()
     a.record()
     for _ in range(k):
-        step()
+        if graph is not None:
+            graph.replay()
+        else:
+            step(marked=False)
     b.record()
     b.synchronize()
     ms = a.elapsed_time(b) / k
     out = {"ms_per_step": ms, "value": 1000.0 / ms, "unit": "steps/s", "dtype": "f32",
-           "timing": "eager, CUDA events, one GPU", "components_ms": comp}
+           "timing": timing, "components_ms": comp}
+    del graph
     del lc, Xf, Df, Wf
     torch.cuda.empty_cache()
     return out
