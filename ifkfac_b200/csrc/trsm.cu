@@ -75,8 +75,10 @@ template <typename TA>
 __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t ldA, int trans,
                                                           float* B, int64_t rs, int64_t cs,
                                                           int64_t n, int64_t N, int64_t s0) {
-  __shared__ float As[NS][NS + 1];
-  __shared__ float Xs[NS][LDS_];
+  // op(A)'s tile transposed (AsT[l][i]) and X's tile, rows 16-byte aligned: the
+  // product loop reads one float4 of each per step
+  __shared__ __align__(16) float AsT[NS][NS + 4];
+  __shared__ __align__(16) float Xs[NS][NRHS + 4];
   const int tid = threadIdx.x;
   // trans (forward): targets are the blocks after s; otherwise the blocks before s.
   const int64_t jb = trans ? (s0 / NS + 1 + blockIdx.x) : blockIdx.x;
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
   for (int idx = tid; idx < NS * NS; idx += 256) {
     // A's contiguous index fastest across threads: l for op = A, i for op = A^T
     const int i = trans ? idx % NS : idx / NS, l = trans ? idx / NS : idx % NS;
-    As[i][l] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
+    AsT[l][i] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
   }
   // B's contiguous index varies fastest across threads (see trsm_diag_kernel):
   // the tile loads and the read-modify-writes of the result coalesce
@@ -104,12 +106,11 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
   const int ty = tid / 16, tx = tid % 16;
   const int ri = (tv ? tx : ty) * 4, ci = (tv ? ty : tx) * 4;
   float acc[4][4] = {};
+#pragma unroll 8
   for (int l = 0; l < NS; ++l) {
-    float av[4], bv[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) av[r] = As[ri + r][l];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) bv[q] = Xs[l][ci + q];
+    const float4 a4 = *reinterpret_cast<const float4*>(&AsT[l][ri]);
+    const float4 b4 = *reinterpret_cast<const float4*>(&Xs[l][ci]);
+    const float av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
