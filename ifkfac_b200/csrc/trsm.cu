@@ -49,20 +49,33 @@ __global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ld
     Bs[i][j] = (i < nb && j < nc) ? B[(b0 + i) * rs + (c0 + j) * cs] : 0.f;
   }
   __syncthreads();
+  // Column c by column-oriented substitution: its residues stay in registers; once
+  // x_r = res_r / op(A)[r][r] is known it is folded into the rows still to come
+  // with independent FMAs (op(A)[l][r] is the same for every column: a broadcast).
+  // Rows past nb are the identity pad and come out zero.
   const int c = tid;
+  float res[NS];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) res[i] = Bs[i][c];
   if (trans) {  // lower: forward
-    for (int r = 0; r < nb; ++r) {
-      float s = Bs[r][c];
-      for (int l = 0; l < r; ++l) s -= Ad[r][l] * Bs[l][c];
-      Bs[r][c] = s / Ad[r][r];
+#pragma unroll
+    for (int r = 0; r < NS; ++r) {
+      const float x = res[r] / Ad[r][r];
+      res[r] = x;
+#pragma unroll
+      for (int l = r + 1; l < NS; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
     }
   } else {  // upper: backward
-    for (int r = nb - 1; r >= 0; --r) {
-      float s = Bs[r][c];
-      for (int l = r + 1; l < nb; ++l) s -= Ad[r][l] * Bs[l][c];
-      Bs[r][c] = s / Ad[r][r];
+#pragma unroll
+    for (int r = NS - 1; r >= 0; --r) {
+      const float x = res[r] / Ad[r][r];
+      res[r] = x;
+#pragma unroll
+      for (int l = 0; l < r; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
     }
   }
+#pragma unroll
+  for (int i = 0; i < NS; ++i) Bs[i][c] = res[i];
   __syncthreads();
   for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
     const int i = tv ? idx % NS : idx / NRHS, j = tv ? idx / NS : idx % NRHS;
@@ -116,13 +129,36 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[r][q] += av[r] * bv[q];
   }
+  // the result's four contiguous elements (the columns of a row-major view, the
+  // rows of a transposed one) by one 16-byte read-modify-write where aligned
+  const int64_t cstride = tv ? rs : cs;  // stride of the contiguous index (1)
+  const bool vec = cstride == 1 && (((uintptr_t)B) & 15) == 0 && ((tv ? cs : rs) & 3) == 0 &&
+                   (((tv ? j0 : c0) & 3) == 0);
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int u = 0; u < 4; ++u) {
+    // u runs over the non-contiguous index of the thread tile
+    const int i0 = tv ? ri : ri + u, cc0 = tv ? ci + u : ci;
+    float* p = B + (j0 + i0) * rs + (c0 + cc0) * cs;
+    const int left = tv ? nj - ri : nc - ci;  // valid contiguous elements from the tile's start
+    const bool inb = tv ? (cc0 < nc) : (i0 < nj);
+    if (!inb) continue;
+    if (vec && left >= 4) {
+      float4 v = *reinterpret_cast<float4*>(p);
+      v.x -= tv ? acc[0][u] : acc[u][0];
+      v.y -= tv ? acc[1][u] : acc[u][1];
+      v.z -= tv ? acc[2][u] : acc[u][2];
+      v.w -= tv ? acc[3][u] : acc[u][3];
+      *reinterpret_cast<float4*>(p) = v;
+    } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = ri + r, c = ci + q;
-      if (i < nj && c < nc) B[(j0 + i) * rs + (c0 + c) * cs] -= acc[r][q];
+      for (int e = 0; e < 4; ++e) {
+        if (e < left) {
+          float* pe = p + (tv ? (int64_t)e * rs : (int64_t)e * cs);
+          *pe -= tv ? acc[e][u] : acc[u][e];
+        }
+      }
     }
+  }
 }
 
 template <typename TA>
