@@ -118,15 +118,17 @@ __global__ void __launch_bounds__(PT2) fold_panel_kernel(FoldBatch fb, int wave)
 
 // Shared-memory row strides of the fp32 trailing update: 16-byte aligned rows, so
 // that the tiles arrive by 16-byte cp.async copies and are read as float4.
-// Every read pattern of the update touches at most two distinct rows of Y and
-// Ts per warp (broadcasts) or one contiguous row of Xb / W, so the padding only
-// has to keep the rows aligned.
-constexpr int LDS = NB + 4;   // Y and Ts rows
-constexpr int LDWS = WC + 4;  // Xb and W rows
+// Every read pattern of the update touches at most four distinct rows of a Y
+// chunk or of Ts per warp (broadcasts) or one contiguous row of an X chunk or
+// of W, so the padding only has to keep the rows aligned.
+constexpr int LDS = NB + 4;   // rows of Y chunks and Ts
+constexpr int LDWS = WC + 4;  // rows of X chunks and W
 static_assert(NB == 64 && WC == 64 && SUB == 256 && PT == 256, "the update's thread tiles");
-constexpr int UCH = 4;  // row chunks of the tiles' copies (GEMM1 starts on the first)
+constexpr int CR = 64;            // rows of a chunk of the sub-tile
+constexpr int NCH = SUB / CR;     // chunks
+constexpr int STAGE = CR * LDS + CR * LDWS;  // floats of one stage: a Y chunk and an X chunk
 constexpr size_t upd_smem_bytes() {
-  return sizeof(float) * ((size_t)SUB * LDS + (size_t)SUB * LDWS + (size_t)NB * LDWS + (size_t)NB * LDS);
+  return sizeof(float) * ((size_t)2 * STAGE + (size_t)NB * LDWS + (size_t)NB * LDS);
 }
 
 // 16 bytes global -> shared, the bytes past `valid` floats zero-filled (valid 0..4)
@@ -137,12 +139,31 @@ __device__ __forceinline__ void cp16(float* dst, const float* src, int valid, co
                : "memory");
 }
 
+// Rows m*CR .. of Y (panel columns c0 ..) and of the sub-tile's columns cs .. into
+// a stage, as one cp.async group (rows past h and columns past the blocks zero).
+__device__ __forceinline__ void load_chunk(float* st, const FoldArgs& a, int64_t row0, int h, int64_t c0,
+                                           int nbk, int64_t cs, int wc, int m) {
+  float* Yc = st;
+  float* Xc = st + CR * LDS;
+  for (int q = threadIdx.x; q < CR * (NB / 4); q += PT) {
+    const int i = q >> 4, j4 = (q & 15) * 4, gi = m * CR + i;
+    const int vy = gi < h ? mx<int>(0, mn<int>(4, nbk - j4)) : 0;
+    const int vx = gi < h ? mx<int>(0, mn<int>(4, wc - j4)) : 0;
+    const float* rowp = a.X + (row0 + gi) * a.ldX;
+    cp16(Yc + i * LDS + j4, rowp + c0 + j4, vy, a.X);
+    cp16(Xc + i * LDWS + j4, rowp + cs + j4, vx, a.X);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // fp32 trailing update of one (sub-tile, panel, column block) per block:
 //   W = Y^T X_t[:, cols] + R[k rows, cols];  W2 = T^T W;  R[k rows, cols] -= W2;
 //   X_t[:, cols] -= Y W2.
-// The tiles come by cp.async in UCH row chunks, so the first GEMM starts while
-// the later chunks are in flight; all reads of shared memory are float4.
-__global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int wave) {
+// The sub-tile's rows stream through two stages of CR-row chunks by cp.async
+// (the next chunk's copy runs under the current chunk's products), once for the
+// first product and once for the last, so a block holds ~104 KB of shared memory
+// and two blocks share an SM.  All shared reads are float4.
+__global__ void __launch_bounds__(PT, 2) fold_update_simt_kernel(FoldBatch fb, int wave) {
   const FoldArgs& a = fb.f[blockIdx.z];
   const int t = blockIdx.x;
   const int k = wave - t;
@@ -152,10 +173,10 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
   if (cs < c0 + NB || cs >= a.n) return;
 
   extern __shared__ __align__(16) float sm[];
-  float* Y = sm;                 // SUB x LDS: the panel's Y
-  float* Xb = Y + SUB * LDS;     // SUB x LDWS: the sub-tile's columns cs ..
-  float* W = Xb + SUB * LDWS;    // NB x LDWS
-  float* Ts = W + NB * LDWS;     // NB x LDS: Ts[i][l] = T[l][i]
+  // chunk stages sm and sm + STAGE: a Y chunk (CR x LDS), then an X chunk (CR x LDWS)
+  auto stage = [&](int idx) { return idx ? sm + STAGE : sm; };
+  float* W = sm + 2 * STAGE;          // NB x LDWS
+  float* Ts = W + NB * LDWS;          // NB x LDS: Ts[i][l] = T[l][i]
 
   const int tid = threadIdx.x;
   const int64_t row0 = (int64_t)t * SUB;
@@ -163,50 +184,46 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
   const int nbk = (int)mn<int64_t>(NB, a.n - c0);
   const int wc = (int)mn<int64_t>(WC, a.n - cs);
   const float* Tb = a.Tb + (size_t)t * NB * NB;  // column-major: Tb[i*NB + l] = T[l][i]
+  const int nch = (h + CR - 1) / CR;              // chunks holding rows of the sub-tile
 
-  // copies: Ts with the first chunk, then SUB / UCH rows of Y and Xb per group
+  // T with chunk 0's group, chunk 1 in the other stage
   for (int q = tid; q < NB * NB / 4; q += PT) {
     const int i = q >> 4, l4 = (q & 15) * 4;
     cp16(Ts + i * LDS + l4, Tb + i * NB + l4, 4, Tb);
   }
-#pragma unroll
-  for (int ch = 0; ch < UCH; ++ch) {
-    for (int q = tid; q < (SUB / UCH) * (NB / 4); q += PT) {
-      const int i = ch * (SUB / UCH) + (q >> 4), j4 = (q & 15) * 4;
-      const int vy = i < h ? mx<int>(0, mn<int>(4, nbk - j4)) : 0;
-      const int vx = i < h ? mx<int>(0, mn<int>(4, wc - j4)) : 0;
-      const float* rowp = a.X + (row0 + i) * a.ldX;
-      cp16(Y + i * LDS + j4, rowp + c0 + j4, vy, a.X);
-      cp16(Xb + i * LDWS + j4, rowp + cs + j4, vx, a.X);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
+  load_chunk(stage(0), a, row0, h, c0, nbk, cs, wc, 0);
+  load_chunk(stage(1), a, row0, h, c0, nbk, cs, wc, 1);
 
   const int ty = tid >> 4, tx = tid & 15;
-  // ---- W = Y^T Xb (+ R rows): thread (ty, tx) owns W[ty*4 .. +3][tx*4 .. +3] ----
+  // ---- W = Y^T X (+ R rows): thread (ty, tx) owns W[ty*4 .. +3][tx*4 .. +3] ----
   float acc[4][4];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
-#pragma unroll
-  for (int ch = 0; ch < UCH; ++ch) {
-    if (ch == 0) asm volatile("cp.async.wait_group 3;" ::: "memory");
-    if (ch == 1) asm volatile("cp.async.wait_group 2;" ::: "memory");
-    if (ch == 2) asm volatile("cp.async.wait_group 1;" ::: "memory");
-    if (ch == 3) asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll 1
+  for (int m = 0; m < NCH; ++m) {
+    // groups in flight: chunks m and m + 1 (the last chunk: m only)
+    if (m + 1 < NCH) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    const int k0 = ch * (SUB / UCH), k1 = mn<int>(h, k0 + SUB / UCH);
+    const float* Yc = stage(m & 1);
+    const float* Xc = Yc + CR * LDS;
+    const int kend = mn<int>(CR, h - m * CR);
 #pragma unroll 4
-    for (int kk = k0; kk < k1; ++kk) {
-      const float4 av = *reinterpret_cast<const float4*>(Y + kk * LDS + ty * 4);
-      const float4 bv = *reinterpret_cast<const float4*>(Xb + kk * LDWS + tx * 4);
+    for (int kk = 0; kk < kend; ++kk) {
+      const float4 av = *reinterpret_cast<const float4*>(Yc + kk * LDS + ty * 4);
+      const float4 bv = *reinterpret_cast<const float4*>(Xc + kk * LDWS + tx * 4);
       const float ar[4] = {av.x, av.y, av.z, av.w}, bq[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[r][q] = fmaf(ar[r], bq[q], acc[r][q]);
     }
+    __syncthreads();  // every thread is done with this stage
+    // refill it: chunk m + 2 for this product; for the last product, the chunks
+    // not resident at its start (it takes the two resident ones first)
+    if (m + 2 < NCH) load_chunk(stage(m & 1), a, row0, h, c0, nbk, cs, wc, m + 2);
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -256,44 +273,66 @@ __global__ void __launch_bounds__(PT) fold_update_simt_kernel(FoldBatch fb, int 
     }
   }
   __syncthreads();
-  // ---- X_t[:, cols] -= Y W2; thread (ty, tx): rows ty*16 .. +15, columns tx*4 .. +3 ----
-  float acc2[16][4];
-#pragma unroll
-  for (int r = 0; r < 16; ++r)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) acc2[r][q] = 0.f;
+  // ---- X_t[:, cols] -= Y W2, chunk by chunk: the two resident chunks (NCH - 2,
+  // NCH - 1) first, the others copied in again behind them; thread (ty, tx): rows
+  // ty*4 .. +3 of a chunk, columns tx*4 .. +3 ----
+  const bool full = tx * 4 + 4 <= wc;
 #pragma unroll 1
-  for (int l = 0; l < NB; l += 4) {
-    float4 bw[4];
+  for (int step = 0; step < NCH; ++step) {
+    const int m = step < 2 ? NCH - 2 + step : step - 2;  // chunk of this step
+    const int sidx = m & 1;                               // its stage
+    if (step >= 2) {
+      // chunk m was copied in after step - 2 finished with its stage
+      if (step + 1 < NCH) asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+    }
+    if (m * CR < h) {
+      const float* Yc = stage(sidx);
+      const float* Xc = Yc + CR * LDS;
+      float a3[4][4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) bw[u] = *reinterpret_cast<const float4*>(W + (l + u) * LDWS + tx * 4);
+      for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float4 yv = *reinterpret_cast<const float4*>(Y + (ty * 16 + r) * LDS + l);
-      const float yl[4] = {yv.x, yv.y, yv.z, yv.w};
+        for (int q = 0; q < 4; ++q) a3[r][q] = 0.f;
+#pragma unroll 4
+      for (int l = 0; l < NB; l += 4) {
+        float4 bw[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        acc2[r][0] = fmaf(yl[u], bw[u].x, acc2[r][0]);
-        acc2[r][1] = fmaf(yl[u], bw[u].y, acc2[r][1]);
-        acc2[r][2] = fmaf(yl[u], bw[u].z, acc2[r][2]);
-        acc2[r][3] = fmaf(yl[u], bw[u].w, acc2[r][3]);
+        for (int u = 0; u < 4; ++u) bw[u] = *reinterpret_cast<const float4*>(W + (l + u) * LDWS + tx * 4);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float4 yv = *reinterpret_cast<const float4*>(Yc + (ty * 4 + r) * LDS + l);
+          const float yl[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            a3[r][0] = fmaf(yl[u], bw[u].x, a3[r][0]);
+            a3[r][1] = fmaf(yl[u], bw[u].y, a3[r][1]);
+            a3[r][2] = fmaf(yl[u], bw[u].z, a3[r][2]);
+            a3[r][3] = fmaf(yl[u], bw[u].w, a3[r][3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int i = m * CR + ty * 4 + r;
+        if (i >= h) continue;
+        const float4 xv = *reinterpret_cast<const float4*>(Xc + (ty * 4 + r) * LDWS + tx * 4);
+        const float o[4] = {xv.x - a3[r][0], xv.y - a3[r][1], xv.z - a3[r][2], xv.w - a3[r][3]};
+        float* dst = a.X + (row0 + i) * a.ldX + cs + tx * 4;
+        if (full) {
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (tx * 4 + q < wc) dst[q] = o[q];
+        }
       }
     }
-  }
-  const bool full = tx * 4 + 4 <= wc;
-#pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const int i = ty * 16 + r;
-    if (i >= h) continue;
-    const float4 xv = *reinterpret_cast<const float4*>(Xb + i * LDWS + tx * 4);
-    const float o[4] = {xv.x - acc2[r][0], xv.y - acc2[r][1], xv.z - acc2[r][2], xv.w - acc2[r][3]};
-    float* dst = a.X + (row0 + i) * a.ldX + cs + tx * 4;
-    if (full) {
-      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (tx * 4 + q < wc) dst[q] = o[q];
+    if (step < 2) {
+      // this stage is free once every thread is done: copy in chunk step again
+      __syncthreads();
+      load_chunk(stage(sidx), a, row0, h, c0, nbk, cs, wc, step);
     }
   }
 }
