@@ -226,14 +226,15 @@ def time_components(lc, per_tile, tiles, X, D, gW, W):
 
 def time_fp32_mode(dev, X, D, gW, W, tiles):
     """The same operator in the fp32 mode (IFK_PREC_FP32, the reference's
-    use_true_bf16=False path at its 1e-5 bound): fp32 rows, one fold launch per tile
-    (fp32 Householder panels, fp32 trailing updates on the CUDA cores), the damping
-    fold, fp32 factors, fp32 solves and the update.  Timed as a CUDA graph of the step
+    use_true_bf16=False path at its 1e-5 bound): fp32 rows, the one-launch schedule
+    like the headline (the 8 tiles of both factors through one wave schedule, then
+    the damping rows; fp32 Householder panels, fp32 trailing updates on the CUDA
+    cores), fp32 factors, fp32 solves and the update.  Timed as a CUDA graph of the step
     (CUDA events, one GPU); the component split is one eager step."""
     import torch
     from ifkfac_b200 import _lib
     from ifkfac_b200.engine import LayerCurvature
-    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_FP32, torch.float32, TILE, window=1)
+    lc = LayerCurvature(N_DIM, N_DIM, dev, _lib.PREC_FP32, torch.float32, TILE, window=len(tiles))
     Xf, Df, Wf = X.float(), D.float(), W.clone()
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
@@ -245,13 +246,14 @@ def time_fp32_mode(dev, X, D, gW, W, tiles):
         for lo, hi in tiles:
             lc.fold(Xf[lo:hi], Df[lo:hi])
         mark(1)
-        lc.refresh(DAMPING)
+        lc.refresh(DAMPING, consume=True)
         mark(2)
         lc.natgrad_update(gW, Wf, LR, MOM)
         mark(3)
         if comp is not None:
             marks[3].synchronize()
-            comp.update(tsqr_ms=marks[0].elapsed_time(marks[1]), fold_ms=marks[1].elapsed_time(marks[2]),
+            # the tiles are kept by fold() and folded with the damping rows by refresh()
+            comp.update(tsqr_fold_ms=marks[0].elapsed_time(marks[2]),
                         trsm_update_ms=marks[2].elapsed_time(marks[3]))
 
     step()

@@ -37,6 +37,7 @@ SIGNATURES = {
     "ifk_tsqr_fold_batched": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp,
                                      _vp, _sz, _vp]),
     "ifk_tsqr_fold_segments_workspace": (_sz, [_int, _vp, _vp, _vp, _vp]),
+    "ifk_tsqr_fold_segments_fp32_workspace": (_sz, [_int, _vp, _vp, _vp, _vp]),
     "ifk_tsqr_fold_segments": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _int, _vp, _vp, _sz, _vp]),
     "ifk_rtree_merge_workspace": (_sz, [_int, _i64]),
     "ifk_rtree_merge": (_int, [_int, _vp, _vp, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),

@@ -362,6 +362,39 @@ size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int*
   return b;
 }
 
+// Rows of fold f's segments in total, and whether they can share one fp32 wave
+// schedule with the sub-tile sequence of one fold per segment in turn: every
+// segment but the last with rows holds a multiple of SUB rows.
+static bool fp32_concat_rows(int f, const int* nseg, const ifk_segment* segs, int64_t* total) {
+  const int64_t base = seg_base(f, nseg);
+  int64_t t = 0;
+  int last = -1;
+  for (int g = 0; g < nseg[f]; ++g)
+    if (segs[base + g].rows > 0) last = g;
+  bool ok = true;
+  for (int g = 0; g < nseg[f]; ++g) {
+    const int64_t r = std::max<int64_t>(segs[base + g].rows, 0);
+    if (r > 0 && g != last && r % SUB != 0) ok = false;
+    t += r;
+  }
+  *total = t;
+  return ok;
+}
+
+size_t ifk_tsqr_fold_segments_fp32_workspace(int nfolds, const int64_t* n, const int* nseg,
+                                             const ifk_segment* segs, const double* ident_tail) {
+  const size_t base = ifk_tsqr_fold_segments_workspace(nfolds, n, nseg, segs, ident_tail);
+  if (base == 0) return 0;
+  size_t b = 0;
+  for (int f = 0; f < nfolds; ++f) {
+    int64_t total = 0;
+    fp32_concat_rows(f, nseg, segs, &total);
+    const int64_t rows = std::max<int64_t>(total, (ident_tail && ident_tail[f] > 0) ? n[f] : 0);
+    if (rows > 0) b += wave_ws(rows, n[f]);
+  }
+  return std::max(base, b);
+}
+
 int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, const int64_t* rows_R,
                            const int64_t* n, const int* nseg, const ifk_segment* segs, int chunk_dtype,
                            const double* ident_tail, int prec, int* d_status, void* workspace,
@@ -449,7 +482,77 @@ int ifk_tsqr_fold_segments(int nfolds, float* const* R, const int64_t* ldR, cons
     // folds without rows are dropped by the launcher
     return run_persistent(nfolds, d.data(), workspace, d_status, s, sp.data(), ns.data());
   }
-  // fp32 mode: the segments of each fold one after another through the wave schedule
+  // fp32 mode.  When every fold's segments can be concatenated (see
+  // fp32_concat_rows) and the workspace covers the concatenation, the segments of
+  // each fold are copied one after another into its part of the workspace and all
+  // folds run one wave schedule together: T + K - 1 waves instead of one schedule
+  // per segment, with the same sub-tile sequence; the identity tails follow as one
+  // more schedule of trapezoidal folds.
+  {
+    bool concat = nfolds <= MAX_FOLDS;
+    size_t need = 0;
+    std::vector<int64_t> tot((size_t)std::max(nfolds, 0));
+    for (int f = 0; f < nfolds && concat; ++f) {
+      concat = fp32_concat_rows(f, nseg, segs, &tot[(size_t)f]);
+      const int64_t rows = std::max<int64_t>(tot[(size_t)f], (ident_tail && ident_tail[f] > 0) ? n[f] : 0);
+      if (rows > 0) need += wave_ws(rows, n[f]);
+    }
+    if (concat && workspace_bytes >= need) {
+      std::vector<char*> wsf((size_t)nfolds);
+      char* w = (char*)workspace;
+      for (int f = 0; f < nfolds; ++f) {
+        wsf[(size_t)f] = w;
+        const int64_t rows = std::max<int64_t>(tot[(size_t)f], (ident_tail && ident_tail[f] > 0) ? n[f] : 0);
+        if (rows > 0) w += wave_ws(rows, n[f]);
+      }
+      auto args = [&](int f, int64_t rows, int64_t rr, int tri) {
+        FoldArgs a;
+        a.R = R[f];
+        a.ldR = ldR[f];
+        a.X = (float*)wsf[(size_t)f];
+        a.ldX = xw_ld(n[f]);
+        a.Tb = (float*)(wsf[(size_t)f] + align_up(xw_bytes(rows, n[f])));
+        a.n = n[f];
+        a.rows = rows;
+        a.rows_R = rr;
+        a.tiles = (int)cdiv(rows, SUB);
+        a.K = (int)cdiv(n[f], NB);
+        a.tri = tri;
+        a.err = d_status;
+        return a;
+      };
+      FoldBatch b;
+      b.nf = 0;
+      for (int f = 0; f < nfolds; ++f) {
+        if (tot[(size_t)f] == 0) continue;
+        FoldArgs a = args(f, tot[(size_t)f], rows_R[f], 0);
+        const int64_t base = seg_base(f, nseg);
+        int64_t off = 0;
+        for (int g = 0; g < nseg[f]; ++g) {
+          const ifk_segment& E = segs[base + g];
+          if (E.rows <= 0) continue;
+          const int rc = copy_chunk(a.X + off * a.ldX, a.ldX, E.chunk, E.ld, E.rows, n[f],
+                                    per_seg ? E.dtype : chunk_dtype, s, E.row_index, E.src_rows, E.cols, d_status,
+                                    E.conv ? &geo[(size_t)(base + g)] : nullptr);
+          if (rc != IFK_OK) return rc;
+          off += E.rows;
+        }
+        b.f[b.nf++] = a;
+      }
+      int rc = fold_run_batch(b, prec, s);
+      if (rc != IFK_OK) return rc;
+      b.nf = 0;
+      for (int f = 0; f < nfolds; ++f) {
+        if (!(ident_tail && ident_tail[f] > 0)) continue;
+        FoldArgs a = args(f, n[f], std::min<int64_t>(n[f], rows_R[f] + tot[(size_t)f]), 1);
+        rc = fill_scaled_identity(a.X, a.ldX, n[f], (float)ident_tail[f], s);
+        if (rc != IFK_OK) return rc;
+        b.f[b.nf++] = a;
+      }
+      return fold_run_batch(b, prec, s);
+    }
+  }
+  // otherwise the segments of each fold one after another through the wave schedule
   for (int f = 0; f < nfolds; ++f) {
     int64_t rr = rows_R[f];
     const int64_t base = seg_base(f, nseg);

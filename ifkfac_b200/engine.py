@@ -258,7 +258,10 @@ def fold_segments(factors: Sequence[Factor], segments: Sequence[Sequence], ws: t
     ns = _arr(ctypes.c_int64, [f.n for f in factors])
     nseg = _arr(ctypes.c_int, [len(cs) for cs in segs])
     tail = _arr(ctypes.c_double, [float(v) for v in ident_tail]) if ident_tail is not None else None
-    need = L.ifk_tsqr_fold_segments_workspace(nf, ns, nseg, arr, tail)
+    # fp32 mode: the workspace with which the segments share one wave schedule
+    wsfn = (L.ifk_tsqr_fold_segments_fp32_workspace if factors[0].prec == _lib.PREC_FP32
+            else L.ifk_tsqr_fold_segments_workspace)
+    need = wsfn(nf, ns, nseg, arr, tail)
     if need == 0 and (flat or ident_tail):
         raise ValueError("ifk_tsqr_fold_segments_workspace rejected the shapes")
     if ws is None or ws.numel() < need:
@@ -314,7 +317,9 @@ class LayerCurvature:
         segs = (_lib.Segment * (2 * self.window))()
         for i in range(2 * self.window):
             segs[i] = _lib.Segment(None, 0, max(chunk_rows, 1), None, 0, 0)
-        self.ws_pair = _ws(L.ifk_tsqr_fold_segments_workspace(
+        wsfn = (L.ifk_tsqr_fold_segments_fp32_workspace if self.fx.prec == _lib.PREC_FP32
+                else L.ifk_tsqr_fold_segments_workspace)
+        self.ws_pair = _ws(wsfn(
             2, _arr(ctypes.c_int64, [n_in, n_out]), _arr(ctypes.c_int, [self.window] * 2), segs,
             _arr(ctypes.c_double, [1.0, 1.0])), self.device)
 

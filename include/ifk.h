@@ -192,6 +192,20 @@ struct ifk_conv2d {
 IFK_API size_t ifk_tsqr_fold_segments_workspace(int nfolds, const int64_t* n, const int* nseg,
                                                 const ifk_segment* segs, const double* ident_tail);
 
+/* Workspace bytes with which ifk_tsqr_fold_segments in fp32 mode (IFK_PREC_FP32)
+ * folds every fold's segments through one wave schedule together (same
+ * arguments; at least ifk_tsqr_fold_segments_workspace).  The segments of a fold
+ * are copied one after another into the workspace, so the schedule has T + K - 1
+ * waves for the fold's T sub-tiles and K panels instead of one schedule per
+ * segment; the sub-tile sequence, and so the result, is that of one fold per
+ * segment in turn.  This applies when every segment of a fold but its last holds
+ * a multiple of 256 rows and at most 16 folds are given; otherwise, or with the
+ * smaller workspace, the segments are folded one after another.  The same
+ * operation as the reference's streaming update per chunk
+ * (ifkfac/triangular.py:246-307) followed by finalize_R (:386-421). */
+IFK_API size_t ifk_tsqr_fold_segments_fp32_workspace(int nfolds, const int64_t* n, const int* nseg,
+                                                     const ifk_segment* segs, const double* ident_tail);
+
 /*
  * Fold a sequence of segments of rows into each of nfolds factors, in order,
  * in one persistent launch where they fit (IFK_PREC_BF16): the result is that

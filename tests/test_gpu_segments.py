@@ -204,3 +204,25 @@ def test_mixed_dtype_segments_in_one_call(prec):
         assert torch.equal(f.R, alone.R)
     with pytest.raises(TypeError):
         fold_segments([Factor(96, "cuda")], [[mk(10, 96, torch.float32), mk(10, 96, torch.bfloat16)]], None)
+
+
+def test_fp32_segments_share_one_schedule_bitwise():
+    """fp32 mode, segments of whole sub-tiles (the last one ragged) with damping
+    rows: the segments of both folds run one wave schedule together, then the
+    identity tails; every factor bit for bit as one fold per tile and then the
+    damping rows as a trapezoidal chunk."""
+    n, tiles, tail = 384, [512, 256, 768, 300], 0.7
+    xs = [_inputs(r, n, 70 + i, torch.float32) for i, r in enumerate(tiles)]
+    ds = [_inputs(r, n, 90 + i, torch.float32) for i, r in enumerate(tiles)]
+    a = (Factor(n, "cuda", _lib.PREC_FP32), Factor(n, "cuda", _lib.PREC_FP32))
+    ws = None
+    for x, d in zip(xs, ds):
+        ws = fold_batched(a, (x, d), ws)
+    eye = torch.eye(n, device="cuda") * tail
+    fold_batched(a, (eye, eye), ws, trapezoidal=True)
+    b = (Factor(n, "cuda", _lib.PREC_FP32), Factor(n, "cuda", _lib.PREC_FP32))
+    fold_segments(b, (xs, ds), None, ident_tail=[tail, tail])
+    torch.cuda.synchronize()
+    for fa, fb in zip(a, b):
+        assert int(fb.status.item()) == 0
+        assert torch.equal(fa.R, fb.R), float((fa.R - fb.R).abs().max())
