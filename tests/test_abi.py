@@ -129,3 +129,28 @@ def test_fold_workspace_stops_at_one_launch_piece():
     piece = 322 // 8  # whole chunks of 8 sub-tiles below the piece size
     assert ws(piece) < ws(piece + 1) == ws(piece + 2) == ws(200)
     assert ws(1) < ws(2) < ws(piece)
+
+
+def test_fp32_segments_workspace_covers_the_concatenation():
+    """ifk_tsqr_fold_segments_fp32_workspace: at least the segments workspace, and
+    an fp32 copy of all of a fold's rows (so it grows with the number of chunks,
+    where the segments workspace stops at one launch piece); the damping rows need
+    n rows of it."""
+    L = _lib.lib()
+    n = 1024
+    a64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
+
+    def both(nchunks, rows=512, tail=None):
+        segs = (_lib.Segment * nchunks)(*[_lib.Segment(0x1000, n, rows, None, 0, n, 0, 0)
+                                          for _ in range(nchunks)])
+        t = (ctypes.c_double * 1)(tail) if tail else None
+        args = (1, a64(n), (ctypes.c_int * 1)(nchunks), segs, t)
+        return L.ifk_tsqr_fold_segments_workspace(*args), L.ifk_tsqr_fold_segments_fp32_workspace(*args)
+
+    for k in (1, 4, 40, 400):
+        base, cat = both(k)
+        assert cat >= base > 0
+        assert cat >= k * 512 * n * 4  # every row of the fold, fp32
+    assert both(400)[1] > both(40)[1] > both(4)[1]
+    assert both(1, rows=64, tail=1.0)[1] >= n * n * 4  # the identity tail takes n rows
+    assert L.ifk_tsqr_fold_segments_fp32_workspace(0, None, None, None, None) == 0
