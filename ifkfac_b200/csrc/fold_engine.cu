@@ -107,8 +107,8 @@ constexpr uint32_t TM_D1 = 0, TM_D2 = 64, TM_D3 = 128, TM_COLS = 512;
 enum { XK_F32 = 0, XK_BF16 = 1, XK_IDENT = 2, XK_CONV = 8 };
 
 #ifdef IFK_TRACE
-// Diagnostic build only: per-task timestamps (globaltimer, ns), 26 int64 per task.
-constexpr int TRN = 26;
+// Diagnostic build only: per-task timestamps (globaltimer, ns), 28 int64 per task.
+constexpr int TRN = 28;
 __device__ long long g_trace[(1 << 14) * TRN];
 __device__ int g_trace_n;
 __device__ __forceinline__ long long gtime() {
@@ -875,6 +875,7 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
 #ifdef IFK_TRACE
     const long long p1 = TR_NOW();
     TR_ADD(11, p1 - p0);
+    TR_ADD(26 + q, p1 - p0);
     TR_ADD(15, clock64() - k0);
 #endif
     TR_ADD(12, 1);
