@@ -26,27 +26,44 @@ __device__ __forceinline__ float opA(const TA* A, int64_t ldA, int trans, int64_
   return trans ? ld_elem(A, j * ldA + i) : ld_elem(A, i * ldA + j);
 }
 
+// DIAG_TPB threads load the tiles (DIAG_LD loads in flight per thread); the
+// first NRHS of them then solve one column each.
+constexpr int DIAG_TPB = 256;
+constexpr int DIAG_LD = NS * NS / DIAG_TPB;  // 16
+static_assert(NS * NRHS == NS * NS, "square tiles");
+
 template <typename TA>
-__global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ldA, int trans,
-                                                         float* B, int64_t rs, int64_t cs,
-                                                         int64_t n, int64_t N, int64_t b0) {
+__global__ void __launch_bounds__(DIAG_TPB) trsm_diag_kernel(const TA* A, int64_t ldA, int trans,
+                                                             float* B, int64_t rs, int64_t cs,
+                                                             int64_t n, int64_t N, int64_t b0) {
   __shared__ float Ad[NS][NS + 1];
   __shared__ float Bs[NS][LDS_];
   const int tid = threadIdx.x;
   const int64_t c0 = (int64_t)blockIdx.x * NRHS;
   const int nb = (int)mn<int64_t>(NS, n - b0);
   const int nc = (int)mn<int64_t>(NRHS, N - c0);
-  for (int idx = tid; idx < NS * NS; idx += NRHS) {
-    // A's contiguous index fastest across threads: j for op = A, i for op = A^T
-    const int i = trans ? idx % NS : idx / NS, j = trans ? idx / NS : idx % NS;
-    Ad[i][j] = (i < nb && j < nb) ? opA(A, ldA, trans, b0 + i, b0 + j) : (i == j ? 1.f : 0.f);
-  }
-  // B's contiguous index varies fastest across threads: the columns of a row-major
-  // view, the rows of a transposed one (rs == 1), so the tile loads coalesce
+  // A's contiguous index fastest across threads: j for op = A, i for op = A^T.
+  // B's contiguous index too: the columns of a row-major view, the rows of a
+  // transposed one (rs == 1).  All loads of a thread are issued before its stores.
   const bool tv = rs == 1 && cs != 1;
-  for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
-    const int i = tv ? idx % NS : idx / NRHS, j = tv ? idx / NS : idx % NRHS;
-    Bs[i][j] = (i < nb && j < nc) ? B[(b0 + i) * rs + (c0 + j) * cs] : 0.f;
+  {
+    float va[DIAG_LD], vb[DIAG_LD];
+#pragma unroll
+    for (int u = 0; u < DIAG_LD; ++u) {
+      const int idx = tid + u * DIAG_TPB;
+      const int i = trans ? idx % NS : idx / NS, j = trans ? idx / NS : idx % NS;
+      va[u] = (i < nb && j < nb) ? opA(A, ldA, trans, b0 + i, b0 + j) : (i == j ? 1.f : 0.f);
+      const int bi = tv ? idx % NS : idx / NRHS, bj = tv ? idx / NS : idx % NRHS;
+      vb[u] = (bi < nb && bj < nc) ? B[(b0 + bi) * rs + (c0 + bj) * cs] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < DIAG_LD; ++u) {
+      const int idx = tid + u * DIAG_TPB;
+      const int i = trans ? idx % NS : idx / NS, j = trans ? idx / NS : idx % NS;
+      Ad[i][j] = va[u];
+      const int bi = tv ? idx % NS : idx / NRHS, bj = tv ? idx / NS : idx % NRHS;
+      Bs[bi][bj] = vb[u];
+    }
   }
   __syncthreads();
   // Column c by column-oriented substitution: its residues stay in registers; once
@@ -54,30 +71,32 @@ __global__ void __launch_bounds__(NRHS) trsm_diag_kernel(const TA* A, int64_t ld
   // with independent FMAs (op(A)[l][r] is the same for every column: a broadcast).
   // Rows past nb are the identity pad and come out zero.
   const int c = tid;
-  float res[NS];
+  if (c < NRHS) {
+    float res[NS];
 #pragma unroll
-  for (int i = 0; i < NS; ++i) res[i] = Bs[i][c];
-  if (trans) {  // lower: forward
+    for (int i = 0; i < NS; ++i) res[i] = Bs[i][c];
+    if (trans) {  // lower: forward
 #pragma unroll
-    for (int r = 0; r < NS; ++r) {
-      const float x = res[r] / Ad[r][r];
-      res[r] = x;
+      for (int r = 0; r < NS; ++r) {
+        const float x = res[r] / Ad[r][r];
+        res[r] = x;
 #pragma unroll
-      for (int l = r + 1; l < NS; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
+        for (int l = r + 1; l < NS; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
+      }
+    } else {  // upper: backward
+#pragma unroll
+      for (int r = NS - 1; r >= 0; --r) {
+        const float x = res[r] / Ad[r][r];
+        res[r] = x;
+#pragma unroll
+        for (int l = 0; l < r; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
+      }
     }
-  } else {  // upper: backward
 #pragma unroll
-    for (int r = NS - 1; r >= 0; --r) {
-      const float x = res[r] / Ad[r][r];
-      res[r] = x;
-#pragma unroll
-      for (int l = 0; l < r; ++l) res[l] = fmaf(-Ad[l][r], x, res[l]);
-    }
+    for (int i = 0; i < NS; ++i) Bs[i][c] = res[i];
   }
-#pragma unroll
-  for (int i = 0; i < NS; ++i) Bs[i][c] = res[i];
   __syncthreads();
-  for (int idx = tid; idx < NS * NRHS; idx += NRHS) {
+  for (int idx = tid; idx < NS * NRHS; idx += DIAG_TPB) {
     const int i = tv ? idx % NS : idx / NRHS, j = tv ? idx / NS : idx % NRHS;
     if (i < nb && j < nc) B[(b0 + i) * rs + (c0 + j) * cs] = Bs[i][j];
   }
@@ -101,17 +120,29 @@ __global__ void __launch_bounds__(256) trsm_update_kernel(const TA* A, int64_t l
   const int nj = (int)mn<int64_t>(NS, n - j0);
   const int ns = (int)mn<int64_t>(NS, n - s0);
   const int nc = (int)mn<int64_t>(NRHS, N - c0);
-  for (int idx = tid; idx < NS * NS; idx += 256) {
-    // A's contiguous index fastest across threads: l for op = A, i for op = A^T
-    const int i = trans ? idx % NS : idx / NS, l = trans ? idx / NS : idx % NS;
-    AsT[l][i] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
-  }
-  // B's contiguous index varies fastest across threads (see trsm_diag_kernel):
-  // the tile loads and the read-modify-writes of the result coalesce
+  // A's contiguous index fastest across threads (l for op = A, i for op = A^T), and
+  // B's (see trsm_diag_kernel): the tile loads and the read-modify-writes of the
+  // result coalesce.  All loads of a thread are issued before its stores.
   const bool tv = rs == 1 && cs != 1;
-  for (int idx = tid; idx < NS * NRHS; idx += 256) {
-    const int l = tv ? idx % NS : idx / NRHS, c = tv ? idx / NS : idx % NRHS;
-    Xs[l][c] = (l < ns && c < nc) ? B[(s0 + l) * rs + (c0 + c) * cs] : 0.f;
+  {
+    constexpr int LD = NS * NS / 256;
+    float va[LD], vx[LD];
+#pragma unroll
+    for (int u = 0; u < LD; ++u) {
+      const int idx = tid + u * 256;
+      const int i = trans ? idx % NS : idx / NS, l = trans ? idx / NS : idx % NS;
+      va[u] = (i < nj && l < ns) ? opA(A, ldA, trans, j0 + i, s0 + l) : 0.f;
+      const int xl = tv ? idx % NS : idx / NRHS, xc = tv ? idx / NS : idx % NRHS;
+      vx[u] = (xl < ns && xc < nc) ? B[(s0 + xl) * rs + (c0 + xc) * cs] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < LD; ++u) {
+      const int idx = tid + u * 256;
+      const int i = trans ? idx % NS : idx / NS, l = trans ? idx / NS : idx % NS;
+      AsT[l][i] = va[u];
+      const int xl = tv ? idx % NS : idx / NRHS, xc = tv ? idx / NS : idx % NRHS;
+      Xs[xl][xc] = vx[u];
+    }
   }
   __syncthreads();
   // thread tile: rows ri .. ri + 3, columns ci .. ci + 3 of the result, the
@@ -169,7 +200,7 @@ int trsm_simt(const TA* A, int64_t ldA, int trans, float* B, int64_t rs, int64_t
   for (int64_t step = 0; step < nblk; ++step) {
     const int64_t sb = trans ? step : (nblk - 1 - step);
     const int64_t s0 = sb * NS;
-    trsm_diag_kernel<TA><<<ctiles, NRHS, 0, s>>>(A, ldA, trans, B, rs, cs, n, N, s0);
+    trsm_diag_kernel<TA><<<ctiles, DIAG_TPB, 0, s>>>(A, ldA, trans, B, rs, cs, n, N, s0);
     const int64_t rem = trans ? (nblk - 1 - sb) : sb;
     if (rem > 0) {
       trsm_update_kernel<TA><<<dim3((unsigned)rem, ctiles), 256, 0, s>>>(A, ldA, trans, B, rs, cs,
