@@ -295,7 +295,11 @@ __host__ __device__ constexpr int stage_done(int K) { return K + 9; }
 // Leaf hooks of the fold's own panels: leaf s of sub-tile t starts once
 // sub-tile t - 1 has published the R diagonal block rows of its leaf s (those
 // rows are then final for t - 1), so consecutive sub-tiles factor the same
-// panel one leaf apart; the rows go back to R when the leaf ends.
+// panel one leaf apart; the rows go back to R when the leaf ends.  When a leaf
+// ends and sub-tile t - 1 has already published the next leaf's rows, they are
+// copied in at once (cp.async, zero-filled like the plain load), so the next
+// leaf finds them without a wait or a load round trip.  Only leaf s touches
+// rows 16s .. 16s + 15 of the block, so the early copy overwrites nothing in use.
 struct FoldLeafHook {
   float* R;
   int64_t ldR, c0;
@@ -304,9 +308,30 @@ struct FoldLeafHook {
   int* prog;
   const PFBatch* b;
   int* s_ok;
+  int* s_pre;  // shared flag: the rows of the next leaf were copied in early
+  template <class SM>
+  __device__ __forceinline__ void copy_rows(SM& S, int s) {
+    const int L0 = s * panel::LEAF;
+    for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
+      const int i = L0 + idx / NB, j = idx % NB;
+      const bool v = i < nbk && j < nbk && j >= i;
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&S.Rk[i * LDP + j]);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst),
+                   "l"(v ? R + (c0 + i) * ldR + c0 + j : R), "r"(v ? 4 : 0)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   template <class SM>
   __device__ __forceinline__ bool before_leaf(SM& S, int s) {
     HK_BEGIN
+    if (s > 0 && *(volatile int*)s_pre) {
+      // copied in when leaf s - 1 ended, after sub-tile t - 1 had published them
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      HK_END
+      return true;
+    }
     if (prev_prog && !cta_wait_ge(prev_prog, stage0 + s, *b, s_ok)) return false;
     const int L0 = s * panel::LEAF;
     for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
@@ -325,7 +350,13 @@ struct FoldLeafHook {
       const int i = L0 + idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) R[(c0 + i) * ldR + c0 + j] = S.Rk[i * LDP + j];
     }
+    // is the next leaf's input already published?  (thread 0's acquire, passed on
+    // to the other threads by the barrier of the publication below)
+    const int s1 = s + 1;
+    if (threadIdx.x == 0)
+      *s_pre = (s1 * panel::LEAF < nbk && (!prev_prog || ld_acquire(prev_prog) >= stage0 + s1)) ? 1 : 0;
     cta_publish_value(prog, stage0 + s);
+    if (*(volatile int*)s_pre) copy_rows(S, s1);
     HK_END
   }
 };
@@ -870,7 +901,8 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
     TR_ADD(8, p0 - l0);
 #endif
     // the R diagonal block is read and written leaf by leaf (FoldLeafHook)
-    FoldLeafHook hook{F.R, F.ldR, c0, nbk, stage_leaf(F.K, q, 0), t > 0 ? prev_prog : nullptr, prog, &b, s_ok};
+    FoldLeafHook hook{F.R, F.ldR, c0, nbk, stage_leaf(F.K, q, 0), t > 0 ? prev_prog : nullptr, prog, &b, s_ok,
+                      c.s_ready};
     if (!panel::panel_factor<SUB>(S, nbk, nact, hook)) return;
 #ifdef IFK_TRACE
     const long long p1 = TR_NOW();
