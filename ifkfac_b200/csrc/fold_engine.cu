@@ -309,6 +309,7 @@ struct FoldLeafHook {
   const PFBatch* b;
   int* s_ok;
   int* s_pre;  // shared flag: the rows of the next leaf were copied in early
+  bool published = false;  // this leaf's rows were stored and published by rows_final
   template <class SM>
   __device__ __forceinline__ void copy_rows(SM& S, int s) {
     const int L0 = s * panel::LEAF;
@@ -343,19 +344,38 @@ struct FoldLeafHook {
     return true;
   }
   template <class SM>
-  __device__ __forceinline__ void after_leaf(SM& S, int s) {
-    HK_BEGIN
+  __device__ __forceinline__ void store_rows(SM& S, int s) {
     const int L0 = s * panel::LEAF;
     for (int idx = threadIdx.x; idx < panel::LEAF * NB; idx += TPB) {
       const int i = L0 + idx / NB, j = idx % NB;
       if (i < nbk && j < nbk && j >= i) R[(c0 + i) * ldR + c0 + j] = S.Rk[i * LDP + j];
     }
+  }
+  // The leaf's rows are final before the update of the panel's trailing columns:
+  // they are published then, so sub-tile t + 1 can start the same leaf meanwhile.
+  template <class SM>
+  __device__ __forceinline__ void rows_final(SM& S, int s) {
+    HK_BEGIN
+    store_rows(S, s);
+    cta_publish_value(prog, stage0 + s);
+    published = true;
+    HK_END
+  }
+  template <class SM>
+  __device__ __forceinline__ void after_leaf(SM& S, int s) {
+    HK_BEGIN
+    if (!published) store_rows(S, s);
     // is the next leaf's input already published?  (thread 0's acquire, passed on
-    // to the other threads by the barrier of the publication below)
+    // to the other threads by the barrier below)
     const int s1 = s + 1;
     if (threadIdx.x == 0)
       *s_pre = (s1 * panel::LEAF < nbk && (!prev_prog || ld_acquire(prev_prog) >= stage0 + s1)) ? 1 : 0;
-    cta_publish_value(prog, stage0 + s);
+    if (published) {
+      __syncthreads();
+    } else {
+      cta_publish_value(prog, stage0 + s);
+    }
+    published = false;
     if (*(volatile int*)s_pre) copy_rows(S, s1);
     HK_END
   }

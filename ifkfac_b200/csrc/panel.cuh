@@ -294,12 +294,16 @@ __device__ __forceinline__ void gram_steps(PanelSmemT<ROWS>& S, int L0, int jl, 
 // Leaf hooks of panel_factor.  Rows L0 .. L0 + 15 of the R diagonal block are
 // read and written by leaf L0 / 16 only, so a caller may load them just before
 // that leaf (before_leaf, which ends with a barrier of the panel's threads and
-// returns false to abandon the panel) and store them as soon as it ends
-// (after_leaf, called after the leaf's last barrier).  NoLeafHook: the caller
-// loads and stores the whole block around the call.
+// returns false to abandon the panel) and store them as soon as they are final:
+// rows_final, called after the barrier that follows the leaf's W (only the update
+// of the panel's trailing columns comes after it; not called for a leaf without
+// reflectors or trailing columns), else after_leaf, called after the leaf's last
+// barrier.  NoLeafHook: the caller loads and stores the whole block around the call.
 struct NoLeafHook {
   template <class SM>
   __device__ __forceinline__ bool before_leaf(SM&, int) { return true; }
+  template <class SM>
+  __device__ __forceinline__ void rows_final(SM&, int) {}
   template <class SM>
   __device__ __forceinline__ void after_leaf(SM&, int) {}
 };
@@ -450,6 +454,8 @@ static __device__ __noinline__ bool panel_factor(PanelSmemT<ROWS>& S, const int 
     }
     psync<ROWS>();
     PH_MARK(5);
+    // the leaf's R rows are final here (the trailing update below touches P only)
+    hook.rows_final(S, s);
     // P[:, C] -= Y_leaf W; this thread's Y_leaf row is still in a[]
     const int nq = (wcI + 3) / 4;
 #pragma unroll 1
