@@ -824,11 +824,12 @@ __device__ void run_task(Ctx& c, const PFBatch& b, int f, int t, int cb, int* s_
       tc::fence_before();
       __syncthreads();
       tc::fence_after();
+      // Panel k - 1 is applied to the block's R rows (written before the
+      // barrier above): thread 0's release store publishes them before the
+      // refresh, so sub-tile t + 1 can take them meanwhile.
+      if (tid == 0) st_release(prog, k);
       refresh_a1(c);
       a1_valid = true;
-      // Panel k - 1 is applied to the block's R rows (written before the
-      // barrier above): thread 0's release store publishes them.
-      if (tid == 0) st_release(prog, k);
     }
     AP_MARK(6);
     // skipped when the previous apply's lookahead saw panel k published and its R rows final
